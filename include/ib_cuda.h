@@ -1,0 +1,166 @@
+/*
+ * ib_cuda.h -- C ABI of the B200 (sm_100a) backend for inference.cpp's
+ * quantized-weight path.
+ *
+ * This library replaces the reference's CUDA backend loader
+ * (src/ops/cuda_backend.cpp: dlopen of libcuda.so.1, cuModuleLoadData of
+ * clang-built sm_75 PTX, cuLaunchKernel by name) with kernels compiled for
+ * sm_100a and called through plain C functions.  Every function returns an int
+ * status (IB_OK on success); on failure ib_last_error() gives a message in the
+ * reference's style ("CUDA: <what> failed: <reason>").  All pointers named
+ * `dev`/device below are device pointers; `host` pointers are host memory.
+ * `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream,
+ * which is what the reference launches on, cuda_backend.cpp:180-181).
+ *
+ * Tensor layout matches the reference after its dimension reversal
+ * (src/models/transformer.cpp:160-161,200): a weight is row-major [rows, cols]
+ * with rows = output features; a GGUF block-quantised weight is the file's
+ * bytes unchanged, i.e. rows * (cols / block_elems) consecutive blocks.
+ */
+#ifndef IB_CUDA_H
+#define IB_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define IB_OK 0
+#define IB_ERR_INVALID 1     /* bad argument (null pointer, size, type) */
+#define IB_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define IB_ERR_UNSUPPORTED 3 /* type/shape not supported by this path */
+#define IB_ERR_OOM 4         /* device memory exhausted */
+#define IB_ERR_TIMEOUT 5     /* a bounded wait expired */
+#define IB_ERR_COMM 6        /* collective / communicator failure */
+
+/* ---- GGUF tensor types (reference include/core/tensor.hpp:16-37) ------------ */
+#define IB_TYPE_F32 0
+#define IB_TYPE_F16 1
+#define IB_TYPE_Q4_0 2
+#define IB_TYPE_Q5_0 6
+#define IB_TYPE_Q5_1 7
+#define IB_TYPE_Q8_0 8
+#define IB_TYPE_Q4_K 12
+#define IB_TYPE_Q6_K 14
+#define IB_TYPE_I16 17
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ib_last_error(void);
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int ib_version(void);
+
+/* Elements and bytes per block of a type (reference type_nbytes_per_block /
+ * block_size, include/core/tensor.hpp:204-262). */
+int ib_type_info(int type, int64_t* block_elems, int64_t* block_bytes);
+
+/* ---- lifecycle (replaces inference::cuda::available, device_name, total_memory,
+ *      free_memory, sync, shutdown: include/ops/cuda_backend.hpp:17-22) ------- */
+int ib_init(int device);                        /* select device; idempotent */
+int ib_available(void);                         /* 1 if a usable sm_100 device exists, else 0 */
+int ib_device_name(char* buf, size_t len);
+int ib_memory_info(size_t* free_bytes, size_t* total_bytes);
+int ib_sync(void);                              /* device-wide synchronise */
+int ib_shutdown(void);                          /* no-op: buffers stay valid to exit */
+
+/* ---- memory (replaces alloc, release, upload, download:
+ *      include/ops/cuda_backend.hpp:25-28; the reference copies synchronously) -- */
+int ib_alloc(void** dev, size_t bytes);
+int ib_free(void* dev);
+int ib_upload(void* dev, const void* host, size_t bytes, void* stream);
+int ib_download(void* host, const void* dev, size_t bytes, void* stream);
+int ib_memset(void* dev, int value, size_t bytes, void* stream);
+
+/* ---- block-quantised weights (the hot path) -------------------------------- */
+
+/* Dequantise a packed [rows, cols] tensor to FP32, bit-exact with the reference
+ * dequantize() (src/gguf/quantization.cpp:250-267; Q4_0 :33, Q8_0 :59, Q5_0 :83,
+ * Q5_1 :112, Q4_K :161, Q6_K :211).  F16 and F32 inputs are converted/copied as
+ * load_tensor does (src/models/transformer.cpp:176-199). */
+int ib_dequant_f32(int type, const void* dev_blocks, float* dev_out, int64_t rows,
+                   int64_t cols, void* stream);
+
+/* Dequantise and requantise each row to symmetric INT16 with one FP32 scale per
+ * row, bit-exact with make_weight (src/models/transformer.cpp:208-251) and
+ * quantize_i16 (src/models/model_cuda.cpp:62-99). */
+int ib_dequant_i16(int type, const void* dev_blocks, int16_t* dev_q, float* dev_row_scale,
+                   int64_t rows, int64_t cols, void* stream);
+
+/* Fused dequant + GEMV on packed blocks: y[r] = sum_c W[r, c] * x[c], FP32
+ * activations and accumulation.  Replaces gemv / gemv_i16
+ * (include/ops/cuda_backend.hpp:31-34; kernels src/ops/cuda_kernels.cu:62-95) for
+ * weights kept in GGUF form.  W is never expanded in memory. */
+int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float* dev_y, int64_t rows,
+              int64_t cols, void* stream);
+
+/* Batched product on packed blocks: Y[T, rows] = X[T, cols] @ W^T.  Replaces
+ * gemm / gemm_i16 (include/ops/cuda_backend.hpp:35-38; kernels
+ * src/ops/cuda_kernels.cu:279-346). */
+int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float* dev_Y, int64_t T,
+              int64_t rows, int64_t cols, void* stream);
+
+/* Embedding gather with dequantisation: out[t, :] = dequant(table[ids[t], :]).
+ * Replaces embedding / embedding_batch (include/ops/cuda_backend.hpp:44-50) for a
+ * packed table; ids outside [0, vocab) read row 0 as Model::forward does
+ * (src/models/model.cpp:259). */
+int ib_embedding_q(int type, const void* dev_table, const int32_t* dev_ids, float* dev_out,
+                   int T, int64_t vocab, int64_t dim, void* stream);
+
+/* ---- FP32 / INT16 operators with the reference's argument meaning
+ *      (include/ops/cuda_backend.hpp:31-64; all tensors FP32 row-major) ------- */
+int ib_gemv(const float* W, const float* x, float* y, int M, int N, void* stream);
+int ib_gemv_i16(const int16_t* W, const float* row_scale, const float* x, float* y, int M,
+                int N, void* stream);
+int ib_gemm(const float* W, const float* X, float* Y, int T, int M, int K, void* stream);
+int ib_gemm_i16(const int16_t* W, const float* row_scale, const float* X, float* Y, int T,
+                int M, int K, void* stream);
+int ib_rmsnorm(const float* x, const float* w, float* out, int rows, int dim, float eps,
+               void* stream);
+int ib_silu(float* x, int n, void* stream);
+int ib_mul(float* a, const float* b, int n, void* stream);
+int ib_add(float* a, const float* b, int n, void* stream);
+int ib_embedding(const float* table, int id, float* out, int dim, void* stream);
+int ib_embedding_i16(const int16_t* table, const float* row_scale, int id, float* out,
+                     int dim, void* stream);
+int ib_embedding_batch(const float* table, const int32_t* ids, float* out, int T, int dim,
+                       void* stream);
+int ib_embedding_batch_i16(const int16_t* table, const float* row_scale, const int32_t* ids,
+                           float* out, int T, int dim, void* stream);
+int ib_kv_write(float* kc, float* vc, const float* k, const float* v, int n_heads,
+                int head_dim, int max_seq, int pos, void* stream);
+int ib_kv_write_batch(float* kc, float* vc, const float* k, const float* v, int n_heads,
+                      int head_dim, int max_seq, int start, int T, void* stream);
+int ib_rope(float* q, float* k, const float* table, int n_heads, int n_kv_heads,
+            int head_dim, int pos, void* stream);
+int ib_rope_batch(float* q, float* k, const float* table, int n_heads, int n_kv_heads,
+                  int head_dim, int start, int T, void* stream);
+int ib_attention(const float* q, const float* kc, const float* vc, float* out, int n_heads,
+                 int n_kv_heads, int head_dim, int max_seq, int pos, float scale,
+                 void* stream);
+int ib_attention_batch(const float* q, const float* kc, const float* vc, float* out,
+                       int n_heads, int n_kv_heads, int head_dim, int max_seq, int start,
+                       int T, float scale, void* stream);
+
+/* Index of the first maximum of x[0..n) (reference sample_argmax,
+ * src/ops/ops.cpp:424-438), written to *dev_out. */
+int ib_argmax(const float* x, int n, int32_t* dev_out, void* stream);
+
+/* ---- seeded synthetic weights (test and benchmark data, not a timed path) ---
+ * Fills a [rows, cols] tensor of `type` with blocks encoding N(0, std) values
+ * drawn from a counter-based stream keyed by `seed`.  The host and device
+ * versions produce identical bytes. */
+int ib_synth_host(int type, int64_t rows, int64_t cols, uint64_t seed, float stdv,
+                  void* host_out, int n_threads);
+int ib_synth_device(int type, int64_t rows, int64_t cols, uint64_t seed, float stdv,
+                    void* dev_out, void* stream);
+/* The FP32 values behind ib_synth_* (before quantisation). */
+int ib_synth_values_host(int64_t n, uint64_t seed, float stdv, float* host_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IB_CUDA_H */
