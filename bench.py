@@ -1,0 +1,363 @@
+"""Benchmark: batch-1 greedy decode of the Llama-3-8B-shaped Q4_K/Q6_K model on
+the native B200 path, with the fused dequant-GEMV's HBM roofline beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama-3-8b|llama-3-70b|tinyllama-1.1b|stories15M]
+
+One step = one decode token (all layers + output head + device argmax) at
+positions prompt_len, prompt_len+1, ...; the KV cache first holds the seeded
+prompt (batched prefill, timed separately).  Weights are synthetic: every linear
+layer and embedding N(0, 0.02) quantised to its GGUF type on the GPU by the
+package's seeded generator; 4.9 GB of weights per token exceed the 126 MB L2, so
+no flush is needed between steps.
+
+value:  decode tok/s timed with CUDA events around K device-side steps
+        (ib_model_decode_loop: inputs resident, argmax fed back on the device).
+e2e:    the same K steps through the public per-token call ib_model_decode with
+        host buffers (token + position in, next id out every step), wall clock.
+roofline: the dominant kernel, the Q4_K fused dequant-GEMV of ffn_gate/ffn_up
+        (14336 x 4096), timed alone with CUDA events over all layers' weights.
+cpu_baseline / --impl reference: the reference's own CPU matvec (oracle/_ref, or
+        the C restatement where it was not built) on a bounded sample: one layer's
+        seven projections plus 1/16 of the output head, extrapolated per token.
+With torchrun (N > 1) every rank decodes its own replica (no collective on the
+data path yet); value is the sum over ranks, timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode tok/s at Llama-3-8B-shape Q4_K; fused dequant-GEMV GB/s vs HBM peak"
+
+
+def load_pkg():
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as ge
+    return ge.package()
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def all_max(world, v):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201):
+    import torch
+    from inference_cpp_b200 import gguf_writer as gw
+    max_seq = prompt_len + warmup + 2 * steps + 16
+    m = ib.Model.create(cfg, precision=ib.NATIVE, device=device, max_seq=max_seq)
+    for name, t, rows, cols in cfg.tensor_specs():
+        if name.endswith("norm.weight"):
+            data = torch.ones(cols, dtype=torch.float32, device="cuda")
+        else:
+            data = ib.synth_device(t, rows, cols, gw.tensor_seed(seed, name), 0.02)
+        m.set_tensor(name, t, rows, cols, data)
+        del data
+    m.finalize()
+    torch.cuda.synchronize()
+    return m
+
+
+def time_gemv(ib, cfg, seed=20261201):
+    """Q4_K GEMV ffn_gate shape over n_layers distinct weight matrices (no L2 reuse)."""
+    import torch
+    from inference_cpp_b200 import gguf_writer as gw
+    rows, cols = cfg.ffn, cfg.dim
+    n = min(cfg.n_layers, 32)
+    Ws = [ib.synth_device(ib.Q4_K, rows, cols, gw.tensor_seed(seed + 1, f"w{i}"), 0.02) for i in range(n)]
+    x = torch.randn(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    st = torch.cuda.current_stream()
+    for i in range(3 * n):
+        ib.gemv_q(ib.Q4_K, Ws[i % n], x, rows, cols, y=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 4 * n
+    e0.record(st)
+    for i in range(reps):
+        ib.gemv_q(ib.Q4_K, Ws[i % n], x, rows, cols, y=y)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    nbytes = ib.packed_nbytes(ib.Q4_K, rows, cols) + 4 * cols + 4 * rows
+    del Ws
+    torch.cuda.empty_cache()
+    return nbytes, ms, reps
+
+
+def traffic_from_profile():
+    p = os.path.join(ROOT, "profiles", "gemv_q4k_14336x4096_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_reference_sample(cfg, reps, warm, use_ref=True):
+    """Reference CPU matvec (FP32 host weights, single thread) on one layer's seven
+    projections plus 1/16 of the output head; returns (tok/s, kind, detail)."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import __graft_entry__ as ge
+    orc = ge.oracle()
+    kind = "reference" if (use_ref and orc.Ref.available()) else "port"
+    impl = orc.Ref() if kind == "reference" else orc.Port()
+    D, F, H, Hkv, HD, V = cfg.dim, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.vocab
+    shapes = [(H * HD, D), (Hkv * HD, D), (Hkv * HD, D), (D, H * HD), (F, D), (D, F), (F, D)]
+    rng = np.random.default_rng(0)
+    mats = [(rng.standard_normal(r * c, dtype=np.float32) * 0.02, r, c) for r, c in shapes]
+    head_rows = V // 16
+    head = rng.standard_normal(head_rows * D, dtype=np.float32) * 0.02
+    xs = {c: rng.standard_normal(c, dtype=np.float32) for _, c in shapes}
+
+    def one():
+        t0 = time.perf_counter()
+        for W, r, c in mats:
+            impl.matvec_f32(W, xs[c], r, c)
+        t1 = time.perf_counter()
+        impl.matvec_f32(head, xs[D], head_rows, D)
+        t2 = time.perf_counter()
+        return cfg.n_layers * (t1 - t0) + 16 * (t2 - t1)
+
+    for _ in range(warm):
+        one()
+    per_tok = [one() for _ in range(reps)]
+    return 1.0 / statistics.mean(per_tok), kind, per_tok
+
+
+def run_reference(args, cfg, world, rank):
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    tps, kind, per = cpu_reference_sample(cfg, args.steps, args.warmup)
+    cores = 1
+    line = {"metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{cfg.name}-q4k-decode", "prompt": args.prompt,
+                       "parallelism": "cpu-1-thread"},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
+                             "sample": "per step: one layer's 7 projections + 1/16 of the output "
+                                       "head with the reference matvec (FP32 host weights), "
+                                       f"extrapolated to {cfg.n_layers} layers + full head"},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "host_cores": os.cpu_count(), "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="llama-3-8b")
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    sys.path.insert(0, ROOT)
+    ib = load_pkg()
+    from inference_cpp_b200 import gguf_writer as gw
+    cfg = gw.CONFIGS[args.workload]
+    # the KV cache holds prompt + warm-up + timed steps + the e2e steps
+    args.prompt = max(8, min(args.prompt, cfg.ctx - args.warmup - 2 * args.steps - 16))
+
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        rc = run_reference(args, cfg, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return rc
+
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    ib.init(local)
+    m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local)
+    rng = np.random.default_rng(42)
+    prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
+
+    ext = torch.cuda.ExternalStream(m.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # prefill (timed separately, reported as an extra field)
+    m.prefill(prompt[:16], 0)
+    torch.cuda.synchronize()
+    e0.record(ext)
+    first = m.prefill(prompt, 0)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+
+    pos = args.prompt
+    toks = m.decode_loop(first, pos, args.warmup)
+    pos += args.warmup
+    tok = int(toks[-1])
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    torch.cuda.synchronize()
+    e0.record(ext)
+    toks = m.decode_loop(tok, pos, args.steps)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    barrier(world)
+    dev_ms = all_max(world, e0.elapsed_time(e1))
+    pos += args.steps
+    tok = int(toks[-1])
+
+    # e2e: the per-token public call with host buffers
+    m.decode_loop(tok, pos, 2)  # settle
+    pos += 2
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    nxt = tok
+    e2e_steps = min(args.steps, cfg.ctx)
+    for i in range(e2e_steps):
+        nxt = m.decode(nxt, pos + i)
+    torch.cuda.synchronize()
+    e2e_s = all_max(world, time.perf_counter() - t0)
+    clk = clocks.stop()
+
+    kernels_per_step = m.step_kernels()
+    nbytes, gemv_ms, gemv_reps = time_gemv(ib, cfg)
+    peak, peak_kind = measured_peaks()
+    achieved = nbytes / (gemv_ms * 1e-3) / 1e9
+    weight_bytes = m.weight_bytes()
+
+    value = world * args.steps / (dev_ms * 1e-3)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            reps = 3
+            tps, kind, _ = cpu_reference_sample(cfg, reps, 1)
+            cpu = {"value": tps, "unit": "tok/s", "cores": 1, "kind": kind,
+                   "sample": f"{reps} samples of one layer's 7 projections + 1/16 of the output head "
+                             "(reference matvec, FP32 host weights, 1 thread), extrapolated to the "
+                             f"full {cfg.n_layers}-layer token"}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": 1, "kind": "unavailable", "sample": str(e)}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{cfg.name}-q4k-decode", "model": cfg.name,
+                       "prompt": args.prompt, "global_batch": world, "seq_len": pos,
+                       "parallelism": f"replica{world}" if world > 1 else "single",
+                       "weights": "Q4_K linears, Q6_K attn_v/ffn_down/output (synthetic)",
+                       "l2": "inputs larger than L2 (weights per step >> 126 MB)"},
+            "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tok/s",
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic_from_profile(),
+                         "kernel": f"gemv_q Q4_K {cfg.ffn}x{cfg.dim}",
+                         "bytes_per_launch": nbytes, "avg_launch_us": gemv_ms * 1e3,
+                         "peak_kind": peak_kind},
+            "decode_hbm": {"weight_bytes": weight_bytes,
+                           "achieved_gbs": weight_bytes * value / world / 1e9,
+                           "frac": weight_bytes * value / world / 1e9 / peak},
+            "prefill": {"tokens": args.prompt, "ms": prefill_ms,
+                        "tok_s": args.prompt / (prefill_ms * 1e-3)},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": kernels_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -148,6 +148,64 @@ int ib_attention_batch(const float* q, const float* kc, const float* vc, float* 
  * src/ops/ops.cpp:424-438), written to *dev_out. */
 int ib_argmax(const float* x, int n, int32_t* dev_out, void* stream);
 
+/* ---- native Llama runner on packed weights ----------------------------------
+ * Replaces the reference's GPU model driver (src/models/model_cuda.cpp:
+ * upload_weights :138-212, prefill :293-368, forward_token :372-407,
+ * generate_cuda :442-495; API include/models/cuda_model.hpp:9-32).  Weights
+ * stay in GGUF block form in HBM (precision NATIVE), or are converted on the
+ * GPU to the reference's symmetric INT16 (INT16, --gpu-precision int16) or to
+ * FP32 (FP32, --gpu-precision fp32).  Decoding is greedy (temperature 0,
+ * repetition penalty 1), the argmax runs on the device. */
+#define IB_PRECISION_NATIVE 0
+#define IB_PRECISION_INT16 1
+#define IB_PRECISION_FP32 2
+
+typedef struct {
+    int32_t n_layers, dim, n_heads, n_kv_heads, ffn, vocab, max_seq;
+    float rope_theta, rms_eps;
+    int32_t precision;
+} ib_model_config;
+
+/* GenerationStats (include/models/cuda_model.hpp:12-17). */
+typedef struct {
+    double init_ms, prefill_ms, decode_ms;
+    int32_t generated;
+} ib_generation_stats;
+
+int ib_model_create(const ib_model_config* cfg, int device, void** model);
+/* Tensor by its GGUF name ("token_embd.weight", "blk.3.attn_q.weight", ...),
+ * shape [rows, cols] (rows = output features), data in host or device memory. */
+int ib_model_set_tensor(void* model, const char* gguf_name, int type, int64_t rows,
+                        int64_t cols, const void* data, int data_on_device);
+/* Checks every tensor is set, allocates the FP32 KV cache and activations,
+ * builds the RoPE table (VRAM preflight as model_cuda.cpp:243-252). */
+int ib_model_finalize(void* model);
+/* Reads a GGUF file (metadata as src/models/transformer.cpp:139-154) and uploads
+ * its tensors unchanged; max_seq <= 0 takes llama.context_length. */
+int ib_model_load_gguf(const char* path, int precision, int device, int max_seq, void** model);
+int ib_model_free(void* model);
+/* Batched prompt prefill at positions start..start+T-1 (fills the KV cache);
+ * logits of the last position to host_logits (may be NULL), greedy id to *next. */
+int ib_model_prefill(void* model, const int32_t* host_ids, int T, int start,
+                     float* host_logits, int32_t* next);
+/* One decode step of `token` at `pos`; logits (optional) and greedy next id. */
+int ib_model_decode(void* model, int32_t token, int pos, float* host_logits, int32_t* next);
+/* Greedy generation: out = prompt + up to max_tokens ids (stops at eos_token_id
+ * when >= 0 or at the context end); *n_out = ids written. */
+int ib_model_generate(void* model, const int32_t* prompt, int n_prompt, int max_tokens,
+                      int32_t eos_token_id, int32_t* out, int* n_out, ib_generation_stats* stats);
+/* n_steps greedy steps on the device from `token` at `pos`, each argmax fed back
+ * as the next input without a host round trip; ids to host_tokens[0..n_steps). */
+int ib_model_decode_loop(void* model, int32_t token, int pos, int n_steps, int32_t* host_tokens);
+/* Capture the decode step in a CUDA graph (default on) or launch it directly. */
+int ib_model_set_graph(void* model, int enabled);
+/* The stream the model launches on (a cudaStream_t), e.g. for event timing. */
+int ib_model_stream(void* model, void** stream);
+/* Number of kernels one decode step launches. */
+int ib_model_step_kernels(void* model, int* n_kernels);
+/* Bytes of weights held on the device. */
+int ib_model_weight_bytes(void* model, size_t* bytes);
+
 /* ---- seeded synthetic weights (test and benchmark data, not a timed path) ---
  * Fills a [rows, cols] tensor of `type` with blocks encoding N(0, std) values
  * drawn from a counter-based stream keyed by `seed`.  The host and device

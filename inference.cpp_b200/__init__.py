@@ -312,3 +312,147 @@ def synth_device(type_: int, rows: int, cols: int, seed: int, std: float = 0.02,
         out = torch.empty(n, dtype=torch.uint8, device=device)
     call("ib_synth_device", type_, rows, cols, seed, std, _ptr(out), _stream(stream))
     return out
+
+
+# ---------------------------------------------------------------------------
+# native model runner (ib_model_*): the generate_cuda counterpart
+# ---------------------------------------------------------------------------
+NATIVE, INT16, FP32 = 0, 1, 2
+PRECISIONS = {"native": NATIVE, "int16": INT16, "fp32": FP32}
+
+
+class ModelConfig(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int32), ("dim", ctypes.c_int32),
+                ("n_heads", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
+                ("ffn", ctypes.c_int32), ("vocab", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("rope_theta", ctypes.c_float),
+                ("rms_eps", ctypes.c_float), ("precision", ctypes.c_int32)]
+
+
+class GenerationStats(ctypes.Structure):
+    _fields_ = [("init_ms", ctypes.c_double), ("prefill_ms", ctypes.c_double),
+                ("decode_ms", ctypes.c_double), ("generated", ctypes.c_int32)]
+
+
+SIGNATURES.update({
+    "ib_model_create": [_vp, _i, _vp],
+    "ib_model_set_tensor": [_vp, _c.c_char_p, _i, _i64, _i64, _vp, _i],
+    "ib_model_finalize": [_vp],
+    "ib_model_load_gguf": [_c.c_char_p, _i, _i, _i, _vp],
+    "ib_model_free": [_vp],
+    "ib_model_prefill": [_vp, _vp, _i, _i, _vp, _vp],
+    "ib_model_decode": [_vp, _c.c_int32, _i, _vp, _vp],
+    "ib_model_generate": [_vp, _vp, _i, _i, _c.c_int32, _vp, _vp, _vp],
+    "ib_model_set_graph": [_vp, _i],
+    "ib_model_weight_bytes": [_vp, _vp],
+    "ib_model_decode_loop": [_vp, _c.c_int32, _i, _i, _vp],
+    "ib_model_stream": [_vp, _vp],
+    "ib_model_step_kernels": [_vp, _vp],
+})
+
+
+class Model:
+    """A Llama model held on one GPU by the native runner."""
+
+    def __init__(self, handle, vocab: int):
+        self.h = ctypes.c_void_p(handle)
+        self.vocab = vocab
+
+    @classmethod
+    def create(cls, cfg, precision: int = NATIVE, device: int = 0, max_seq: int | None = None):
+        c = ModelConfig(cfg.n_layers, cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.ffn, cfg.vocab,
+                        max_seq or cfg.ctx, cfg.rope_theta, cfg.rms_eps, precision)
+        h = ctypes.c_void_p()
+        call("ib_model_create", ctypes.byref(c), device, ctypes.byref(h))
+        return cls(h.value, cfg.vocab)
+
+    @classmethod
+    def from_tensors(cls, cfg, tensors: dict, precision: int = NATIVE, device: int = 0,
+                     max_seq: int | None = None):
+        """tensors: {gguf name: (type, rows, cols, numpy bytes or CUDA tensor)}."""
+        m = cls.create(cfg, precision, device, max_seq)
+        for name, (t, r, c, data) in tensors.items():
+            m.set_tensor(name, t, r, c, data)
+        m.finalize()
+        return m
+
+    @classmethod
+    def from_gguf(cls, path: str, precision: int = NATIVE, device: int = 0, max_seq: int = 0):
+        h = ctypes.c_void_p()
+        call("ib_model_load_gguf", path.encode(), precision, device, max_seq, ctypes.byref(h))
+        from .gguf_writer import _read_vocab  # type: ignore
+        return cls(h.value, _read_vocab(path))
+
+    def set_tensor(self, name, type_, rows, cols, data):
+        on_dev = 0
+        if hasattr(data, "data_ptr"):
+            ptr, on_dev = data.data_ptr(), 1 if data.is_cuda else 0
+        else:
+            ptr = data.ctypes.data
+        call("ib_model_set_tensor", self.h, name.encode(), type_, rows, cols, ptr, on_dev)
+
+    def finalize(self):
+        call("ib_model_finalize", self.h)
+
+    def set_graph(self, enabled: bool):
+        call("ib_model_set_graph", self.h, 1 if enabled else 0)
+
+    def weight_bytes(self) -> int:
+        n = ctypes.c_size_t()
+        call("ib_model_weight_bytes", self.h, ctypes.byref(n))
+        return n.value
+
+    def prefill(self, ids, start: int = 0, want_logits: bool = False):
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        lg = np.empty(self.vocab, np.float32) if want_logits else None
+        nxt = ctypes.c_int32()
+        call("ib_model_prefill", self.h, ids.ctypes.data, ids.size, start,
+             lg.ctypes.data if want_logits else None, ctypes.byref(nxt))
+        return (nxt.value, lg) if want_logits else nxt.value
+
+    def decode(self, token: int, pos: int, want_logits: bool = False):
+        import numpy as np
+        lg = np.empty(self.vocab, np.float32) if want_logits else None
+        nxt = ctypes.c_int32()
+        call("ib_model_decode", self.h, int(token), int(pos),
+             lg.ctypes.data if want_logits else None, ctypes.byref(nxt))
+        return (nxt.value, lg) if want_logits else nxt.value
+
+    def decode_loop(self, token: int, pos: int, n_steps: int):
+        """n_steps greedy steps on the device; returns the generated ids."""
+        import numpy as np
+        out = np.empty(max(n_steps, 1), np.int32)
+        call("ib_model_decode_loop", self.h, int(token), int(pos), int(n_steps), out.ctypes.data)
+        return out[:n_steps]
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        call("ib_model_stream", self.h, ctypes.byref(s))
+        return s.value or 0
+
+    def step_kernels(self) -> int:
+        n = ctypes.c_int()
+        call("ib_model_step_kernels", self.h, ctypes.byref(n))
+        return n.value
+
+    def generate(self, prompt, max_tokens: int, eos: int = -1):
+        import numpy as np
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(prompt.size + max_tokens, np.int32)
+        n = ctypes.c_int()
+        st = GenerationStats()
+        call("ib_model_generate", self.h, prompt.ctypes.data, prompt.size, max_tokens, eos,
+             out.ctypes.data, ctypes.byref(n), ctypes.byref(st))
+        return out[:n.value], st
+
+    def close(self):
+        if self.h:
+            lib().ib_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,725 @@
+// Native Llama runner over the quantized-weight kernels -- the B200 counterpart
+// of the reference's GPU model driver (src/models/model_cuda.cpp):
+//   upload_weights (:138-212)  -> ib_model_set_tensor / ib_model_finalize: GGUF
+//                                 blocks are copied to HBM unchanged ("native"),
+//                                 or converted on the GPU to INT16 + row scale
+//                                 ("int16", bit-exact with make_weight) or FP32;
+//   prefill (:293-368)         -> ib_model_prefill: batched GEMM per linear;
+//   forward_token (:372-407)   -> ib_model_decode: one token, every kernel reads
+//                                 the position from device memory so the step is
+//                                 captured once as a CUDA graph and replayed;
+//   pick_token / generate_cuda -> greedy argmax on the device, ib_model_generate.
+// Layouts follow the reference: activations FP32, KV cache FP32
+// [layer][Hkv][max_seq][head_dim], RoPE from a host-built cos/sin table
+// (model_cuda.cpp:175-187).
+#include <math.h>
+
+#include <chrono>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gguf_reader.h"
+#include "model.h"
+#include "ops.cuh"
+#include "quant.cuh"
+
+namespace ib {
+
+__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float a = g[i];
+        g[i] = a * (1.0f / (1.0f + expf(-a))) * u[i];
+    }
+}
+
+// Greedy feedback at the end of a captured step: token <- next, pos <- pos + 1,
+// and the token is recorded at out_tokens[pos] (when given).
+__global__ void feedback_kernel(int32_t* dev_i32, int32_t* out_tokens, int max_seq) {
+    const int next = dev_i32[2], pos = dev_i32[1];
+    if (out_tokens && pos >= 0 && pos < max_seq) out_tokens[pos] = next;
+    dev_i32[0] = next;
+    dev_i32[1] = pos + 1;
+}
+
+__global__ void add_vec_kernel(float* __restrict__ a, const float* __restrict__ b, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        a[i] += b[i];
+}
+
+static double now_ms() {
+    return std::chrono::duration<double, std::milli>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+int Linear::forward(const float* x, float* y, cudaStream_t st) const {
+    switch (repr) {
+        case REPR_PACKED: return ib_gemv_q(type, w, x, y, rows, cols, st);
+        case REPR_I16: return ib_gemv_i16(q, s, x, y, (int)rows, (int)cols, st);
+        case REPR_F32: return ib_gemv(f, x, y, (int)rows, (int)cols, st);
+    }
+    return IB_ERR_INVALID;
+}
+
+int Linear::forward_batch(const float* X, float* Y, int T, cudaStream_t st) const {
+    switch (repr) {
+        case REPR_PACKED: return ib_gemm_q(type, w, X, Y, T, rows, cols, st);
+        case REPR_I16: return ib_gemm_i16(q, s, X, Y, T, (int)rows, (int)cols, st);
+        case REPR_F32: return ib_gemm(f, X, Y, T, (int)rows, (int)cols, st);
+    }
+    return IB_ERR_INVALID;
+}
+
+void Linear::release() {
+    if (w) cudaFree(w);
+    if (q) cudaFree(q);
+    if (s) cudaFree(s);
+    if (f) cudaFree(f);
+    w = nullptr;
+    q = nullptr;
+    s = nullptr;
+    f = nullptr;
+}
+
+Model::~Model() {
+    if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    if (stream) cudaStreamDestroy(stream);
+    tok.release();
+    out.release();
+    for (auto& L : layers) {
+        for (Linear* l : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3}) l->release();
+        cudaFree(L.attn_norm);
+        cudaFree(L.ffn_norm);
+    }
+    for (void* p : allocations) cudaFree(p);
+    if (host_pinned) cudaFreeHost(host_pinned);
+}
+
+}  // namespace ib
+
+using namespace ib;
+
+static int set_linear(Model* m, Linear& L, int type, int64_t rows, int64_t cols,
+                      const void* data, int on_device) {
+    if (!is_block_quant(type) && type != IB_TYPE_F32 && type != IB_TYPE_F16) {
+        set_error(std::string("model: unsupported tensor type ") + type_name(type));
+        return IB_ERR_UNSUPPORTED;
+    }
+    L.release();
+    L.type = type;
+    L.rows = rows;
+    L.cols = cols;
+    const int64_t nbytes = type == IB_TYPE_F32   ? rows * cols * 4
+                           : type == IB_TYPE_F16 ? rows * cols * 2
+                                                 : packed_bytes(type, rows, cols);
+    void* dev = nullptr;
+    // +16 so 16-byte vector loads of the last block never leave the allocation
+    IB_CUDA_CHECK(cudaMalloc(&dev, (size_t)nbytes + 16));
+    IB_CUDA_CHECK(cudaMemcpyAsync(dev, data, (size_t)nbytes,
+                                  on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                  m->stream));
+    const bool packed_ok = is_block_quant(type) && m->cfg.precision == IB_PRECISION_NATIVE;
+    if (packed_ok) {
+        L.repr = REPR_PACKED;
+        L.w = dev;
+        return IB_OK;
+    }
+    // INT16 (reference gpu_int16) or FP32 copies, produced on the GPU
+    int st = IB_OK;
+    if (m->cfg.precision == IB_PRECISION_INT16) {
+        IB_CUDA_CHECK(cudaMalloc(&L.q, (size_t)(rows * cols) * 2 + 16));
+        IB_CUDA_CHECK(cudaMalloc(&L.s, (size_t)rows * 4));
+        float* tmp = nullptr;
+        if (type == IB_TYPE_F16) {
+            IB_CUDA_CHECK(cudaMalloc(&tmp, (size_t)(rows * cols) * 4));
+            st = ib_dequant_f32(type, dev, tmp, rows, cols, m->stream);
+            if (st == IB_OK) st = ib_dequant_i16(IB_TYPE_F32, tmp, L.q, L.s, rows, cols, m->stream);
+        } else {
+            st = ib_dequant_i16(type, dev, L.q, L.s, rows, cols, m->stream);
+        }
+        IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+        if (tmp) cudaFree(tmp);
+        L.repr = REPR_I16;
+    } else {
+        IB_CUDA_CHECK(cudaMalloc(&L.f, (size_t)(rows * cols) * 4 + 16));
+        st = ib_dequant_f32(type, dev, L.f, rows, cols, m->stream);
+        IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+        L.repr = REPR_F32;
+    }
+    cudaFree(dev);
+    return st;
+}
+
+static int set_vector(Model* m, float** dst, int type, int64_t n, const void* data, int on_device) {
+    if (*dst) cudaFree(*dst);
+    IB_CUDA_CHECK(cudaMalloc(dst, (size_t)n * 4));
+    if (type == IB_TYPE_F32) {
+        IB_CUDA_CHECK(cudaMemcpyAsync(*dst, data, (size_t)n * 4,
+                                      on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                      m->stream));
+        return IB_OK;
+    }
+    if (type == IB_TYPE_F16) {
+        void* tmp = nullptr;
+        IB_CUDA_CHECK(cudaMalloc(&tmp, (size_t)n * 2));
+        IB_CUDA_CHECK(cudaMemcpyAsync(tmp, data, (size_t)n * 2,
+                                      on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                      m->stream));
+        int st = ib_dequant_f32(IB_TYPE_F16, tmp, *dst, 1, n, m->stream);
+        IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+        cudaFree(tmp);
+        return st;
+    }
+    set_error("model: norm weights must be F32 or F16");
+    return IB_ERR_UNSUPPORTED;
+}
+
+extern "C" int ib_model_create(const ib_model_config* cfg, int device, void** out) {
+    IB_REQUIRE(cfg && out, "null pointer argument");
+    *out = nullptr;
+    IB_REQUIRE(cfg->n_layers >= 0 && cfg->dim > 0 && cfg->n_heads > 0 && cfg->n_kv_heads > 0 &&
+                   cfg->n_heads % cfg->n_kv_heads == 0 && cfg->dim % cfg->n_heads == 0 &&
+                   cfg->ffn > 0 && cfg->vocab > 0 && cfg->max_seq > 0,
+               "model: invalid configuration");
+    IB_REQUIRE(cfg->precision >= 0 && cfg->precision <= 2, "model: precision must be 0, 1 or 2");
+    IB_REQUIRE((cfg->dim / cfg->n_heads) % 2 == 0, "model: head_dim must be even");
+    int st = ib_init(device);
+    if (st != IB_OK) return st;
+    auto m = std::make_unique<Model>();
+    m->cfg = *cfg;
+    m->device = device;
+    m->HD = cfg->dim / cfg->n_heads;
+    IB_CUDA_CHECK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    m->layers.resize(cfg->n_layers);
+    *out = m.release();
+    return IB_OK;
+}
+
+extern "C" int ib_model_free(void* h) {
+    if (!h) return IB_OK;
+    Model* m = (Model*)h;
+    cudaSetDevice(m->device);
+    delete m;
+    return IB_OK;
+}
+
+// Tensor names as the reference loader reads them (src/models/transformer.cpp:267-306).
+extern "C" int ib_model_set_tensor(void* h, const char* name, int type, int64_t rows,
+                                   int64_t cols, const void* data, int on_device) {
+    IB_REQUIRE(h && name && data, "null pointer argument");
+    Model* m = (Model*)h;
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    IB_REQUIRE(!m->finalized, "model: tensors cannot change after finalize");
+    const std::string n(name);
+    const auto& c = m->cfg;
+    const int D = c.dim, HD = m->HD;
+    auto expect = [&](int64_t r, int64_t cc) -> int {
+        if (rows != r || cols != cc) {
+            set_error("model: tensor " + n + " has shape [" + std::to_string(rows) + ", " +
+                      std::to_string(cols) + "], expected [" + std::to_string(r) + ", " +
+                      std::to_string(cc) + "]");
+            return IB_ERR_INVALID;
+        }
+        return IB_OK;
+    };
+    int st;
+    if (n == "token_embd.weight") {
+        if ((st = expect(c.vocab, D))) return st;
+        return set_linear(m, m->tok, type, rows, cols, data, on_device);
+    }
+    if (n == "output.weight") {
+        if ((st = expect(c.vocab, D))) return st;
+        m->has_output = true;
+        return set_linear(m, m->out, type, rows, cols, data, on_device);
+    }
+    if (n == "output_norm.weight") {
+        if ((st = expect(1, D))) return st;
+        return set_vector(m, &m->out_norm, type, D, data, on_device);
+    }
+    int l = -1;
+    char kind[64] = {0};
+    if (sscanf(name, "blk.%d.%63[a-z_].weight", &l, kind) != 2 || l < 0 || l >= c.n_layers) {
+        set_error("model: unknown tensor " + n);
+        return IB_ERR_INVALID;
+    }
+    Layer& L = m->layers[l];
+    const std::string k(kind);
+    if (k == "attn_q") { if ((st = expect((int64_t)c.n_heads * HD, D))) return st; return set_linear(m, L.wq, type, rows, cols, data, on_device); }
+    if (k == "attn_k") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wk, type, rows, cols, data, on_device); }
+    if (k == "attn_v") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wv, type, rows, cols, data, on_device); }
+    if (k == "attn_output") { if ((st = expect(D, (int64_t)c.n_heads * HD))) return st; return set_linear(m, L.wo, type, rows, cols, data, on_device); }
+    if (k == "ffn_gate") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w1, type, rows, cols, data, on_device); }
+    if (k == "ffn_down") { if ((st = expect(D, c.ffn))) return st; return set_linear(m, L.w2, type, rows, cols, data, on_device); }
+    if (k == "ffn_up") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w3, type, rows, cols, data, on_device); }
+    if (k == "attn_norm") { if ((st = expect(1, D))) return st; return set_vector(m, &L.attn_norm, type, D, data, on_device); }
+    if (k == "ffn_norm") { if ((st = expect(1, D))) return st; return set_vector(m, &L.ffn_norm, type, D, data, on_device); }
+    set_error("model: unknown tensor " + n);
+    return IB_ERR_INVALID;
+}
+
+static int alloc_f(Model* m, float** p, size_t n) {
+    IB_CUDA_CHECK(cudaMalloc(p, n * sizeof(float) + 16));
+    m->allocations.push_back(*p);
+    return IB_OK;
+}
+
+extern "C" int ib_model_finalize(void* h) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    if (m->finalized) return IB_OK;
+    const auto& c = m->cfg;
+    auto missing = [&](const std::string& what) {
+        set_error("model: tensor not set: " + what);
+        return IB_ERR_INVALID;
+    };
+    if (m->tok.repr == REPR_NONE) return missing("token_embd.weight");
+    if (!m->out_norm) return missing("output_norm.weight");
+    for (int l = 0; l < c.n_layers; ++l) {
+        Layer& L = m->layers[l];
+        const std::string p = "blk." + std::to_string(l) + ".";
+        if (L.wq.repr == REPR_NONE) return missing(p + "attn_q.weight");
+        if (L.wk.repr == REPR_NONE) return missing(p + "attn_k.weight");
+        if (L.wv.repr == REPR_NONE) return missing(p + "attn_v.weight");
+        if (L.wo.repr == REPR_NONE) return missing(p + "attn_output.weight");
+        if (L.w1.repr == REPR_NONE) return missing(p + "ffn_gate.weight");
+        if (L.w2.repr == REPR_NONE) return missing(p + "ffn_down.weight");
+        if (L.w3.repr == REPR_NONE) return missing(p + "ffn_up.weight");
+        if (!L.attn_norm) return missing(p + "attn_norm.weight");
+        if (!L.ffn_norm) return missing(p + "ffn_norm.weight");
+    }
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
+    const int S = c.max_seq;
+    // VRAM preflight as the reference does before upload (model_cuda.cpp:243-252)
+    const size_t kv_bytes = (size_t)c.n_layers * 2 * Hkv * (size_t)S * HD * 4;
+    size_t free_b = 0, total_b = 0;
+    IB_CUDA_CHECK(cudaMemGetInfo(&free_b, &total_b));
+    if (kv_bytes + (64ull << 20) > free_b) {
+        set_error("CUDA: model needs ~" + std::to_string(kv_bytes >> 20) +
+                  " MB VRAM for the KV cache but only " + std::to_string(free_b >> 20) +
+                  " MB is free. Reduce the context length.");
+        return IB_ERR_OOM;
+    }
+    for (auto& L : m->layers) {
+        int st;
+        if ((st = alloc_f(m, &L.kc, (size_t)Hkv * S * HD))) return st;
+        if ((st = alloc_f(m, &L.vc, (size_t)Hkv * S * HD))) return st;
+        IB_CUDA_CHECK(cudaMemsetAsync(L.kc, 0, (size_t)Hkv * S * HD * 4, m->stream));
+        IB_CUDA_CHECK(cudaMemsetAsync(L.vc, 0, (size_t)Hkv * S * HD * 4, m->stream));
+    }
+    // RoPE table, computed on the host exactly as model_cuda.cpp:175-187 does
+    const int half = HD / 2;
+    std::vector<float> table((size_t)S * half * 2);
+    for (int pos = 0; pos < S; ++pos)
+        for (int j = 0; j < half; ++j) {
+            const float freq = 1.0f / powf(c.rope_theta, (float)(2 * j) / (float)HD);
+            const float angle = (float)pos * freq;
+            table[((size_t)pos * half + j) * 2] = cosf(angle);
+            table[((size_t)pos * half + j) * 2 + 1] = sinf(angle);
+        }
+    int st;
+    if ((st = alloc_f(m, &m->rope_table, table.size()))) return st;
+    IB_CUDA_CHECK(cudaMemcpyAsync(m->rope_table, table.data(), table.size() * 4,
+                                  cudaMemcpyHostToDevice, m->stream));
+    // decode activations
+    float** bufs[] = {&m->x, &m->xn, &m->q, &m->k, &m->v, &m->att, &m->proj, &m->gate, &m->up,
+                      &m->logits};
+    const size_t sizes[] = {(size_t)D, (size_t)D, (size_t)H * HD, (size_t)Hkv * HD,
+                            (size_t)Hkv * HD, (size_t)H * HD, (size_t)D, (size_t)F, (size_t)F,
+                            (size_t)V};
+    for (int i = 0; i < 10; ++i)
+        if ((st = alloc_f(m, bufs[i], sizes[i]))) return st;
+    if ((st = alloc_f(m, &m->att_part, attention_partial_bytes(H, HD, S - 1) / 4 + 1))) return st;
+    IB_CUDA_CHECK(cudaMalloc(&m->dev_i32, 64));
+    m->allocations.push_back(m->dev_i32);
+    IB_CUDA_CHECK(cudaMalloc(&m->dev_tokens, (size_t)S * 4 + 16));
+    m->allocations.push_back(m->dev_tokens);
+    IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    m->finalized = true;
+    return IB_OK;
+}
+
+namespace ib {
+
+// One decode step for the token in dev_i32[0] at position dev_i32[1]; the greedy
+// next token lands in dev_i32[2].  Every launch reads the position on the device.
+static int decode_launches(Model* m) {
+    const auto& c = m->cfg;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
+    cudaStream_t st = m->stream;
+    const int* tok = m->dev_i32;
+    const int* pos = m->dev_i32 + 1;
+    const float scale = 1.0f / sqrtf((float)HD);
+    int r;
+    if (m->tok.repr == REPR_PACKED) r = ib_embedding_q(m->tok.type, m->tok.w, tok, m->x, 1, V, D, st);
+    else if (m->tok.repr == REPR_I16) r = ib_embedding_batch_i16(m->tok.q, m->tok.s, tok, m->x, 1, D, st);
+    else r = ib_embedding_batch(m->tok.f, tok, m->x, 1, D, st);
+    if (r) return r;
+    const int g_add = (D + 255) / 256 < 1184 ? (D + 255) / 256 : 1184;
+    const int g_ffn = (F + 255) / 256 < 1184 ? (F + 255) / 256 : 1184;
+    for (auto& L : m->layers) {
+        if ((r = rmsnorm_launch(m->x, L.attn_norm, m->xn, 1, D, c.rms_eps, st))) return r;
+        if ((r = L.wq.forward(m->xn, m->q, st))) return r;
+        if ((r = L.wk.forward(m->xn, m->k, st))) return r;
+        if ((r = L.wv.forward(m->xn, m->v, st))) return r;
+        if ((r = rope_launch(m->q, m->k, m->rope_table, H, Hkv, HD, 0, 1, st, pos))) return r;
+        if ((r = kv_write_launch(L.kc, L.vc, m->k, m->v, Hkv, HD, c.max_seq, 0, 1, st, pos))) return r;
+        if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
+                                  m->att_part, st, pos)))
+            return r;
+        if ((r = L.wo.forward(m->att, m->proj, st))) return r;
+        add_vec_kernel<<<g_add, 256, 0, st>>>(m->x, m->proj, D);
+        if ((r = rmsnorm_launch(m->x, L.ffn_norm, m->xn, 1, D, c.rms_eps, st))) return r;
+        if ((r = L.w1.forward(m->xn, m->gate, st))) return r;
+        if ((r = L.w3.forward(m->xn, m->up, st))) return r;
+        silu_mul_kernel<<<g_ffn, 256, 0, st>>>(m->gate, m->up, F);
+        if ((r = L.w2.forward(m->gate, m->proj, st))) return r;
+        add_vec_kernel<<<g_add, 256, 0, st>>>(m->x, m->proj, D);
+    }
+    if ((r = rmsnorm_launch(m->x, m->out_norm, m->xn, 1, D, c.rms_eps, st))) return r;
+    const Linear& O = m->has_output ? m->out : m->tok;
+    if ((r = O.forward(m->xn, m->logits, st))) return r;
+    if ((r = argmax_launch(m->logits, V, m->dev_i32 + 2, st))) return r;
+    feedback_kernel<<<1, 1, 0, st>>>(m->dev_i32, m->dev_tokens, c.max_seq);
+    IB_LAUNCH_CHECK("decode step");
+    return IB_OK;
+}
+
+static int ensure_graph(Model* m) {
+    if (m->graph_exec || !m->use_graph) return IB_OK;
+    cudaGraph_t g = nullptr;
+    IB_CUDA_CHECK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int r = decode_launches(m);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (r != IB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return r;
+    }
+    IB_CUDA_CHECK(e);
+    IB_CUDA_CHECK(cudaGraphInstantiate(&m->graph_exec, g, 0));
+    cudaGraphDestroy(g);
+    return IB_OK;
+}
+
+int decode_step(Model* m, int token, int pos, float* host_logits, int* next) {
+    IB_REQUIRE(pos >= 0 && pos < m->cfg.max_seq, "CUDA generate: position beyond the context");
+    int* hp = (int*)m->host_pinned;
+    hp[0] = token;
+    hp[1] = pos;
+    IB_CUDA_CHECK(cudaMemcpyAsync(m->dev_i32, hp, 8, cudaMemcpyHostToDevice, m->stream));
+    int r = ensure_graph(m);
+    if (r) return r;
+    if (m->graph_exec) {
+        IB_CUDA_CHECK(cudaGraphLaunch(m->graph_exec, m->stream));
+    } else if ((r = decode_launches(m))) {
+        return r;
+    }
+    IB_CUDA_CHECK(cudaMemcpyAsync(hp + 2, m->dev_i32 + 2, 4, cudaMemcpyDeviceToHost, m->stream));
+    if (host_logits)
+        IB_CUDA_CHECK(cudaMemcpyAsync(host_logits, m->logits, (size_t)m->cfg.vocab * 4,
+                                      cudaMemcpyDeviceToHost, m->stream));
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    if (next) *next = hp[2];
+    return IB_OK;
+}
+
+static int ensure_prefill_scratch(Model* m, int T) {
+    if (T <= m->pf_cap) return IB_OK;
+    for (void* p : m->pf_bufs) cudaFree(p);
+    m->pf_bufs.clear();
+    const auto& c = m->cfg;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn;
+    float** bufs[] = {&m->pf_x, &m->pf_xn, &m->pf_q, &m->pf_k, &m->pf_v, &m->pf_att, &m->pf_proj,
+                      &m->pf_gate, &m->pf_up};
+    const size_t per[] = {(size_t)D, (size_t)D, (size_t)H * HD, (size_t)Hkv * HD, (size_t)Hkv * HD,
+                          (size_t)H * HD, (size_t)D, (size_t)F, (size_t)F};
+    size_t need = 0;
+    for (size_t s : per) need += s * T * 4;
+    size_t free_b = 0, total_b = 0;
+    IB_CUDA_CHECK(cudaMemGetInfo(&free_b, &total_b));
+    if (need + (32ull << 20) > free_b) {
+        set_error("CUDA prefill: prompt needs ~" + std::to_string(need >> 20) +
+                  " MB scratch but only " + std::to_string(free_b >> 20) +
+                  " MB VRAM is free. Shorten the prompt or use the CPU backend.");
+        return IB_ERR_OOM;
+    }
+    for (int i = 0; i < 9; ++i) {
+        IB_CUDA_CHECK(cudaMalloc(bufs[i], per[i] * T * 4 + 16));
+        m->pf_bufs.push_back(*bufs[i]);
+    }
+    IB_CUDA_CHECK(cudaMalloc(&m->pf_ids, (size_t)T * 4 + 16));
+    m->pf_bufs.push_back(m->pf_ids);
+    m->pf_cap = T;
+    return IB_OK;
+}
+
+int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_logits, int* next) {
+    const auto& c = m->cfg;
+    IB_REQUIRE(T > 0 && start >= 0 && start + T <= c.max_seq, "CUDA generate: prompt longer than context");
+    int r = ensure_prefill_scratch(m, T);
+    if (r) return r;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
+    cudaStream_t st = m->stream;
+    IB_CUDA_CHECK(cudaMemcpyAsync(m->pf_ids, host_ids, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+    if (m->tok.repr == REPR_PACKED) r = ib_embedding_q(m->tok.type, m->tok.w, m->pf_ids, m->pf_x, T, V, D, st);
+    else if (m->tok.repr == REPR_I16) r = ib_embedding_batch_i16(m->tok.q, m->tok.s, m->pf_ids, m->pf_x, T, D, st);
+    else r = ib_embedding_batch(m->tok.f, m->pf_ids, m->pf_x, T, D, st);
+    if (r) return r;
+    const float scale = 1.0f / sqrtf((float)HD);
+    for (auto& L : m->layers) {
+        if ((r = rmsnorm_launch(m->pf_x, L.attn_norm, m->pf_xn, T, D, c.rms_eps, st))) return r;
+        if ((r = L.wq.forward_batch(m->pf_xn, m->pf_q, T, st))) return r;
+        if ((r = L.wk.forward_batch(m->pf_xn, m->pf_k, T, st))) return r;
+        if ((r = L.wv.forward_batch(m->pf_xn, m->pf_v, T, st))) return r;
+        if ((r = rope_launch(m->pf_q, m->pf_k, m->rope_table, H, Hkv, HD, start, T, st, nullptr))) return r;
+        if ((r = kv_write_launch(L.kc, L.vc, m->pf_k, m->pf_v, Hkv, HD, c.max_seq, start, T, st, nullptr))) return r;
+        if ((r = attention_batch_launch(m->pf_q, L.kc, L.vc, m->pf_att, H, Hkv, HD, c.max_seq, start,
+                                        T, scale, st)))
+            return r;
+        if ((r = L.wo.forward_batch(m->pf_att, m->pf_proj, T, st))) return r;
+        if ((r = elementwise_launch(2, m->pf_x, m->pf_proj, T * D, st))) return r;
+        if ((r = rmsnorm_launch(m->pf_x, L.ffn_norm, m->pf_xn, T, D, c.rms_eps, st))) return r;
+        if ((r = L.w1.forward_batch(m->pf_xn, m->pf_gate, T, st))) return r;
+        if ((r = L.w3.forward_batch(m->pf_xn, m->pf_up, T, st))) return r;
+        silu_mul_kernel<<<1184, 256, 0, st>>>(m->pf_gate, m->pf_up, T * F);
+        if ((r = L.w2.forward_batch(m->pf_gate, m->pf_proj, T, st))) return r;
+        if ((r = elementwise_launch(2, m->pf_x, m->pf_proj, T * D, st))) return r;
+    }
+    // logits of the last prompt position only (model_cuda.cpp:394-398)
+    if ((r = rmsnorm_launch(m->pf_x + (size_t)(T - 1) * D, m->out_norm, m->xn, 1, D, c.rms_eps, st))) return r;
+    const Linear& O = m->has_output ? m->out : m->tok;
+    if ((r = O.forward(m->xn, m->logits, st))) return r;
+    if ((r = argmax_launch(m->logits, V, m->dev_i32 + 2, st))) return r;
+    int* hp = (int*)m->host_pinned;
+    IB_CUDA_CHECK(cudaMemcpyAsync(hp + 2, m->dev_i32 + 2, 4, cudaMemcpyDeviceToHost, st));
+    if (host_logits)
+        IB_CUDA_CHECK(cudaMemcpyAsync(host_logits, m->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, st));
+    IB_CUDA_CHECK(cudaStreamSynchronize(st));
+    if (next) *next = hp[2];
+    return IB_OK;
+}
+
+}  // namespace ib
+
+extern "C" int ib_model_prefill(void* h, const int32_t* host_ids, int T, int start,
+                                float* host_logits, int32_t* next) {
+    IB_REQUIRE(h && host_ids, "null pointer argument");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized, "model: call ib_model_finalize first");
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    return prefill(m, host_ids, T, start, host_logits, next);
+}
+
+extern "C" int ib_model_decode(void* h, int32_t token, int pos, float* host_logits,
+                               int32_t* next) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized, "model: call ib_model_finalize first");
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    return decode_step(m, token, pos, host_logits, next);
+}
+
+// n_steps greedy decode steps entirely on the device: token `token` at `pos`,
+// each step's argmax fed back as the next input (no host round trip between
+// steps).  The generated ids are copied to host_tokens[0..n_steps).
+extern "C" int ib_model_decode_loop(void* h, int32_t token, int pos, int n_steps,
+                                    int32_t* host_tokens) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized, "model: call ib_model_finalize first");
+    IB_REQUIRE(n_steps >= 0 && pos >= 0 && pos + n_steps <= m->cfg.max_seq,
+               "CUDA generate: position beyond the context");
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    int* hp = (int*)m->host_pinned;
+    hp[0] = token;
+    hp[1] = pos;
+    IB_CUDA_CHECK(cudaMemcpyAsync(m->dev_i32, hp, 8, cudaMemcpyHostToDevice, m->stream));
+    int r = ensure_graph(m);
+    if (r) return r;
+    for (int i = 0; i < n_steps; ++i) {
+        if (m->graph_exec) IB_CUDA_CHECK(cudaGraphLaunch(m->graph_exec, m->stream));
+        else if ((r = decode_launches(m))) return r;
+    }
+    if (host_tokens && n_steps > 0)
+        IB_CUDA_CHECK(cudaMemcpyAsync(host_tokens, m->dev_tokens + pos, (size_t)n_steps * 4,
+                                      cudaMemcpyDeviceToHost, m->stream));
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    return IB_OK;
+}
+
+// The stream the model launches on (cudaStream_t as void*), for event timing.
+extern "C" int ib_model_stream(void* h, void** stream) {
+    IB_REQUIRE(h && stream, "null pointer argument");
+    *stream = ((Model*)h)->stream;
+    return IB_OK;
+}
+
+// Kernels launched by one decode step (nodes of the captured graph).
+extern "C" int ib_model_step_kernels(void* h, int* n) {
+    IB_REQUIRE(h && n, "null pointer argument");
+    Model* m = (Model*)h;
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    int r = ensure_graph(m);
+    if (r) return r;
+    cudaGraph_t g = nullptr;
+    IB_CUDA_CHECK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    r = decode_launches(m);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (r) { if (g) cudaGraphDestroy(g); return r; }
+    IB_CUDA_CHECK(e);
+    size_t count = 0;
+    IB_CUDA_CHECK(cudaGraphGetNodes(g, nullptr, &count));
+    std::vector<cudaGraphNode_t> nodes(count);
+    IB_CUDA_CHECK(cudaGraphGetNodes(g, nodes.data(), &count));
+    int k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        IB_CUDA_CHECK(cudaGraphNodeGetType(nd, &t));
+        if (t == cudaGraphNodeTypeKernel) ++k;
+    }
+    cudaGraphDestroy(g);
+    *n = k;
+    return IB_OK;
+}
+
+extern "C" int ib_model_set_graph(void* h, int enabled) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    m->use_graph = enabled != 0;
+    if (!m->use_graph && m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    return IB_OK;
+}
+
+// Greedy generation with the reference's loop structure (generate_cuda,
+// model_cuda.cpp:442-495): batched prefill, first token from the prefill
+// logits, then one decode step per token until max_tokens, the context end, or
+// eos_token_id (when >= 0).
+extern "C" int ib_model_generate(void* h, const int32_t* prompt, int n_prompt, int max_tokens,
+                                 int32_t eos_token_id, int32_t* out, int* n_out,
+                                 ib_generation_stats* stats) {
+    IB_REQUIRE(h && prompt && out && n_out, "null pointer argument");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized, "model: call ib_model_finalize first");
+    if (n_prompt <= 0) {
+        set_error("CUDA generate: empty prompt");
+        return IB_ERR_INVALID;
+    }
+    if (n_prompt > m->cfg.max_seq) {
+        set_error("CUDA generate: prompt longer than context");
+        return IB_ERR_INVALID;
+    }
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    const double t1 = now_ms();
+    int n = 0;
+    for (int i = 0; i < n_prompt; ++i) out[n++] = prompt[i];
+    int next = 0;
+    int r = prefill(m, prompt, n_prompt, 0, nullptr, &next);
+    if (r) return r;
+    const double t2 = now_ms();
+    int pos = n_prompt;
+    if (max_tokens > 0) out[n++] = next;
+    for (int step = 1; step < max_tokens; ++step) {
+        if (eos_token_id >= 0 && next == eos_token_id) break;
+        if (pos >= m->cfg.max_seq) break;
+        if ((r = decode_step(m, next, pos, nullptr, &next))) return r;
+        ++pos;
+        out[n++] = next;
+    }
+    const double t3 = now_ms();
+    *n_out = n;
+    if (stats) {
+        stats->init_ms = 0;
+        stats->prefill_ms = t2 - t1;
+        stats->decode_ms = t3 - t2;
+        stats->generated = n - n_prompt;
+    }
+    return IB_OK;
+}
+
+// Loads a GGUF file: metadata keys as load_model_weights reads them
+// (src/models/transformer.cpp:139-154), tensors copied to HBM in their GGUF form.
+extern "C" int ib_model_load_gguf(const char* path, int precision, int device, int max_seq,
+                                  void** out) {
+    IB_REQUIRE(path && out, "null pointer argument");
+    *out = nullptr;
+    try {
+        GGUFFile f;
+        f.open(path);
+        ib_model_config c{};
+        c.n_layers = (int)f.get_int("llama.block_count", 0);
+        c.dim = (int)f.get_int("llama.embedding_length", 0);
+        c.n_heads = (int)f.get_int("llama.attention.head_count", 0);
+        c.n_kv_heads = (int)f.get_int("llama.attention.head_count_kv", c.n_heads);
+        c.max_seq = max_seq > 0 ? max_seq : (int)f.get_int("llama.context_length", 2048);
+        c.rope_theta = f.get_float("llama.rope.freq_base", 10000.0f);
+        c.rms_eps = f.get_float("llama.attention.layer_norm_rms_epsilon", 1e-6f);
+        c.precision = precision;
+        const auto* te = f.find("token_embd.weight");
+        if (!te || te->dims.size() != 2) {
+            set_error("Tensor not found: token_embd.weight");
+            return IB_ERR_INVALID;
+        }
+        c.vocab = (int)te->dims[1];
+        const auto* g = f.find("blk.0.ffn_gate.weight");
+        c.ffn = g && g->dims.size() == 2 ? (int)g->dims[1] : (int)f.get_int("llama.feed_forward_length", 0);
+        void* h = nullptr;
+        int st = ib_model_create(&c, device, &h);
+        if (st) return st;
+        for (const auto& t : f.tensors()) {
+            int64_t cols = t.dims.empty() ? 0 : t.dims[0];
+            int64_t rows = 1;
+            for (size_t d = 1; d < t.dims.size(); ++d) rows *= t.dims[d];
+            const int64_t nb = t.type == IB_TYPE_F32 ? rows * cols * 4
+                               : t.type == IB_TYPE_F16 ? rows * cols * 2
+                                                       : packed_bytes(t.type, rows, cols);
+            if (nb < 0) {
+                ib_model_free(h);
+                set_error("model: unsupported tensor type in " + t.name);
+                return IB_ERR_UNSUPPORTED;
+            }
+            st = ib_model_set_tensor(h, t.name.c_str(), t.type, rows, cols, f.data(t, (size_t)nb), 0);
+            if (st) {
+                if (st == IB_ERR_INVALID && ib::last_error().rfind("model: unknown tensor", 0) == 0) continue;
+                ib_model_free(h);
+                return st;
+            }
+        }
+        Model* m = (Model*)h;
+        IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+        st = ib_model_finalize(h);
+        if (st) {
+            ib_model_free(h);
+            return st;
+        }
+        *out = h;
+        return IB_OK;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return IB_ERR_INVALID;
+    }
+}
+
+extern "C" int ib_model_weight_bytes(void* h, size_t* bytes) {
+    IB_REQUIRE(h && bytes, "null pointer argument");
+    Model* m = (Model*)h;
+    size_t n = 0;
+    auto add = [&](const Linear& L) {
+        if (L.repr == REPR_PACKED) n += (size_t)packed_bytes(L.type, L.rows, L.cols);
+        else if (L.repr == REPR_I16) n += (size_t)(L.rows * L.cols) * 2 + (size_t)L.rows * 4;
+        else if (L.repr == REPR_F32) n += (size_t)(L.rows * L.cols) * 4;
+    };
+    add(m->tok);
+    if (m->has_output) add(m->out);
+    for (auto& L : m->layers)
+        for (const Linear* l : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3}) add(*l);
+    n += (size_t)m->cfg.dim * 4 * (1 + 2 * m->cfg.n_layers);
+    *bytes = n;
+    return IB_OK;
+}

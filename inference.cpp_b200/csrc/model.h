@@ -1,0 +1,68 @@
+// Internal state of the native model runner (model.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/ib_cuda.h"
+
+namespace ib {
+
+enum Repr { REPR_NONE = 0, REPR_PACKED = 1, REPR_I16 = 2, REPR_F32 = 3 };
+
+// One weight matrix [rows, cols]: GGUF blocks (packed), INT16 + row scale, or FP32.
+struct Linear {
+    int repr = REPR_NONE;
+    int type = 0;
+    int64_t rows = 0, cols = 0;
+    void* w = nullptr;       // packed blocks
+    int16_t* q = nullptr;    // INT16 values
+    float* s = nullptr;      // INT16 row scales
+    float* f = nullptr;      // FP32 values
+    int forward(const float* x, float* y, cudaStream_t st) const;
+    int forward_batch(const float* X, float* Y, int T, cudaStream_t st) const;
+    void release();
+};
+
+struct Layer {
+    Linear wq, wk, wv, wo, w1, w2, w3;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    float* kc = nullptr;  // [Hkv][max_seq][HD]
+    float* vc = nullptr;
+};
+
+struct Model {
+    ib_model_config cfg{};
+    int device = 0;
+    int HD = 0;
+    bool finalized = false;
+    bool has_output = false;
+    bool use_graph = true;
+    Linear tok, out;
+    float* out_norm = nullptr;
+    std::vector<Layer> layers;
+    float* rope_table = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    // decode activations
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
+    float *proj = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *att_part = nullptr;
+    int32_t* dev_i32 = nullptr;  // [0] token, [1] position, [2] next token
+    int32_t* dev_tokens = nullptr;  // [max_seq] ids produced by decode steps, by position
+    void* host_pinned = nullptr;
+    // prefill scratch (grown on demand)
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr;
+    float *pf_att = nullptr, *pf_proj = nullptr, *pf_gate = nullptr, *pf_up = nullptr;
+    int32_t* pf_ids = nullptr;
+    std::vector<void*> pf_bufs;
+    std::vector<void*> allocations;
+    ~Model();
+};
+
+int decode_step(Model* m, int token, int pos, float* host_logits, int* next);
+int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_logits, int* next);
+
+}  // namespace ib

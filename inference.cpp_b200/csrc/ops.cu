@@ -94,8 +94,11 @@ __global__ void embedding_f32_kernel(const float* table, const int32_t* ids, int
 
 // ---- KV write: cache [n_heads][max_seq][head_dim] (cuda_kernels.cu:163-176,403-419)
 __global__ void kv_write_kernel(float* kc, float* vc, const float* k, const float* v,
-                                int n_heads, int head_dim, int max_seq, int start, int T) {
+                                int n_heads, int head_dim, int max_seq, int start, int T,
+                                const int* start_dev) {
     const int t = blockIdx.y;
+    if (start_dev) start = *start_dev;
+    if (start + t >= max_seq) return;
     const int total = n_heads * head_dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int h = i / head_dim, d = i - h * head_dim;
@@ -107,9 +110,10 @@ __global__ void kv_write_kernel(float* kc, float* vc, const float* k, const floa
 
 // ---- RoPE from a cos/sin table: table[(pos*half + j)*2 + {0,1}] (cuda_kernels.cu:183-208)
 __global__ void rope_kernel(float* q, float* k, const float* table, int n_heads,
-                            int n_kv_heads, int head_dim, int start) {
+                            int n_kv_heads, int head_dim, int start, const int* start_dev) {
     const int b = blockIdx.x, t = blockIdx.y, j = threadIdx.x, half = head_dim / 2;
     if (j >= half) return;
+    if (start_dev) start = *start_dev;
     const int pos = start + t;
     const float c = table[((int64_t)pos * half + j) * 2];
     const float s = table[((int64_t)pos * half + j) * 2 + 1];
@@ -129,10 +133,12 @@ constexpr int ATT_MAX_GROUP = 16;
 __global__ void __launch_bounds__(128) attn_decode_partial_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ part, int n_heads, int n_kv_heads, int head_dim, int max_seq, int pos,
-    float scale, int n_chunks) {
+    float scale, int n_chunks, const int* pos_dev) {
     extern __shared__ float smem[];
+    if (pos_dev) pos = *pos_dev;
     const int G = n_heads / n_kv_heads;
     const int hk = blockIdx.x, chunk = blockIdx.y;
+    if (chunk * ATT_CH > pos || pos >= max_seq) return;  // beyond the live context
     const int s0 = chunk * ATT_CH;
     const int s1 = min(s0 + ATT_CH, pos + 1);
     const int n = s1 - s0;
@@ -199,20 +205,21 @@ __global__ void __launch_bounds__(128) attn_decode_partial_kernel(
 
 // grid n_heads, block 128: out[h, :] = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c
 __global__ void attn_decode_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                           int head_dim, int n_chunks) {
+                                           int head_dim, int n_chunks, const int* pos_dev) {
     const int h = blockIdx.x;
     const float* p = part + (int64_t)h * n_chunks * (head_dim + 2);
+    const int live = pos_dev ? (*pos_dev + ATT_CH) / ATT_CH : n_chunks;
     float M = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, p[(int64_t)c * (head_dim + 2)]);
+    for (int c = 0; c < live; ++c) M = fmaxf(M, p[(int64_t)c * (head_dim + 2)]);
     float L = 0.f;
-    for (int c = 0; c < n_chunks; ++c) {
+    for (int c = 0; c < live; ++c) {
         const float* pc = p + (int64_t)c * (head_dim + 2);
         L += expf(pc[0] - M) * pc[1];
     }
     const float inv = 1.0f / L;
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
         float acc = 0.f;
-        for (int c = 0; c < n_chunks; ++c) {
+        for (int c = 0; c < live; ++c) {
             const float* pc = p + (int64_t)c * (head_dim + 2);
             acc = fmaf(expf(pc[0] - M), pc[2 + d], acc);
         }
@@ -429,20 +436,21 @@ int workspace_get(size_t bytes, void** out) {
 
 int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st) {
-    const int n_chunks = (pos + 1 + ATT_CH - 1) / ATT_CH;
+                     cudaStream_t st, const int* pos_dev) {
+    // with pos_dev the grid covers the whole cache and chunks past *pos_dev exit
+    const int n_chunks = pos_dev ? (max_seq + ATT_CH - 1) / ATT_CH : (pos + 1 + ATT_CH - 1) / ATT_CH;
     const int G = H / Hkv;
     const size_t smem = (size_t)(G * HD + G * ATT_CH) * sizeof(float);
     attn_decode_partial_kernel<<<dim3(Hkv, n_chunks), 128, smem, st>>>(
-        q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks);
+        q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
     IB_LAUNCH_CHECK("attention_partial_kernel");
-    attn_decode_combine_kernel<<<H, 128, 0, st>>>(part, out, HD, n_chunks);
+    attn_decode_combine_kernel<<<H, 128, 0, st>>>(part, out, HD, n_chunks, pos_dev);
     IB_LAUNCH_CHECK("attention_combine_kernel");
     return IB_OK;
 }
 
 size_t attention_partial_bytes(int H, int HD, int pos) {
-    const int n_chunks = (pos + 1 + ATT_CH - 1) / ATT_CH;
+    const int n_chunks = (pos + ATT_CH) / ATT_CH;
     return (size_t)H * n_chunks * (HD + 2) * sizeof(float);
 }
 
@@ -482,8 +490,8 @@ int gemm_q_simt(int type, const void* W, const float* X, float* Y, int T, int M,
 }
 
 int rope_launch(float* q, float* k, const float* table, int H, int Hkv, int HD, int start,
-                int T, cudaStream_t st) {
-    rope_kernel<<<dim3(H + Hkv, T), HD / 2, 0, st>>>(q, k, table, H, Hkv, HD, start);
+                int T, cudaStream_t st, const int* start_dev) {
+    rope_kernel<<<dim3(H + Hkv, T), HD / 2, 0, st>>>(q, k, table, H, Hkv, HD, start, start_dev);
     IB_LAUNCH_CHECK("rope_kernel");
     return IB_OK;
 }
@@ -496,10 +504,10 @@ int rmsnorm_launch(const float* x, const float* w, float* out, int rows, int dim
 }
 
 int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hkv, int HD,
-                    int max_seq, int start, int T, cudaStream_t st) {
+                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev) {
     const int total = Hkv * HD;
     kv_write_kernel<<<dim3((total + 255) / 256, T), 256, 0, st>>>(kc, vc, k, v, Hkv, HD,
-                                                                  max_seq, start, T);
+                                                                  max_seq, start, T, start_dev);
     IB_LAUNCH_CHECK("kv_write_kernel");
     return IB_OK;
 }
@@ -598,7 +606,8 @@ extern "C" int ib_kv_write(float* kc, float* vc, const float* k, const float* v,
                            int head_dim, int max_seq, int pos, void* stream) {
     IB_REQUIRE(kc && vc && k && v && n_heads > 0 && head_dim > 0, "bad kv_write arguments");
     IB_REQUIRE(pos >= 0 && pos < max_seq, "pos outside the KV cache");
-    return kv_write_launch(kc, vc, k, v, n_heads, head_dim, max_seq, pos, 1, as_stream(stream));
+    return kv_write_launch(kc, vc, k, v, n_heads, head_dim, max_seq, pos, 1, as_stream(stream),
+                           nullptr);
 }
 extern "C" int ib_kv_write_batch(float* kc, float* vc, const float* k, const float* v,
                                  int n_heads, int head_dim, int max_seq, int start, int T,
@@ -607,7 +616,8 @@ extern "C" int ib_kv_write_batch(float* kc, float* vc, const float* k, const flo
     IB_REQUIRE(kc && vc && k && v && n_heads > 0 && head_dim > 0 && T > 0,
                "bad kv_write_batch arguments");
     IB_REQUIRE(start >= 0 && start + T <= max_seq, "positions outside the KV cache");
-    return kv_write_launch(kc, vc, k, v, n_heads, head_dim, max_seq, start, T, as_stream(stream));
+    return kv_write_launch(kc, vc, k, v, n_heads, head_dim, max_seq, start, T, as_stream(stream),
+                           nullptr);
 }
 
 extern "C" int ib_rope(float* q, float* k, const float* table, int n_heads, int n_kv_heads,
@@ -615,7 +625,7 @@ extern "C" int ib_rope(float* q, float* k, const float* table, int n_heads, int 
     IB_REQUIRE(q && k && table && n_heads > 0 && n_kv_heads >= 0 && head_dim > 1 &&
                    head_dim <= 2048 && pos >= 0,
                "bad rope arguments");
-    return rope_launch(q, k, table, n_heads, n_kv_heads, head_dim, pos, 1, as_stream(stream));
+    return rope_launch(q, k, table, n_heads, n_kv_heads, head_dim, pos, 1, as_stream(stream), nullptr);
 }
 extern "C" int ib_rope_batch(float* q, float* k, const float* table, int n_heads,
                              int n_kv_heads, int head_dim, int start, int T, void* stream) {
@@ -623,7 +633,8 @@ extern "C" int ib_rope_batch(float* q, float* k, const float* table, int n_heads
     IB_REQUIRE(q && k && table && n_heads > 0 && head_dim > 1 && head_dim <= 2048 && start >= 0 &&
                    T > 0 && T <= 65535,
                "bad rope_batch arguments");
-    return rope_launch(q, k, table, n_heads, n_kv_heads, head_dim, start, T, as_stream(stream));
+    return rope_launch(q, k, table, n_heads, n_kv_heads, head_dim, start, T, as_stream(stream),
+                       nullptr);
 }
 
 extern "C" int ib_attention(const float* q, const float* kc, const float* vc, float* out,
@@ -636,7 +647,7 @@ extern "C" int ib_attention(const float* q, const float* kc, const float* vc, fl
     st = workspace_get(attention_partial_bytes(n_heads, head_dim, pos), &part);
     if (st != IB_OK) return st;
     return attention_decode(q, kc, vc, out, n_heads, n_kv_heads, head_dim, max_seq, pos, scale,
-                            (float*)part, as_stream(stream));
+                            (float*)part, as_stream(stream), nullptr);
 }
 
 extern "C" int ib_attention_batch(const float* q, const float* kc, const float* vc, float* out,

@@ -9,18 +9,20 @@ namespace ib {
 int workspace_get(size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
 int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
+// pos_dev != nullptr: the position is read on the device (graph-capturable) and the
+// partial buffer must hold attention_partial_bytes(H, HD, max_seq - 1).
 int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st);
+                     cudaStream_t st, const int* pos_dev);
 int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
                            cudaStream_t st);
 int rope_launch(float* q, float* k, const float* table, int H, int Hkv, int HD, int start,
-                int T, cudaStream_t st);
+                int T, cudaStream_t st, const int* start_dev);
 int rmsnorm_launch(const float* x, const float* w, float* out, int rows, int dim, float eps,
                    cudaStream_t st);
 int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hkv, int HD,
-                    int max_seq, int start, int T, cudaStream_t st);
+                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev);
 int argmax_launch(const float* x, int n, int32_t* out, cudaStream_t st);
 // op: 0 silu(a), 1 a *= b, 2 a += b
 int elementwise_launch(int op, float* a, const float* b, int n, cudaStream_t st);

@@ -181,3 +181,41 @@ def write_llama_gguf(path: str, cfg: LlamaConfig, seed: int, synth_host) -> dict
         table[name] = (ttype, rows, cols, data)
     write_gguf(path, llama_metadata(cfg), tensors)
     return table
+
+
+def _read_vocab(path: str) -> int:
+    """Vocabulary size of a GGUF model (rows of token_embd.weight)."""
+    with open(path, "rb") as f:
+        head = f.read(24)
+        magic, version, n_t, n_kv = struct.unpack("<IIQQ", head)
+
+        def rd(fmt):
+            return struct.unpack(fmt, f.read(struct.calcsize(fmt)))[0]
+
+        def rstr():
+            return f.read(rd("<Q")).decode()
+
+        sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+        for _ in range(n_kv):
+            rstr()
+            t = rd("<I")
+            if t == 8:
+                rstr()
+            elif t == 9:
+                at, n = rd("<I"), rd("<Q")
+                if at == 8:
+                    for _ in range(n):
+                        rstr()
+                else:
+                    f.read(sizes[at] * n)
+            else:
+                f.read(sizes[t])
+        for _ in range(n_t):
+            name = rstr()
+            nd = rd("<I")
+            dims = [rd("<Q") for _ in range(nd)]
+            rd("<I")
+            rd("<Q")
+            if name == "token_embd.weight":
+                return int(dims[1])
+    raise ValueError("token_embd.weight not found")

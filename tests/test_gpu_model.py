@@ -1,0 +1,125 @@
+"""End-to-end parity of the native model runner (ib_model_*) with the CPU oracle.
+
+Greedy decoding must produce the identical token sequence; logits must agree
+within  max|l_gpu - l_ref| <= 1e-3 * max|l_ref|  (row-wise).  Three precisions
+mirror --gpu-precision: native (packed GGUF blocks, checked against the oracle
+with FP32 host weights, host_int16 = false), int16 (checked against the oracle
+with INT16 host weights) and fp32.
+"""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+from conftest import load_package
+
+ib = load_package()
+from inference_cpp_b200 import gguf_writer as gw  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+LOGIT_RTOL = 1e-3
+
+
+def tiny_cfgs():
+    return [
+        gw.LlamaConfig("tiny-q4_0", 2, 64, 4, 2, 128, 256, 64, 10000.0, 1e-5,
+                       embed_type=ib.Q4_0, linear_type=ib.Q4_0, attn_v_type=ib.Q5_1,
+                       ffn_down_type=ib.Q8_0, output_type=ib.Q5_0),
+        gw.LlamaConfig("tiny-k", 2, 256, 4, 1, 512, 300, 160, 500000.0, 1e-5,
+                       embed_type=ib.Q4_K, linear_type=ib.Q4_K, attn_v_type=ib.Q6_K,
+                       ffn_down_type=ib.Q6_K, output_type=ib.Q6_K, q6k_alternate=True),
+        gw.LlamaConfig("tiny-tied", 1, 64, 2, 2, 64, 128, 32, 10000.0, 1e-6,
+                       embed_type=ib.Q8_0, linear_type=ib.Q8_0, attn_v_type=ib.Q8_0,
+                       ffn_down_type=ib.Q8_0, tied_output=True),
+    ]
+
+
+def close_logits(a, b):
+    a, b = np.atleast_2d(a), np.atleast_2d(b)
+    scale = np.abs(b).max(axis=1, keepdims=True)
+    return bool(np.all(np.abs(a - b) <= LOGIT_RTOL * scale))
+
+
+def synth(cfg, seed=2024):
+    return {n: (t, r, c, d) for n, t, r, c, d in gw.synth_tensors(cfg, seed, ib.synth_host)}
+
+
+@pytest.mark.parametrize("cfg", tiny_cfgs(), ids=lambda c: c.name)
+@pytest.mark.parametrize("precision", ["native", "int16", "fp32"])
+def test_tiny_generate_matches_oracle(cuda, port, cfg, precision):
+    tensors = synth(cfg)
+    prec = ib.PRECISIONS[precision]
+    om = port.model(cfg, tensors, host_int16=(precision == "int16"))
+    m = ib.Model.from_tensors(cfg, tensors, precision=prec)
+    prompt = np.array([1, 17, 5, 99, 3, 42, 7, 11], dtype=np.int32) % cfg.vocab
+    n_new = min(40, cfg.ctx - prompt.size)
+    want, want_logits = om.generate(prompt, n_new, want_logits=True)
+    got, stats = m.generate(prompt, n_new)
+    assert list(got) == list(want)
+    assert stats.generated == n_new
+    # logits: prefill row, then every decode step
+    nxt, lg = m.prefill(prompt, 0, want_logits=True)
+    assert nxt == want[prompt.size] and close_logits(lg, want_logits[0])
+    for i in range(1, n_new):
+        nxt, lg = m.decode(int(want[prompt.size + i - 1]), prompt.size + i - 1, want_logits=True)
+        assert nxt == want[prompt.size + i], i
+        assert close_logits(lg, want_logits[i]), i
+    m.close()
+
+
+def test_graph_and_direct_launches_agree(cuda):
+    cfg = tiny_cfgs()[1]
+    tensors = synth(cfg, 5)
+    a = ib.Model.from_tensors(cfg, tensors)
+    b = ib.Model.from_tensors(cfg, tensors)
+    b.set_graph(False)
+    prompt = np.arange(1, 20, dtype=np.int32)
+    ta, _ = a.generate(prompt, 30)
+    tb, _ = b.generate(prompt, 30)
+    assert list(ta) == list(tb)
+    _, la = a.decode(int(ta[-1]), 49, want_logits=True)
+    _, lb = b.decode(int(ta[-1]), 49, want_logits=True)
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
+def test_gguf_load_path_matches_tensor_path(cuda):
+    cfg = tiny_cfgs()[1]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m.gguf")
+        tensors = gw.write_llama_gguf(path, cfg, seed=9, synth_host=ib.synth_host)
+        a = ib.Model.from_gguf(path)
+    b = ib.Model.from_tensors(cfg, tensors)
+    prompt = np.array([3, 1, 4, 1, 5, 9, 2, 6], dtype=np.int32)
+    assert list(a.generate(prompt, 25)[0]) == list(b.generate(prompt, 25)[0])
+
+
+def test_stories15m_greedy_matches_oracle(cuda, port):
+    """stories15M shape, all Q4_0: 8 prompt ids uniform in [1, 32000), 128 greedy steps."""
+    cfg = gw.STORIES15M
+    tensors = synth(cfg, 15)
+    rng = np.random.default_rng(15)
+    prompt = rng.integers(1, cfg.vocab, size=8).astype(np.int32)
+    want = port.model(cfg, tensors).generate(prompt, 128)
+    m = ib.Model.from_tensors(cfg, tensors)
+    got, _ = m.generate(prompt, 128)
+    assert list(got) == list(want)
+
+
+def test_context_limit_and_errors(cuda):
+    cfg = tiny_cfgs()[2]  # ctx 32
+    m = ib.Model.from_tensors(cfg, synth(cfg))
+    prompt = np.arange(1, 31, dtype=np.int32)
+    got, st = m.generate(prompt, 10)
+    assert len(got) == 33  # decodes up to position ctx-1, like generate_cuda
+    with pytest.raises(RuntimeError, match="empty prompt"):
+        m.generate(np.zeros(0, np.int32), 4)
+    with pytest.raises(RuntimeError, match="longer than context"):
+        m.prefill(np.arange(40, dtype=np.int32), 0)
+    with pytest.raises(RuntimeError, match="beyond the context"):
+        m.decode(1, 32)
+    m2 = ib.Model.create(cfg)
+    with pytest.raises(RuntimeError, match="tensor not set"):
+        m2.finalize()
+    with pytest.raises(RuntimeError, match="expected"):
+        m2.set_tensor("blk.0.attn_q.weight", ib.Q8_0, 10, 64, np.zeros(1000, np.uint8))
