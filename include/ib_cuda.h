@@ -64,6 +64,11 @@ int ib_available(void);                         /* 1 if a usable sm_100 device e
 int ib_device_name(char* buf, size_t len);
 int ib_memory_info(size_t* free_bytes, size_t* total_bytes);
 int ib_sync(void);                              /* device-wide synchronise */
+/* Every wait inside a pipelined kernel is bounded; an expired wait makes the
+ * kernel record a code and return early instead of hanging.  This reads and
+ * clears that record on the current device: IB_ERR_TIMEOUT (and *code != 0)
+ * means results since the previous check are invalid. */
+int ib_check_fault(int* code);
 int ib_shutdown(void);                          /* no-op: buffers stay valid to exit */
 
 /* ---- memory (replaces alloc, release, upload, download:

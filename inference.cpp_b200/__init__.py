@@ -45,6 +45,7 @@ SIGNATURES = {
     "ib_device_name": [_c.c_char_p, _sz],
     "ib_memory_info": [_vp, _vp],
     "ib_sync": [],
+    "ib_check_fault": [_vp],
     "ib_shutdown": [],
     "ib_alloc": [_vp, _sz],
     "ib_free": [_vp],
@@ -154,6 +155,13 @@ def memory_info() -> tuple[int, int]:
 
 def sync() -> None:
     call("ib_sync")
+
+
+def check_fault() -> int:
+    """Raises if a bounded pipeline wait expired since the last check."""
+    code = ctypes.c_int()
+    call("ib_check_fault", ctypes.byref(code))
+    return code.value
 
 
 def dequantize(type_: int, W, rows: int, cols: int, out=None, stream=None):

@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemv_mma.cuh"
 
 namespace ib {
 
@@ -129,5 +130,17 @@ extern "C" int ib_memset(void* dev, int value, size_t bytes, void* stream) {
     if (bytes == 0) return IB_OK;
     IB_REQUIRE(dev, "null pointer argument");
     IB_CUDA_CHECK(cudaMemsetAsync(dev, value, bytes, as_stream(stream)));
+    return IB_OK;
+}
+
+extern "C" int ib_check_fault(int* code) {
+    IB_REQUIRE(code, "null pointer argument");
+    int st = gemv_fault_take(code);
+    if (st != IB_OK) return st;
+    if (*code) {
+        set_error("CUDA: a pipeline wait expired in a GEMV kernel (code " + std::to_string(*code) +
+                  "); results of the calls since the last check are invalid");
+        return IB_ERR_TIMEOUT;
+    }
     return IB_OK;
 }

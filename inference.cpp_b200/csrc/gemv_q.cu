@@ -14,6 +14,8 @@
 // Integer -> float conversion of small unsigned fields uses the exponent trick
 // f = as_float(0x4B000000 | u) - 2^23, exact for u < 2^23.
 #include "common.cuh"
+#include "gemv_mma.cuh"
+#include "ops.cuh"
 #include "quant.cuh"
 
 namespace ib {
@@ -330,6 +332,16 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     IB_REQUIRE(cols % be == 0, "cols must be a multiple of the block size");
     cudaStream_t st = as_stream(stream);
     const uint8_t* W = (const uint8_t*)dev_W;
+    if (gemv_mma_supported(type) && ((uintptr_t)W % gemv_mma_align(type)) == 0 &&
+        cols <= (1 << 30) && rows < (1ll << 31)) {
+        void* ws = nullptr;
+        int r = workspace_get(WS_GEMV, xlimbs_bytes((int)cols), &ws);
+        if (r != IB_OK) return r;
+        XLimbs xb;
+        xlimbs_carve(ws, (int)cols, xb);
+        if ((r = xq_launch(dev_x, (int)cols, gemv_mma_group(type), xb, st)) != IB_OK) return r;
+        return gemv_mma_launch(type, W, xb, dev_y, rows, cols, st);
+    }
     switch (type) {
         case IB_TYPE_Q4_K:
             IB_REQUIRE(((uintptr_t)W & 15) == 0, "Q4_K weights must be 16-byte aligned");

@@ -48,12 +48,33 @@ __device__ float block_max(float v, float* sh) {
 }
 
 // ---- RMSNorm: out = x / sqrt(mean(x^2) + eps) * w (model.cpp:54-57) -------------
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                               float* __restrict__ out, int dim, float eps) {
+// One CTA per row; float4 path when dim % 4 == 0 and the row is 16-byte aligned
+// (every thread's loads are issued before the reduction).
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ w,
+                                                       float* __restrict__ out, int dim,
+                                                       float eps) {
     __shared__ float sh[32];
     const float* xr = x + (int64_t)blockIdx.x * dim;
     float* o = out + (int64_t)blockIdx.x * dim;
+    const bool vec = (dim & 3) == 0 && ((((uintptr_t)xr) | ((uintptr_t)o) | ((uintptr_t)w)) & 15) == 0;
     float ss = 0.f;
+    if (vec) {
+        const int n4 = dim >> 2;
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4*>(xr)[i];
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
+        ss = block_sum(ss, sh);
+        const float rms = sqrtf(ss / (float)dim + eps);
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4*>(xr)[i];
+            const float4 g = reinterpret_cast<const float4*>(w)[i];
+            reinterpret_cast<float4*>(o)[i] =
+                make_float4(v.x / rms * g.x, v.y / rms * g.y, v.z / rms * g.z, v.w / rms * g.w);
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
     ss = block_sum(ss, sh);
     const float rms = sqrtf(ss / (float)dim + eps);
@@ -124,109 +145,6 @@ __global__ void rope_kernel(float* q, float* k, const float* table, int n_heads,
     vec[2 * j + 1] = x0 * s + x1 * c;
 }
 
-// ---- attention, one query position, split-K over the KV cache ------------------
-// grid (n_kv_heads, n_chunks); block 128.  Chunk c covers positions
-// [c*CH, min((c+1)*CH, pos+1)).  Partials: m, l, acc[HD] per (query head, chunk).
-constexpr int ATT_CH = 128;
-constexpr int ATT_MAX_GROUP = 16;
-
-__global__ void __launch_bounds__(128) attn_decode_partial_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-    float* __restrict__ part, int n_heads, int n_kv_heads, int head_dim, int max_seq, int pos,
-    float scale, int n_chunks, const int* pos_dev) {
-    extern __shared__ float smem[];
-    if (pos_dev) pos = *pos_dev;
-    const int G = n_heads / n_kv_heads;
-    const int hk = blockIdx.x, chunk = blockIdx.y;
-    if (chunk * ATT_CH > pos || pos >= max_seq) return;  // beyond the live context
-    const int s0 = chunk * ATT_CH;
-    const int s1 = min(s0 + ATT_CH, pos + 1);
-    const int n = s1 - s0;
-    float* qs = smem;                    // [G][HD]
-    float* sc = smem + G * head_dim;     // [G][ATT_CH]
-    __shared__ float red[32];
-    for (int i = threadIdx.x; i < G * head_dim; i += blockDim.x)
-        qs[i] = q[(int64_t)(hk * G) * head_dim + i];
-    __syncthreads();
-    const float* kh = kc + (int64_t)hk * max_seq * head_dim;
-    const float* vh = vc + (int64_t)hk * max_seq * head_dim;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // scores: each warp takes positions, lanes split head_dim
-    for (int s = warp; s < n; s += 4) {
-        const float* kr = kh + (int64_t)(s0 + s) * head_dim;
-        float dots[ATT_MAX_GROUP];
-#pragma unroll
-        for (int g = 0; g < ATT_MAX_GROUP; ++g) dots[g] = 0.f;
-        for (int d = lane; d < head_dim; d += 32) {
-            const float kv = kr[d];
-#pragma unroll
-            for (int g = 0; g < ATT_MAX_GROUP; ++g)
-                if (g < G) dots[g] = fmaf(qs[g * head_dim + d], kv, dots[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < ATT_MAX_GROUP; ++g)
-            if (g < G) {
-                const float v = warp_sum_f(dots[g]);
-                if (lane == 0) sc[g * ATT_CH + s] = v * scale;
-            }
-    }
-    __syncthreads();
-    // per head: chunk max and exp-sum
-    for (int g = 0; g < G; ++g) {
-        float m = -INFINITY;
-        for (int s = threadIdx.x; s < n; s += blockDim.x) m = fmaxf(m, sc[g * ATT_CH + s]);
-        m = block_max(m, red);
-        float l = 0.f;
-        for (int s = threadIdx.x; s < n; s += blockDim.x) {
-            const float e = expf(sc[g * ATT_CH + s] - m);
-            sc[g * ATT_CH + s] = e;
-            l += e;
-        }
-        l = block_sum(l, red);
-        float* pp = part + ((int64_t)(hk * G + g) * n_chunks + chunk) * (head_dim + 2);
-        if (threadIdx.x == 0) { pp[0] = m; pp[1] = l; }
-    }
-    __syncthreads();
-    // weighted V: thread per d (loop if head_dim > blockDim)
-    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-        float acc[ATT_MAX_GROUP];
-#pragma unroll
-        for (int g = 0; g < ATT_MAX_GROUP; ++g) acc[g] = 0.f;
-        for (int s = 0; s < n; ++s) {
-            const float vv = vh[(int64_t)(s0 + s) * head_dim + d];
-#pragma unroll
-            for (int g = 0; g < ATT_MAX_GROUP; ++g)
-                if (g < G) acc[g] = fmaf(sc[g * ATT_CH + s], vv, acc[g]);
-        }
-        for (int g = 0; g < G; ++g)
-            part[((int64_t)(hk * G + g) * n_chunks + chunk) * (head_dim + 2) + 2 + d] = acc[g];
-    }
-}
-
-// grid n_heads, block 128: out[h, :] = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c
-__global__ void attn_decode_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                           int head_dim, int n_chunks, const int* pos_dev) {
-    const int h = blockIdx.x;
-    const float* p = part + (int64_t)h * n_chunks * (head_dim + 2);
-    const int live = pos_dev ? (*pos_dev + ATT_CH) / ATT_CH : n_chunks;
-    float M = -INFINITY;
-    for (int c = 0; c < live; ++c) M = fmaxf(M, p[(int64_t)c * (head_dim + 2)]);
-    float L = 0.f;
-    for (int c = 0; c < live; ++c) {
-        const float* pc = p + (int64_t)c * (head_dim + 2);
-        L += expf(pc[0] - M) * pc[1];
-    }
-    const float inv = 1.0f / L;
-    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-        float acc = 0.f;
-        for (int c = 0; c < live; ++c) {
-            const float* pc = p + (int64_t)c * (head_dim + 2);
-            acc = fmaf(expf(pc[0] - M), pc[2 + d], acc);
-        }
-        out[(int64_t)h * head_dim + d] = acc * inv;
-    }
-}
-
 // ---- attention for a batch of query positions (prefill), causal ----------------
 // q, out: [T][H][HD]; grid (H, T); dynamic shared (start+T) floats of scores.
 __global__ void __launch_bounds__(128) attn_batch_kernel(const float* __restrict__ q,
@@ -279,7 +197,29 @@ __global__ void argmax_kernel(const float* __restrict__ x, int n, int32_t* __res
     __shared__ int si[32];
     float bv = -INFINITY;
     int bi = 0x7FFFFFFF;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    // four independent float4 loads per thread and step (first maximum kept per lane)
+    const bool vec = ((uintptr_t)x & 15) == 0;
+    int i0 = 0;
+    if (vec) {
+        const int n4 = n >> 2, step = blockDim.x * 4;
+        for (int b = threadIdx.x; b < n4; b += step) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                v[u] = b + u * blockDim.x < n4 ? reinterpret_cast<const float4*>(x)[b + u * blockDim.x]
+                                              : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int base = 4 * (b + u * blockDim.x);
+                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (e[k] > bv || (e[k] == bv && base + k < bi)) { bv = e[k]; bi = base + k; }
+            }
+        }
+        i0 = n4 * 4;
+    }
+    for (int i = i0 + threadIdx.x; i < n; i += blockDim.x) {
         const float v = x[i];
         if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
     }
@@ -403,64 +343,37 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const void* __restrict__
     }
 }
 
-// Workspace for the split-K attention partials, grown on demand per device.
+// Scratch for the C-ABI operators (split-K attention partials, GEMV activation
+// limbs), one buffer per (slot, device), grown on demand.  Calls that share a
+// slot must be ordered on one stream (each operator uses its own slot).
 struct Workspace {
     std::mutex mu;
     std::vector<void*> ptr;
     std::vector<size_t> bytes;
 };
-static Workspace g_ws;
+static Workspace g_ws[WS_SLOTS];
 
-int workspace_get(size_t bytes, void** out) {
+int workspace_get(int slot, size_t bytes, void** out) {
     int dev = 0;
     IB_CUDA_CHECK(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> lock(g_ws.mu);
-    if ((int)g_ws.ptr.size() <= dev) {
-        g_ws.ptr.resize(dev + 1, nullptr);
-        g_ws.bytes.resize(dev + 1, 0);
+    Workspace& ws = g_ws[slot];
+    std::lock_guard<std::mutex> lock(ws.mu);
+    if ((int)ws.ptr.size() <= dev) {
+        ws.ptr.resize(dev + 1, nullptr);
+        ws.bytes.resize(dev + 1, 0);
     }
-    if (g_ws.bytes[dev] < bytes) {
-        if (g_ws.ptr[dev]) {
+    if (ws.bytes[dev] < bytes) {
+        if (ws.ptr[dev]) {
             IB_CUDA_CHECK(cudaDeviceSynchronize());
-            IB_CUDA_CHECK(cudaFree(g_ws.ptr[dev]));
-            g_ws.ptr[dev] = nullptr;
-            g_ws.bytes[dev] = 0;
+            IB_CUDA_CHECK(cudaFree(ws.ptr[dev]));
+            ws.ptr[dev] = nullptr;
+            ws.bytes[dev] = 0;
         }
         size_t b = bytes < (1u << 20) ? (1u << 20) : bytes;
-        IB_CUDA_CHECK(cudaMalloc(&g_ws.ptr[dev], b));
-        g_ws.bytes[dev] = b;
+        IB_CUDA_CHECK(cudaMalloc(&ws.ptr[dev], b));
+        ws.bytes[dev] = b;
     }
-    *out = g_ws.ptr[dev];
-    return IB_OK;
-}
-
-int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
-                     int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st, const int* pos_dev) {
-    // with pos_dev the grid covers the whole cache and chunks past *pos_dev exit
-    const int n_chunks = pos_dev ? (max_seq + ATT_CH - 1) / ATT_CH : (pos + 1 + ATT_CH - 1) / ATT_CH;
-    const int G = H / Hkv;
-    const size_t smem = (size_t)(G * HD + G * ATT_CH) * sizeof(float);
-    attn_decode_partial_kernel<<<dim3(Hkv, n_chunks), 128, smem, st>>>(
-        q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
-    IB_LAUNCH_CHECK("attention_partial_kernel");
-    attn_decode_combine_kernel<<<H, 128, 0, st>>>(part, out, HD, n_chunks, pos_dev);
-    IB_LAUNCH_CHECK("attention_combine_kernel");
-    return IB_OK;
-}
-
-size_t attention_partial_bytes(int H, int HD, int pos) {
-    const int n_chunks = (pos + ATT_CH) / ATT_CH;
-    return (size_t)H * n_chunks * (HD + 2) * sizeof(float);
-}
-
-int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos) {
-    IB_REQUIRE(H > 0 && Hkv > 0 && H % Hkv == 0, "n_heads must be a multiple of n_kv_heads");
-    IB_REQUIRE(H / Hkv <= ATT_MAX_GROUP, "GQA group larger than 16 is not supported");
-    IB_REQUIRE(HD > 0 && HD <= 256, "head_dim must be in (0, 256]");
-    IB_REQUIRE(pos >= 0 && pos < max_seq, "pos outside the KV cache");
-    const size_t smem = (size_t)((H / Hkv) * HD + (H / Hkv) * ATT_CH) * sizeof(float);
-    IB_REQUIRE(smem <= 48 * 1024, "attention group too large for shared memory");
+    *out = ws.ptr[dev];
     return IB_OK;
 }
 
@@ -498,7 +411,7 @@ int rope_launch(float* q, float* k, const float* table, int H, int Hkv, int HD, 
 
 int rmsnorm_launch(const float* x, const float* w, float* out, int rows, int dim, float eps,
                    cudaStream_t st) {
-    rmsnorm_kernel<<<rows, 256, 0, st>>>(x, w, out, dim, eps);
+    rmsnorm_kernel<<<rows, dim >= 2048 ? 1024 : 256, 0, st>>>(x, w, out, dim, eps);
     IB_LAUNCH_CHECK("rmsnorm_kernel");
     return IB_OK;
 }
@@ -644,7 +557,7 @@ extern "C" int ib_attention(const float* q, const float* kc, const float* vc, fl
     int st = check_attention_args(n_heads, n_kv_heads, head_dim, max_seq, pos);
     if (st != IB_OK) return st;
     void* part = nullptr;
-    st = workspace_get(attention_partial_bytes(n_heads, head_dim, pos), &part);
+    st = workspace_get(WS_ATTENTION, attention_partial_bytes(n_heads, head_dim, pos), &part);
     if (st != IB_OK) return st;
     return attention_decode(q, kc, vc, out, n_heads, n_kv_heads, head_dim, max_seq, pos, scale,
                             (float*)part, as_stream(stream), nullptr);

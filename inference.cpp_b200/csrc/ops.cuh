@@ -6,7 +6,8 @@
 
 namespace ib {
 
-int workspace_get(size_t bytes, void** out);
+enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_SLOTS = 2 };
+int workspace_get(int slot, size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
 int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
 // pos_dev != nullptr: the position is read on the device (graph-capturable) and the
