@@ -55,6 +55,7 @@ SIGNATURES = {
     "ib_dequant_f32": [_i, _vp, _vp, _i64, _i64, _vp],
     "ib_dequant_i16": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_gemv_q": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
+    "ib_gemv_q_noalloc": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_gemm_q": [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ib_embedding_q": [_i, _vp, _vp, _vp, _i, _i64, _i64, _vp],
     "ib_gemv": [_vp, _vp, _vp, _i, _i, _vp],
@@ -185,6 +186,16 @@ def gemv_q(type_: int, W, x, rows: int, cols: int, y=None, stream=None):
     if y is None:
         y = torch.empty(rows, dtype=torch.float32, device=x.device)
     call("ib_gemv_q", type_, _ptr(W), _ptr(x), _ptr(y), rows, cols, _stream(stream))
+    return y
+
+
+NOALLOC_MAX_COLS = 32768
+
+
+def gemv_q_noalloc(type_: int, W, x, y, rows: int, cols: int, stream=None):
+    """ib_gemv_q with its scratch in a static device array: y must be given (the
+    call allocates nothing); cols <= NOALLOC_MAX_COLS."""
+    call("ib_gemv_q_noalloc", type_, _ptr(W), _ptr(x), _ptr(y), rows, cols, _stream(stream))
     return y
 
 
