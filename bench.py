@@ -237,6 +237,11 @@ def main():
     ap.add_argument("--workload", default="llama-3-8b")
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nvtx-step", action="store_true",
+                    help="after the measurement, run one ungraphed decode step in an NVTX "
+                         "range named decode_step (for profiler launch lists)")
+    ap.add_argument("--decode-path", default="fused", choices=["fused", "separate"],
+                    help="fused decode kernels (default) or the separate per-op kernels")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -260,6 +265,7 @@ def main():
     torch.cuda.set_device(local)
     ib.init(local)
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local)
+    m.set_fused(args.decode_path == "fused")
     rng = np.random.default_rng(42)
     prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
 
@@ -333,6 +339,7 @@ def main():
                        "prompt": args.prompt, "global_batch": world, "seq_len": pos,
                        "parallelism": f"replica{world}" if world > 1 else "single",
                        "weights": "Q4_K linears, Q6_K attn_v/ffn_down/output (synthetic)",
+                       "decode_path": "fused" if m.uses_fused() else "separate",
                        "l2": "inputs larger than L2 (weights per step >> 126 MB)"},
             "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
@@ -351,6 +358,15 @@ def main():
             "gpu_launches": kernels_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
+    if args.nvtx_step:
+        # one ungraphed decode step in an NVTX range, for a profiler's launch list
+        m.set_graph(False)
+        m.decode(nxt, pos + e2e_steps)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        m.decode(nxt, pos + e2e_steps + 1)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     m.close()
     if world > 1:
         import torch.distributed as dist

@@ -218,6 +218,13 @@ int ib_model_generate(void* model, const int32_t* prompt, int n_prompt, int max_
 int ib_model_decode_loop(void* model, int32_t token, int pos, int n_steps, int32_t* host_tokens);
 /* Capture the decode step in a CUDA graph (default on) or launch it directly. */
 int ib_model_set_graph(void* model, int enabled);
+/* Fused decode kernels (default on): per layer one QKV GEMV with RMSNorm, RoPE and
+ * the KV write, attention, one wo GEMV with the residual add, one gate+up GEMV with
+ * SwiGLU and one down GEMV with the residual add, chained by programmatic dependent
+ * launch.  Used only when every weight's format and shape has a fused kernel. */
+int ib_model_set_fused(void* model, int enabled);
+/* *fused = 1 when decode steps run on the fused kernels. */
+int ib_model_uses_fused(void* model, int* fused);
 /* The stream the model launches on (a cudaStream_t), e.g. for event timing. */
 int ib_model_stream(void* model, void** stream);
 /* Number of kernels one decode step launches. */

@@ -363,6 +363,8 @@ SIGNATURES.update({
     "ib_model_decode": [_vp, _c.c_int32, _i, _vp, _vp],
     "ib_model_generate": [_vp, _vp, _i, _i, _c.c_int32, _vp, _vp, _vp],
     "ib_model_set_graph": [_vp, _i],
+    "ib_model_set_fused": [_vp, _i],
+    "ib_model_uses_fused": [_vp, _vp],
     "ib_model_weight_bytes": [_vp, _vp],
     "ib_model_decode_loop": [_vp, _c.c_int32, _i, _i, _vp],
     "ib_model_stream": [_vp, _vp],
@@ -415,6 +417,14 @@ class Model:
 
     def set_graph(self, enabled: bool):
         call("ib_model_set_graph", self.h, 1 if enabled else 0)
+
+    def set_fused(self, enabled: bool):
+        call("ib_model_set_fused", self.h, 1 if enabled else 0)
+
+    def uses_fused(self) -> bool:
+        f = ctypes.c_int()
+        call("ib_model_uses_fused", self.h, ctypes.byref(f))
+        return bool(f.value)
 
     def weight_bytes(self) -> int:
         n = ctypes.c_size_t()

@@ -14,6 +14,7 @@
 // so a decode step can be captured once in a CUDA graph.
 #include "common.cuh"
 #include "ops.cuh"
+#include "pdl.cuh"
 
 namespace ib {
 
@@ -38,6 +39,8 @@ __global__ void __launch_bounds__(128) attn_partial_fast_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ part, int n_heads, int n_kv_heads, int head_dim, int max_seq, int pos,
     float scale, int n_chunks, const int* __restrict__ pos_dev) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int CH = ATT_CH_FAST, PW = CH / 4;  // 4 warps x 16 positions
     __shared__ float4 qs[GMAX][32];
     __shared__ float sc[GMAX][CH];
@@ -167,6 +170,8 @@ __global__ void __launch_bounds__(128) attn_partial_generic_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ part, int n_heads, int n_kv_heads, int head_dim, int max_seq, int pos,
     float scale, int n_chunks, const int* __restrict__ pos_dev) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int CH = ATT_CH_GENERIC;
     extern __shared__ float smem[];
     __shared__ float red[32];
@@ -247,6 +252,8 @@ __global__ void __launch_bounds__(128) attn_partial_generic_kernel(
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
                                     int head_dim, int n_chunks, int ch, int n_live,
                                     const int* __restrict__ pos_dev) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x;
     const float* p = part + (size_t)h * n_chunks * (head_dim + 2);
     const int live = pos_dev ? *pos_dev / ch + 1 : n_live;
@@ -274,7 +281,7 @@ static bool fast_ok(int H, int Hkv, int HD) {
 
 int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st, const int* pos_dev) {
+                     cudaStream_t st, const int* pos_dev, bool pdl) {
     const int G = H / Hkv;
     const bool fast = fast_ok(H, Hkv, HD) && ((uintptr_t)q % 16 == 0) &&
                       ((uintptr_t)kc % 16 == 0) && ((uintptr_t)vc % 16 == 0);
@@ -283,17 +290,18 @@ int attention_decode(const float* q, const float* kc, const float* vc, float* ou
     const int n_chunks = pos_dev ? (max_seq + ch - 1) / ch : pos / ch + 1;
     const dim3 grid(Hkv, n_chunks);
     if (fast) {
-        if (G <= 1) attn_partial_fast_kernel<1><<<grid, 128, 0, st>>>(q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
-        else if (G <= 2) attn_partial_fast_kernel<2><<<grid, 128, 0, st>>>(q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
-        else if (G <= 4) attn_partial_fast_kernel<4><<<grid, 128, 0, st>>>(q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
-        else attn_partial_fast_kernel<8><<<grid, 128, 0, st>>>(q, kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev);
+        auto kern = G <= 1 ? attn_partial_fast_kernel<1> : G <= 2 ? attn_partial_fast_kernel<2> :
+                    G <= 4 ? attn_partial_fast_kernel<4> : attn_partial_fast_kernel<8>;
+        IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(128), 0, st, pdl, q, kc, vc, part, H, Hkv, HD,
+                                 max_seq, pos, scale, n_chunks, pos_dev));
     } else {
         const size_t smem = (size_t)(G * HD + G * ATT_CH_GENERIC) * sizeof(float);
-        attn_partial_generic_kernel<<<grid, 128, smem, st>>>(q, kc, vc, part, H, Hkv, HD, max_seq,
-                                                             pos, scale, n_chunks, pos_dev);
+        IB_CUDA_CHECK(launch_pdl(attn_partial_generic_kernel, grid, dim3(128), smem, st, pdl, q,
+                                 kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev));
     }
     IB_LAUNCH_CHECK("attention_partial_kernel");
-    attn_combine_kernel<<<H, 128, 0, st>>>(part, out, HD, n_chunks, ch, pos / ch + 1, pos_dev);
+    IB_CUDA_CHECK(launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, pdl, part, out, HD,
+                             n_chunks, ch, pos / ch + 1, pos_dev));
     IB_LAUNCH_CHECK("attention_combine_kernel");
     return IB_OK;
 }

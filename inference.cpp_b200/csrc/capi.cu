@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "gemv_mma.cuh"
 
 namespace ib {
@@ -135,8 +136,11 @@ extern "C" int ib_memset(void* dev, int value, size_t bytes, void* stream) {
 
 extern "C" int ib_check_fault(int* code) {
     IB_REQUIRE(code, "null pointer argument");
+    int c2 = 0;
     int st = gemv_fault_take(code);
     if (st != IB_OK) return st;
+    if ((st = decode_fault_take(&c2)) != IB_OK) return st;
+    if (!*code) *code = c2;
     if (*code) {
         set_error("CUDA: a pipeline wait expired in a GEMV kernel (code " + std::to_string(*code) +
                   "); results of the calls since the last check are invalid");

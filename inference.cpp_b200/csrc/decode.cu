@@ -1,0 +1,614 @@
+// Fused decode GEMV on GGUF blocks for the native Llama runner (sm_100a).
+//
+// Two kernels replace the chain  RMSNorm -> GEMV(s) -> elementwise  of the reference's
+// forward_token (src/models/model_cuda.cpp:372-407):
+//   xq_slab   splits the FP32 input (for a normed input: x * w, with per-group sums of
+//             x^2 kept for the RMSNorm) once into exact int8 limbs, written as a slab of
+//             per-stage slices (layout in decode.cuh);
+//   GEMV      a producer warp streams, per pipeline stage, the packed bytes of 16 weight
+//             rows plus the matching limb slice with 1-D TMA bulk copies (no multicast)
+//             into a shared-memory ring; eight consumer warps run the int8-MMA block
+//             math of gemv_math.cuh on it; the epilogue applies the RMSNorm divisor
+//             sqrt(mean(x^2) + eps) (src/ops/cuda_kernels.cu:101-130) and one of
+//             STORE, RESID (residual add), QKV (RoPE on q/k with the reference's table,
+//             q to a buffer, k/v into the cache at the device position), SWIGLU
+//             (silu(gate) * up, gate and up rows paired in one tile) or ARGMAX (logits
+//             + a 64-bit atomic max of (ordered logit, ~row): the first maximum, as the
+//             argmax kernel's tie rule).
+// Weights are constant, so the producer issues the first ring fill before
+// griddepcontrol.wait: under programmatic dependent launch the weight stream of a
+// GEMV overlaps the tail of the previous kernel.
+#include <math.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "gemv_math.cuh"
+#include "pdl.cuh"
+#include "pipeline.cuh"
+
+namespace ib {
+
+static __device__ int g_decode_fault;
+
+constexpr int kNWC = 8;        // consumer warps
+constexpr int kMaxStages = 8;  // ring stages
+
+template <int TA, int TB>
+struct Pair {
+    using FA = Fmt<TA>;
+    using FB = Fmt<TB>;
+    static_assert(FA::K == FB::K && FA::KB == FB::KB && FA::UNIT == FB::UNIT,
+                  "the two formats of a fused kernel share block geometry");
+    static constexpr bool KQ = FA::K;
+    static constexpr int BE = KQ ? 256 : 32;  // elements per block
+    static constexpr int KB = FA::KB;         // blocks per stage per row
+    static constexpr int UNIT = FA::UNIT;
+    static constexpr int SE = KB * BE;        // elements per stage = slab slice
+    static constexpr int GS = KQ ? 256 : 32;  // elements per limb scale
+    static constexpr int SLICE = ((SE * 4 + (SE / GS + SE / 32 + SE / 16) * 4) + 15) / 16 * 16;
+};
+
+bool slab_kquant(int type) { return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K; }
+
+// ---- limb slab ----------------------------------------------------------------------
+__device__ __forceinline__ float exp2i(int e) {  // 2^e for e in [-126, 127]
+    return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+// Smallest e >= -126 with m <= 127 * 2^e, from the exponent bits (m >= 0).
+__device__ __forceinline__ int limb_exp_bits(float m) {
+    if (!(m > 0.f)) return 0;
+    int e = (int)((__float_as_uint(m) >> 23) & 0xFFu) - 133;  // floor(log2 m) - 6
+    if (e < -126) e = -126;
+    if (m > 127.0f * exp2i(e)) ++e;
+    return e;
+}
+
+// One warp per scale group of GS elements.
+template <int GS, int SE, int SLICE>
+__global__ void __launch_bounds__(256) xq_slab_kernel(const float* __restrict__ x,
+                                                      const float* __restrict__ norm, int K,
+                                                      uint8_t* __restrict__ slab,
+                                                      float* __restrict__ ssq) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int gi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (gi * GS >= K) return;
+    constexpr int PER = GS / 32;
+    float v[PER];
+    float m = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = (gi * PER + j) * 32 + lane;
+        float t = x[i];
+        ss = fmaf(t, t, ss);
+        if (norm) t *= norm[i];
+        v[j] = t;
+        m = fmaxf(m, fabsf(t));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if (ssq && lane == 0) ssq[gi] = ss;
+    const int e = limb_exp_bits(m);
+    const float inv_s = exp2i(-e);
+    const int slice = (gi * GS) / SE, gl = (gi * GS - slice * SE) / GS;
+    uint8_t* base = slab + (size_t)slice * SLICE;
+    int8_t* limbs = reinterpret_cast<int8_t*>(base);
+    float* scale = reinterpret_cast<float*>(base + SE * 4);
+    float* sum32 = scale + SE / GS;
+    float* sum16 = sum32 + SE / 32;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int sg = gl * PER + j;  // 32-group within the slice
+        float tt = v[j] * inv_s;      // exact: |tt| <= 127
+        int8_t* o = limbs + (size_t)sg * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float r = rintf(tt);
+            o[i * 32 + lane] = (int8_t)(int)r;
+            tt = (tt - r) * 128.0f;
+        }
+        float sm = v[j];
+#pragma unroll
+        for (int o2 = 8; o2 > 0; o2 >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o2);
+        if ((lane & 15) == 0) sum16[sg * 2 + (lane >> 4)] = sm;
+        sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+        if (lane == 0) sum32[sg] = sm;
+    }
+    if (lane == 0) scale[gl] = exp2i(e);
+}
+
+int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_t* slab,
+                   float* ssq, cudaStream_t st, bool pdl) {
+    IB_REQUIRE(x && slab && K > 0, "xq_slab: bad arguments");
+    const int GS = kquant ? 256 : 32;
+    IB_REQUIRE(K % GS == 0, "xq_slab: K must be a multiple of the limb group");
+    const int groups = K / GS, grid = (groups + 7) / 8;
+    if (kquant) {
+        using P = Pair<IB_TYPE_Q4_K, IB_TYPE_Q6_K>;
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<P::GS, P::SE, P::SLICE>, dim3(grid), dim3(256), 0,
+                                 st, pdl, x, norm, K, slab, ssq));
+    } else {
+        using P = Pair<IB_TYPE_Q4_0, IB_TYPE_Q8_0>;
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<P::GS, P::SE, P::SLICE>, dim3(grid), dim3(256), 0,
+                                 st, pdl, x, norm, K, slab, ssq));
+    }
+    return IB_OK;
+}
+
+// ---- row geometry --------------------------------------------------------------------
+__device__ __forceinline__ int total_rows(const FusedGemv& p) {
+    return p.paired ? 2 * p.rows[0] : p.rows[0] + p.rows[1] + p.rows[2];
+}
+
+// Rows of row group rg that exist (16 except in the last group of a ragged last
+// segment).
+__device__ __forceinline__ int group_rows(const FusedGemv& p, int rg) {
+    if (p.paired) return 16;
+    const int left = total_rows(p) - rg * 16;
+    return left < 16 ? left : 16;
+}
+
+// Tile row i (0..15) of row group rg -> (segment, row within the segment); rows past
+// the end map to the last row.
+__device__ __forceinline__ void tile_row(const FusedGemv& p, int rg, int i, int& seg, int& lr) {
+    if (p.paired) {
+        seg = i >> 3;
+        lr = rg * 8 + (i & 7);
+        return;
+    }
+    int R = rg * 16 + i;
+    const int tot = total_rows(p);
+    if (R >= tot) R = tot - 1;
+    if (R < p.rows[0]) {
+        seg = 0;
+        lr = R;
+    } else if (R < p.rows[0] + p.rows[1]) {
+        seg = 1;
+        lr = R - p.rows[0];
+    } else {
+        seg = 2;
+        lr = R - p.rows[0] - p.rows[1];
+    }
+}
+
+template <int TA, int TB>
+__device__ __forceinline__ bool group_is_b(const FusedGemv& p, int rg) {
+    if (TA == TB) return false;
+    int seg, lr;
+    tile_row(p, rg, 0, seg, lr);
+    return p.type[seg] == TB;
+}
+
+// RMSNorm divisor sqrt(sum(x^2) / K + eps) from the per-group sums (warp-wide).
+template <int GS>
+__device__ __forceinline__ float rms_of(const FusedGemv& p, int lane) {
+    float t = 0.f;
+    for (int i = lane; i < p.K / GS; i += 32) t += p.ssq[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return sqrtf(t / (float)p.K + p.eps);
+}
+
+// ---- epilogue ------------------------------------------------------------------------
+// Row-group epilogue on warp 0: lanes 0..15 hold the finished rows (v).
+template <int EPI>
+__device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, float v) {
+    const unsigned FULL = 0xffffffffu;
+    int seg = 0, lr = 0;
+    tile_row(p, rg, lane & 15, seg, lr);
+    const bool live = lane < group_rows(p, rg);
+    if (EPI == EPI_STORE || EPI == EPI_RESID) {
+        const int R = rg * 16 + lane;
+        if (live) {
+            if (EPI == EPI_STORE) p.y[R] = v;
+            else p.y[R] += v;
+        }
+    } else if (EPI == EPI_QKV) {
+        const int HD = p.head_dim;
+        const int d = lr % HD;
+        const int ps = *p.pos;
+        const float other = __shfl_xor_sync(FULL, v, 1);
+        float out = v;
+        if (seg < 2) {  // RoPE, rope_kernel's formula on the pair (2j, 2j+1)
+            const int j = d >> 1;
+            const float c = p.rope[((size_t)ps * (HD / 2) + j) * 2];
+            const float s = p.rope[((size_t)ps * (HD / 2) + j) * 2 + 1];
+            out = (d & 1) == 0 ? v * c - other * s : other * s + v * c;
+        }
+        if (live) {
+            if (seg == 0) {
+                p.q[lr] = out;
+            } else {
+                const size_t at = ((size_t)(lr / HD) * p.max_seq + ps) * HD + d;
+                if (seg == 1) p.kc[at] = out;
+                else p.vc[at] = out;
+            }
+        }
+    } else if (EPI == EPI_SWIGLU) {
+        const float u = __shfl_down_sync(FULL, v, 8);
+        if (lane < 8) p.y[rg * 8 + lane] = v * (1.0f / (1.0f + expf(-v))) * u;
+    } else if (EPI == EPI_ARGMAX) {
+        const int R = rg * 16 + lane;
+        unsigned long long key = 0ull;
+        if (live) {
+            p.y[R] = v;
+            if (!(v != v)) {  // NaN never wins (the argmax kernel compares with >)
+                const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+                const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+                key = ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)R);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(FULL, key, o);
+            key = k2 > key ? k2 : key;
+        }
+        if (lane == 0 && key) atomicMax(p.best, key);
+    }
+}
+
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kNWC * 32) : "memory");
+}
+
+// Sums the consumer warps' partials of the row group, applies the RMSNorm divisor
+// and runs the epilogue.
+template <int EPI>
+__device__ __forceinline__ void finish_group(const FusedGemv& p, float (*r)[16], int rg,
+                                             int warp, int lane, const LaneCtx& c, float rms,
+                                             float& acc_a, float& acc_b) {
+    acc_a = quad_sum(acc_a);
+    acc_b = quad_sum(acc_b);
+    if (c.t == 0) {
+        r[warp][c.g] = acc_a;
+        r[warp][c.g + 8] = acc_b;
+    }
+    consumers_sync();
+    if (warp == 0) {
+        float v = 0.f;
+        if (lane < 16) {
+#pragma unroll
+            for (int w = 0; w < kNWC; ++w) v += r[w][lane];
+        }
+        epilogue<EPI>(p, rg, lane, v / rms);
+    }
+    acc_a = 0.f;
+    acc_b = 0.f;
+}
+
+// One stage (KB blocks of the 16 tile rows; limb slice at `slab`) for this warp's
+// share of the blocks.
+template <int TYPE, int KB, int SE, int GS>
+__device__ __forceinline__ void stage_math(const uint8_t* base, const uint8_t* slab, int slot,
+                                           int ra, int rb, const LaneCtx& c, const LeanLane& ll,
+                                           int warp, float& acc_a, float& acc_b) {
+    using F = Fmt<TYPE>;
+    if constexpr (TYPE == IB_TYPE_Q4_K) {
+        const uint32_t b = smem_u32(base), x = smem_u32(slab);
+        const uint32_t wa = b + (uint32_t)(ra * slot), wb = b + (uint32_t)(rb * slot);
+        const float* scale = reinterpret_cast<const float*>(slab + SE * 4);
+        const uint32_t sum32 = x + SE * 4 + (SE / GS) * 4;
+#pragma unroll
+        for (int kbl = warp; kbl < KB; kbl += kNWC)
+            q4k_tile_lean(wa + kbl * F::BB, wb + kbl * F::BB, x + kbl * 1024, sum32 + kbl * 32,
+                          scale[kbl], c, ll, acc_a, acc_b);
+    } else {
+        XLimbs xs;
+        xs.limbs = (int8_t*)slab;
+        xs.scale = (float*)(slab + SE * 4);
+        xs.sum32 = xs.scale + SE / GS;
+        xs.sum16 = xs.sum32 + SE / 32;
+        const uint8_t* sa = base + (size_t)ra * slot;
+        const uint8_t* sb = base + (size_t)rb * slot;
+#pragma unroll
+        for (int kbl = warp * F::UNIT; kbl < KB; kbl += kNWC * F::UNIT)
+            block_math<TYPE, true, true>(sa + kbl * F::BB, sb + kbl * F::BB, kbl, KB, xs, c,
+                                         acc_a, acc_b);
+    }
+}
+
+// ---- TMA-staged persistent kernel: kNWC consumer warps + 1 producer warp ---------
+// Stage layout: 16 weight rows at slot_a / slot_b bytes apart (padded so the
+// consumers' loads of 8 rows spread over the shared-memory banks), then the limb
+// slice at byte wbytes.
+template <int TA, int TB, int PRO, int EPI>
+__global__ void __launch_bounds__((kNWC + 1) * 32)
+    fused_tma_kernel(const FusedGemv p, int S, int slot_a, int slot_b, int wbytes) {
+    using P = Pair<TA, TB>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ float red[2][kNWC][16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = p.K / P::BE;
+    const int spg = nb / P::KB;
+    const int stage_bytes = wbytes + P::SLICE;
+    const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
+    const int my_rg = (int)blockIdx.x < n_rg ? (n_rg - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_rg * spg;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kNWC);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    if (warp == kNWC) {
+        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice
+        auto weights = [&](int it) {
+            const int s = it % S;
+            const int rg = blockIdx.x + (it / spg) * gridDim.x, st = it % spg;
+            const bool isb = group_is_b<TA, TB>(p, rg);
+            const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
+            const int chunk = P::KB * bb;
+            const int n = group_rows(p, rg);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
+            __syncwarp();
+            if (lane < n) {
+                int seg, lr;
+                tile_row(p, rg, lane, seg, lr);
+                const size_t rbytes = (size_t)nb * bb;
+                bulk_g2s(smem + (size_t)s * stage_bytes + (size_t)lane * (isb ? slot_b : slot_a),
+                         p.W[seg] + (size_t)lr * rbytes + (size_t)st * chunk, (uint32_t)chunk,
+                         &full[s]);
+            }
+        };
+        auto limbs = [&](int it) {
+            const int s = it % S, st = it % spg;
+            if (lane == 16)
+                bulk_g2s(smem + (size_t)s * stage_bytes + wbytes, p.slab + (size_t)st * P::SLICE,
+                         (uint32_t)P::SLICE, &full[s]);
+        };
+        const int pre = total < S ? total : S;
+        for (int it = 0; it < pre; ++it) weights(it);  // constant data: before the grid wait
+        pdl_wait();
+        for (int it = 0; it < pre; ++it) limbs(it);
+        int issued = pre;
+        for (int it = pre; it < total; ++it) {
+            if (!mbar_wait(&empty[it % S], ((it / S) - 1) & 1, &g_decode_fault, 11)) break;
+            weights(it);
+            limbs(it);
+            issued = it + 1;
+        }
+        for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+            mbar_wait(&full[it % S], (it / S) & 1, &g_decode_fault, 12);
+        return;
+    }
+    pdl_wait();
+    const float rms = PRO == PRO_NORM ? rms_of<P::GS>(p, lane) : 1.0f;
+    const LaneCtx c = lane_ctx();
+    const LeanLane ll = lean_lane(c);
+    float acc_a = 0.f, acc_b = 0.f;
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+        const int s = it % S;
+        const int rgl = it / spg, st = it % spg;
+        const int rg = blockIdx.x + rgl * gridDim.x;
+        if (ok && !mbar_wait(&full[s], (it / S) & 1, &g_decode_fault, 13)) ok = false;
+        if (ok) {
+            const uint8_t* base = smem + (size_t)s * stage_bytes;
+            const uint8_t* slab = base + wbytes;
+            const int n = group_rows(p, rg);
+            const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
+            if (group_is_b<TA, TB>(p, rg))
+                stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp,
+                                                    acc_a, acc_b);
+            else
+                stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp,
+                                                    acc_a, acc_b);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (st == spg - 1)
+            finish_group<EPI>(p, red[rgl & 1], rg, warp, lane, c, rms, acc_a, acc_b);
+    }
+}
+
+// ---- direct-load kernel (rows not sliceable into 16-byte TMA copies) ---------------
+template <int TA, int TB, int PRO, int EPI>
+__global__ void __launch_bounds__(kNWC * 32) fused_direct_kernel(const FusedGemv p) {
+    using P = Pair<TA, TB>;
+    __shared__ float red[2][kNWC][16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = p.K / P::BE;
+    const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
+    pdl_launch_dependents();
+    pdl_wait();
+    const float rms = PRO == PRO_NORM ? rms_of<P::GS>(p, lane) : 1.0f;
+    const LaneCtx c = lane_ctx();
+    float acc_a = 0.f, acc_b = 0.f;
+    int k = 0;
+    for (int rg = blockIdx.x; rg < n_rg; rg += gridDim.x, ++k) {
+        int sa_, la, sb_, lb;
+        tile_row(p, rg, c.g, sa_, la);
+        tile_row(p, rg, c.g + 8, sb_, lb);
+        const bool isb = group_is_b<TA, TB>(p, rg);
+        const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
+        const size_t rb = (size_t)nb * bb;
+        const uint8_t* Wa = p.W[sa_] + (size_t)la * rb;
+        const uint8_t* Wb = p.W[sb_] + (size_t)lb * rb;
+        for (int kb = warp * P::UNIT; kb < nb; kb += kNWC * P::UNIT) {
+            const int slice = kb / P::KB, kbl = kb - slice * P::KB;
+            const int nbl = nb - slice * P::KB < P::KB ? nb - slice * P::KB : P::KB;
+            const uint8_t* sl = p.slab + (size_t)slice * P::SLICE;
+            XLimbs xs;
+            xs.limbs = (int8_t*)sl;
+            xs.scale = (float*)(sl + P::SE * 4);
+            xs.sum32 = xs.scale + P::SE / P::GS;
+            xs.sum16 = xs.sum32 + P::SE / 32;
+            if (isb)
+                block_math<TB, false, false>(Wa + (size_t)kb * bb, Wb + (size_t)kb * bb, kbl, nbl,
+                                             xs, c, acc_a, acc_b);
+            else
+                block_math<TA, false, false>(Wa + (size_t)kb * bb, Wb + (size_t)kb * bb, kbl, nbl,
+                                             xs, c, acc_a, acc_b);
+        }
+        finish_group<EPI>(p, red[k & 1], rg, warp, lane, c, rms, acc_a, acc_b);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------------
+// Row stride in a stage: >= the chunk, a multiple of 16, and congruent to 32 (Q4_K's
+// 8-byte loads) or 16 (the 2/4-byte loads of the other formats) modulo 128.
+static int ring_slot(int type, int chunk) {
+    const int want = type == IB_TYPE_Q4_K ? 32 : 16;
+    int s = (chunk + 15) / 16 * 16;
+    while (s % 128 != want) s += 16;
+    return s;
+}
+
+static int pair_of(int type) {  // 0: K-quants, 1: Q4_0/Q8_0, 2: Q5_0/Q5_1, -1: none
+    switch (type) {
+        case IB_TYPE_Q4_K:
+        case IB_TYPE_Q6_K: return 0;
+        case IB_TYPE_Q4_0:
+        case IB_TYPE_Q8_0: return 1;
+        case IB_TYPE_Q5_0:
+        case IB_TYPE_Q5_1: return 2;
+    }
+    return -1;
+}
+
+struct OccKey {
+    const void* f;
+    size_t smem;
+    bool operator<(const OccKey& o) const { return f < o.f || (f == o.f && smem < o.smem); }
+};
+
+static int max_ctas(const void* f, int threads, size_t smem, int* out) {
+    static std::mutex mu;
+    static std::map<std::pair<int, OccKey>, int> cache;
+    static std::map<std::pair<int, const void*>, size_t> attr;
+    int dev = 0;
+    IB_CUDA_CHECK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    auto ak = std::make_pair(dev, f);
+    if (smem > 48 * 1024 - 4096 && attr[ak] < smem) {
+        IB_CUDA_CHECK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr[ak] = smem;
+    }
+    auto key = std::make_pair(dev, OccKey{f, smem});
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+        int per_sm = 0, sms = 0;
+        IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, threads, smem));
+        IB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (per_sm < 1) {
+            set_error("fused GEMV: launch configuration does not fit on an SM");
+            return IB_ERR_UNSUPPORTED;
+        }
+        it = cache.emplace(key, per_sm * sms).first;
+    }
+    *out = it->second;
+    return IB_OK;
+}
+
+bool fused_gemv_supported(const FusedGemv& p, int epi) {
+    if (p.n_seg < 1 || p.n_seg > 3 || p.K <= 0 || !p.slab || ((uintptr_t)p.slab & 15)) return false;
+    const int pr = pair_of(p.type[0]);
+    if (pr < 0) return false;
+    const int be = pr == 0 ? 256 : 32;
+    if (p.K % be) return false;
+    for (int s = 0; s < p.n_seg; ++s) {
+        if (pair_of(p.type[s]) != pr || !p.W[s] || p.rows[s] <= 0) return false;
+        if (((uintptr_t)p.W[s] % 16) != 0) return false;
+        if (!p.paired && s < p.n_seg - 1 && p.rows[s] % 16) return false;
+    }
+    for (int s = p.n_seg; s < 3; ++s)
+        if (p.rows[s] != 0) return false;
+    if (p.paired && (p.n_seg != 2 || p.rows[0] != p.rows[1] || p.type[0] != p.type[1] ||
+                     p.rows[0] % 8))
+        return false;
+    if (epi == EPI_SWIGLU && !p.paired) return false;
+    if (epi != EPI_SWIGLU && p.paired) return false;
+    if (epi == EPI_QKV && (p.n_seg != 3 || p.head_dim <= 0 || p.head_dim % 2 || p.rows[2] % 16 ||
+                           p.rows[0] % p.head_dim || p.rows[1] % p.head_dim ||
+                           p.rows[1] != p.rows[2] || !p.pos || !p.rope || !p.q || !p.kc || !p.vc))
+        return false;
+    if (epi == EPI_ARGMAX && !p.best) return false;
+    if (!p.y && epi != EPI_QKV) return false;
+    return true;
+}
+
+template <int TA, int TB, int PRO, int EPI>
+static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
+    using P = Pair<TA, TB>;
+    const int nb = p.K / P::BE;
+    const int n_rg = p.paired ? p.rows[0] / 8 : (p.rows[0] + p.rows[1] + p.rows[2] + 15) / 16;
+    bool has_a = false, has_b = false;
+    for (int s = 0; s < p.n_seg; ++s) (p.type[s] == TA ? has_a : has_b) = true;
+    int r;
+    if (nb % P::KB == 0) {
+        const int slot_a = ring_slot(TA, P::KB * Fmt<TA>::BB);
+        const int slot_b = ring_slot(TB, P::KB * Fmt<TB>::BB);
+        const int wbytes = 16 * ((has_b && (!has_a || slot_b > slot_a)) ? slot_b : slot_a);
+        const int stage = wbytes + P::SLICE;
+        // shallow rings and many CTAs per SM: the consumers' latency is hidden by warps
+        int S = 73728 / stage;
+        if (S < 2) S = 2;
+        if (S > kMaxStages) S = kMaxStages;
+        const size_t smem = (size_t)S * stage;
+        auto kern = fused_tma_kernel<TA, TB, PRO, EPI>;
+        int cap = 0;
+        if ((r = max_ctas((const void*)kern, (kNWC + 1) * 32, smem, &cap))) return r;
+        const int per = (n_rg + cap - 1) / cap;
+        const int grid = (n_rg + per - 1) / per;
+        IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3((kNWC + 1) * 32), smem, st, pdl, p, S,
+                                 slot_a, slot_b, wbytes));
+        return IB_OK;
+    }
+    auto kern = fused_direct_kernel<TA, TB, PRO, EPI>;
+    int cap = 0;
+    if ((r = max_ctas((const void*)kern, kNWC * 32, 0, &cap))) return r;
+    const int grid = n_rg < cap ? n_rg : cap;
+    IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kNWC * 32), 0, st, pdl, p));
+    return IB_OK;
+}
+
+template <int TA, int TB>
+static int launch_pair(const FusedGemv& p, int pro, int epi, cudaStream_t st, bool pdl) {
+    if (pro == PRO_NORM && epi == EPI_QKV) return launch_inst<TA, TB, PRO_NORM, EPI_QKV>(p, st, pdl);
+    if (pro == PRO_PLAIN && epi == EPI_RESID) return launch_inst<TA, TB, PRO_PLAIN, EPI_RESID>(p, st, pdl);
+    if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_inst<TA, TB, PRO_NORM, EPI_SWIGLU>(p, st, pdl);
+    if (pro == PRO_NORM && epi == EPI_ARGMAX) return launch_inst<TA, TB, PRO_NORM, EPI_ARGMAX>(p, st, pdl);
+    if (pro == PRO_PLAIN && epi == EPI_STORE) return launch_inst<TA, TB, PRO_PLAIN, EPI_STORE>(p, st, pdl);
+    set_error("fused GEMV: unsupported prologue/epilogue combination");
+    return IB_ERR_UNSUPPORTED;
+}
+
+int fused_gemv_launch(const FusedGemv& p, int pro, int epi, cudaStream_t st, bool pdl) {
+    if (!fused_gemv_supported(p, epi)) {
+        set_error("fused GEMV: unsupported types or shapes");
+        return IB_ERR_UNSUPPORTED;
+    }
+    if (pro == PRO_NORM && !p.ssq) {
+        set_error("fused GEMV: a normed input needs its sums of squares");
+        return IB_ERR_INVALID;
+    }
+    switch (pair_of(p.type[0])) {
+        case 0: return launch_pair<IB_TYPE_Q4_K, IB_TYPE_Q6_K>(p, pro, epi, st, pdl);
+        case 1: return launch_pair<IB_TYPE_Q4_0, IB_TYPE_Q8_0>(p, pro, epi, st, pdl);
+        case 2: return launch_pair<IB_TYPE_Q5_0, IB_TYPE_Q5_1>(p, pro, epi, st, pdl);
+    }
+    return IB_ERR_UNSUPPORTED;
+}
+
+int decode_fault_take(int* code) {
+    int v = 0, z = 0;
+    IB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_decode_fault, sizeof(int)));
+    if (v) IB_CUDA_CHECK(cudaMemcpyToSymbol(g_decode_fault, &z, sizeof(int)));
+    *code = v;
+    return IB_OK;
+}
+
+}  // namespace ib

@@ -1,0 +1,83 @@
+// Fused decode GEMV (decode.cu).
+//
+// An activation vector enters a GEMV as a "limb slab": the exact four-int8-limb split
+// of its FP32 values (see gemv_math.cuh), laid out in slices of SE elements so that
+// the GEMV's producer warp can TMA-copy the slice of each pipeline stage next to the
+// stage's weight rows.  Slice layout (bytes): limbs [SE/32][4][32] int8 | scale
+// [SE/GS] | sum32 [SE/32] | sum16 [SE/16] (FP32), padded to 16 bytes.  K-quant weights
+// use SE = 2048, GS = 256; 32-element blocks SE = 1024, GS = 32.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ib {
+
+enum { PRO_PLAIN = 0, PRO_NORM = 1 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+struct SlabGeom {
+    int SE;           // elements per slice
+    int GS;           // elements per limb scale
+    int slice_bytes;  // bytes per slice
+};
+
+__host__ __device__ inline SlabGeom slab_geom(bool kquant) {
+    SlabGeom g;
+    g.SE = kquant ? 2048 : 1024;
+    g.GS = kquant ? 256 : 32;
+    const int b = g.SE * 4 + (g.SE / g.GS + g.SE / 32 + g.SE / 16) * 4;
+    g.slice_bytes = (b + 15) / 16 * 16;
+    return g;
+}
+
+__host__ __device__ inline size_t slab_total_bytes(int K, bool kquant) {
+    const SlabGeom g = slab_geom(kquant);
+    return (size_t)((K + g.SE - 1) / g.SE) * g.slice_bytes;
+}
+
+// True for the K-quant formats (slab geometry SE 2048 / GS 256).
+bool slab_kquant(int type);
+
+// slab <- limbs of x (norm == nullptr) or of x * norm; ssq[g] <- sum of x^2 over scale
+// group g (when ssq != nullptr; the RMSNorm of x is then applied in the GEMV
+// epilogue as 1 / sqrt(sum(ssq) / K + eps)).  K must be a multiple of GS.
+int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_t* slab,
+                   float* ssq, cudaStream_t st, bool pdl);
+
+struct FusedGemv {
+    // Weight rows: segments concatenated in row order (row groups of 16), or, with
+    // `paired`, row group i = rows [8i, 8i+8) of segment 0 followed by the same
+    // rows of segment 1 (both segments of equal shape and type).
+    const uint8_t* W[3];
+    int type[3];
+    int rows[3];
+    int n_seg;
+    int paired;
+    int K;  // columns of every segment
+    // input: limb slab of x (xq_slab_launch); PRO_NORM: sums of squares for RMSNorm
+    const uint8_t* slab;
+    const float* ssq;
+    float eps;
+    // epilogue
+    float* y;  // STORE / ARGMAX: y[row]; RESID: y[row] += ; SWIGLU: y[i] = silu(g_i) * u_i
+    float* q;  // QKV: segment 0 after RoPE -> q; segment 1 -> kc; segment 2 -> vc
+    float* kc;
+    float* vc;
+    const float* rope;  // [max_seq][head_dim / 2][cos, sin]
+    const int* pos;     // device position of the token
+    int head_dim, max_seq;
+    unsigned long long* best;  // ARGMAX: max of (ordered logit << 32 | ~row)
+};
+
+// Launches the fused GEMV; IB_ERR_UNSUPPORTED when the type mix or shapes have no
+// fused kernel (the caller then uses the separate kernels).
+int fused_gemv_launch(const FusedGemv& p, int pro, int epi, cudaStream_t st, bool pdl);
+bool fused_gemv_supported(const FusedGemv& p, int epi);
+// Reads and clears the fused kernels' fault word (0 = no bounded wait expired).
+int decode_fault_take(int* code);
+// Decodes the ARGMAX key into a row index (resets nothing).
+__host__ __device__ inline int argmax_key_row(unsigned long long key) {
+    return (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+}
+
+}  // namespace ib

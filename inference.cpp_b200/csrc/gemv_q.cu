@@ -14,6 +14,7 @@
 // Integer -> float conversion of small unsigned fields uses the exponent trick
 // f = as_float(0x4B000000 | u) - 2^23, exact for u < 2^23.
 #include "common.cuh"
+#include "decode.cuh"
 #include "gemv_mma.cuh"
 #include "ops.cuh"
 #include "quant.cuh"
@@ -332,6 +333,27 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     IB_REQUIRE(cols % be == 0, "cols must be a multiple of the block size");
     cudaStream_t st = as_stream(stream);
     const uint8_t* W = (const uint8_t*)dev_W;
+    if (cols <= (1 << 30) && rows < (1ll << 31) && gemv_mma_supported(type)) {
+        // limb slab of x, then the TMA-staged GEMV (decode.cu)
+        const bool kq = slab_kquant(type);
+        FusedGemv f = {};
+        f.W[0] = W;
+        f.type[0] = type;
+        f.rows[0] = (int)rows;
+        f.n_seg = 1;
+        f.K = (int)cols;
+        f.y = dev_y;
+        f.slab = (const uint8_t*)16;  // placeholder for the shape check
+        if (fused_gemv_supported(f, EPI_STORE)) {
+            void* ws = nullptr;
+            int r = workspace_get(WS_GEMV, slab_total_bytes((int)cols, kq), &ws);
+            if (r != IB_OK) return r;
+            if ((r = xq_slab_launch(dev_x, nullptr, (int)cols, kq, (uint8_t*)ws, nullptr, st, false)))
+                return r;
+            f.slab = (const uint8_t*)ws;
+            return fused_gemv_launch(f, PRO_PLAIN, EPI_STORE, st, false);
+        }
+    }
     if (gemv_mma_supported(type) && ((uintptr_t)W % gemv_mma_align(type)) == 0 &&
         cols <= (1 << 30) && rows < (1ll << 31)) {
         void* ws = nullptr;

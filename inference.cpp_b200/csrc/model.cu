@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "gguf_reader.h"
 #include "model.h"
 #include "ops.cuh"
@@ -39,6 +40,19 @@ __global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__
 // and the token is recorded at out_tokens[pos] (when given).
 __global__ void feedback_kernel(int32_t* dev_i32, int32_t* out_tokens, int max_seq) {
     const int next = dev_i32[2], pos = dev_i32[1];
+    if (out_tokens && pos >= 0 && pos < max_seq) out_tokens[pos] = next;
+    dev_i32[0] = next;
+    dev_i32[1] = pos + 1;
+}
+
+// Fused-path feedback: the head's argmax key gives the next token; the key is reset
+// for the next step.
+__global__ void feedback_best_kernel(unsigned long long* best, int32_t* dev_i32,
+                                     int32_t* out_tokens, int max_seq) {
+    const int next = argmax_key_row(*best);
+    *best = 0ull;
+    const int pos = dev_i32[1];
+    dev_i32[2] = next;
     if (out_tokens && pos >= 0 && pos < max_seq) out_tokens[pos] = next;
     dev_i32[0] = next;
     dev_i32[1] = pos + 1;
@@ -337,6 +351,20 @@ extern "C" int ib_model_finalize(void* h) {
     m->allocations.push_back(m->dev_i32);
     IB_CUDA_CHECK(cudaMalloc(&m->dev_tokens, (size_t)S * 4 + 16));
     m->allocations.push_back(m->dev_tokens);
+    IB_CUDA_CHECK(cudaMalloc(&m->best, 16));
+    m->allocations.push_back(m->best);
+    IB_CUDA_CHECK(cudaMemsetAsync(m->best, 0, 16, m->stream));
+    m->slab_kq = slab_kquant(m->layers.empty() ? m->tok.type : m->layers[0].wq.type);
+    {
+        uint8_t** slabs[] = {&m->slab_x, &m->slab_att, &m->slab_h};
+        const int lens[] = {D, H * HD, F};
+        for (int i = 0; i < 3; ++i) {
+            IB_CUDA_CHECK(cudaMalloc(slabs[i], slab_total_bytes(lens[i], m->slab_kq) + 16));
+            m->allocations.push_back(*slabs[i]);
+        }
+        if ((st = alloc_f(m, &m->ssq, (size_t)D / 32 + 1))) return st;
+    }
+    m->fused_ok = fused_supported(m);
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
     IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
     m->finalized = true;
@@ -345,20 +373,156 @@ extern "C" int ib_model_finalize(void* h) {
 
 namespace ib {
 
-// One decode step for the token in dev_i32[0] at position dev_i32[1]; the greedy
-// next token lands in dev_i32[2].  Every launch reads the position on the device.
-static int decode_launches(Model* m) {
+// ---- fused decode path: five launches per layer ------------------------------------
+//   QKV    RMSNorm(x) -> q, k, v in one GEMV over [wq; wk; wv]; RoPE; k, v into the cache
+//   attn   split-K partial + combine (attention.cu)
+//   wo     x += wo . att
+//   ffn    RMSNorm(x) -> silu(w1 . xn) * (w3 . xn), gate and up rows paired per tile
+//   down   x += w2 . h
+// then the head (RMSNorm, logits, argmax) and the token feedback.
+static FusedGemv fg_common(const Model* m) {
+    FusedGemv p = {};
+    p.eps = m->cfg.rms_eps;
+    return p;
+}
+
+static void fg_seg(FusedGemv& p, int i, const Linear& l) {
+    p.W[i] = (const uint8_t*)l.w;
+    p.type[i] = l.type;
+    p.rows[i] = (int)l.rows;
+    p.n_seg = i + 1;
+}
+
+static FusedGemv fg_qkv(const Model* m, const Layer& L) {
+    FusedGemv p = fg_common(m);
+    fg_seg(p, 0, L.wq);
+    fg_seg(p, 1, L.wk);
+    fg_seg(p, 2, L.wv);
+    p.K = m->cfg.dim;
+    p.slab = m->slab_x;
+    p.ssq = m->ssq;
+    p.q = m->q;
+    p.kc = L.kc;
+    p.vc = L.vc;
+    p.rope = m->rope_table;
+    p.pos = m->dev_i32 + 1;
+    p.head_dim = m->HD;
+    p.max_seq = m->cfg.max_seq;
+    return p;
+}
+
+static FusedGemv fg_wo(const Model* m, const Layer& L) {
+    FusedGemv p = fg_common(m);
+    fg_seg(p, 0, L.wo);
+    p.K = (int)L.wo.cols;
+    p.slab = m->slab_att;
+    p.y = m->x;
+    return p;
+}
+
+static FusedGemv fg_ffn_in(const Model* m, const Layer& L) {
+    FusedGemv p = fg_common(m);
+    fg_seg(p, 0, L.w1);
+    fg_seg(p, 1, L.w3);
+    p.paired = 1;
+    p.K = m->cfg.dim;
+    p.slab = m->slab_x;
+    p.ssq = m->ssq;
+    p.y = m->gate;
+    return p;
+}
+
+static FusedGemv fg_ffn_out(const Model* m, const Layer& L) {
+    FusedGemv p = fg_common(m);
+    fg_seg(p, 0, L.w2);
+    p.K = (int)L.w2.cols;
+    p.slab = m->slab_h;
+    p.y = m->x;
+    return p;
+}
+
+static FusedGemv fg_head(const Model* m) {
+    FusedGemv p = fg_common(m);
+    fg_seg(p, 0, m->has_output ? m->out : m->tok);
+    p.K = m->cfg.dim;
+    p.slab = m->slab_x;
+    p.ssq = m->ssq;
+    p.y = m->logits;
+    p.best = m->best;
+    return p;
+}
+
+bool fused_supported(const Model* m) {
     const auto& c = m->cfg;
-    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
-    cudaStream_t st = m->stream;
+    const Linear& O = m->has_output ? m->out : m->tok;
+    const int GS = m->slab_kq ? 256 : 32;
+    if (c.dim % GS || c.ffn % GS || (c.n_heads * m->HD) % GS) return false;
+    if (O.repr != REPR_PACKED || slab_kquant(O.type) != m->slab_kq ||
+        !fused_gemv_supported(fg_head(m), EPI_ARGMAX))
+        return false;
+    for (const Layer& L : m->layers) {
+        for (const Linear* l : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3})
+            if (l->repr != REPR_PACKED || slab_kquant(l->type) != m->slab_kq) return false;
+        if (!fused_gemv_supported(fg_qkv(m, L), EPI_QKV) ||
+            !fused_gemv_supported(fg_wo(m, L), EPI_RESID) ||
+            !fused_gemv_supported(fg_ffn_in(m, L), EPI_SWIGLU) ||
+            !fused_gemv_supported(fg_ffn_out(m, L), EPI_RESID))
+            return false;
+    }
+    return true;
+}
+
+static int embed_launch(Model* m) {
+    const auto& c = m->cfg;
     const int* tok = m->dev_i32;
+    cudaStream_t st = m->stream;
+    if (m->tok.repr == REPR_PACKED)
+        return ib_embedding_q(m->tok.type, m->tok.w, tok, m->x, 1, c.vocab, c.dim, st);
+    if (m->tok.repr == REPR_I16)
+        return ib_embedding_batch_i16(m->tok.q, m->tok.s, tok, m->x, 1, c.dim, st);
+    return ib_embedding_batch(m->tok.f, tok, m->x, 1, c.dim, st);
+}
+
+static int decode_launches_fused(Model* m) {
+    const auto& c = m->cfg;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn;
+    const bool kq = m->slab_kq;
+    cudaStream_t st = m->stream;
     const int* pos = m->dev_i32 + 1;
     const float scale = 1.0f / sqrtf((float)HD);
     int r;
-    if (m->tok.repr == REPR_PACKED) r = ib_embedding_q(m->tok.type, m->tok.w, tok, m->x, 1, V, D, st);
-    else if (m->tok.repr == REPR_I16) r = ib_embedding_batch_i16(m->tok.q, m->tok.s, tok, m->x, 1, D, st);
-    else r = ib_embedding_batch(m->tok.f, tok, m->x, 1, D, st);
-    if (r) return r;
+    if ((r = embed_launch(m))) return r;
+    for (auto& L : m->layers) {
+        if ((r = xq_slab_launch(m->x, L.attn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+        if ((r = fused_gemv_launch(fg_qkv(m, L), PRO_NORM, EPI_QKV, st, true))) return r;
+        if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
+                                  m->att_part, st, pos, true)))
+            return r;
+        if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true))) return r;
+        if ((r = fused_gemv_launch(fg_wo(m, L), PRO_PLAIN, EPI_RESID, st, true))) return r;
+        if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+        if ((r = fused_gemv_launch(fg_ffn_in(m, L), PRO_NORM, EPI_SWIGLU, st, true))) return r;
+        if ((r = xq_slab_launch(m->gate, nullptr, F, kq, m->slab_h, nullptr, st, true))) return r;
+        if ((r = fused_gemv_launch(fg_ffn_out(m, L), PRO_PLAIN, EPI_RESID, st, true))) return r;
+    }
+    if ((r = xq_slab_launch(m->x, m->out_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+    if ((r = fused_gemv_launch(fg_head(m), PRO_NORM, EPI_ARGMAX, st, true))) return r;
+    feedback_best_kernel<<<1, 1, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq);
+    IB_LAUNCH_CHECK("decode step");
+    return IB_OK;
+}
+
+// One decode step for the token in dev_i32[0] at position dev_i32[1]; the greedy
+// next token lands in dev_i32[2].  Every launch reads the position on the device.
+static int decode_launches(Model* m) {
+    if (m->use_fused && m->fused_ok) return decode_launches_fused(m);
+    const auto& c = m->cfg;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
+    cudaStream_t st = m->stream;
+    const int* pos = m->dev_i32 + 1;
+    const float scale = 1.0f / sqrtf((float)HD);
+    int r;
+    if ((r = embed_launch(m))) return r;
     const int g_add = (D + 255) / 256 < 1184 ? (D + 255) / 256 : 1184;
     const int g_ffn = (F + 255) / 256 < 1184 ? (F + 255) / 256 : 1184;
     for (auto& L : m->layers) {
@@ -583,6 +747,24 @@ extern "C" int ib_model_step_kernels(void* h, int* n) {
     }
     cudaGraphDestroy(g);
     *n = k;
+    return IB_OK;
+}
+
+extern "C" int ib_model_set_fused(void* h, int enabled) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    m->use_fused = enabled != 0;
+    if (m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    return IB_OK;
+}
+
+extern "C" int ib_model_uses_fused(void* h, int* fused) {
+    IB_REQUIRE(h && fused, "null pointer argument");
+    Model* m = (Model*)h;
+    *fused = (m->use_fused && m->fused_ok) ? 1 : 0;
     return IB_OK;
 }
 

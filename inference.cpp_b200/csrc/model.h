@@ -40,6 +40,8 @@ struct Model {
     bool finalized = false;
     bool has_output = false;
     bool use_graph = true;
+    bool use_fused = true;  // fused decode kernels when every weight supports them
+    bool fused_ok = false;
     Linear tok, out;
     float* out_norm = nullptr;
     std::vector<Layer> layers;
@@ -50,6 +52,11 @@ struct Model {
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr;
     float *proj = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *att_part = nullptr;
     int32_t* dev_i32 = nullptr;  // [0] token, [1] position, [2] next token
+    unsigned long long* best = nullptr;  // fused head: (ordered logit << 32 | ~row) max
+    // fused path: limb slabs of the GEMV inputs and RMSNorm sums of squares
+    bool slab_kq = true;
+    uint8_t *slab_x = nullptr, *slab_att = nullptr, *slab_h = nullptr;
+    float* ssq = nullptr;
     int32_t* dev_tokens = nullptr;  // [max_seq] ids produced by decode steps, by position
     void* host_pinned = nullptr;
     // prefill scratch (grown on demand)
@@ -63,6 +70,8 @@ struct Model {
 };
 
 int decode_step(Model* m, int token, int pos, float* host_logits, int* next);
+// True when every decode GEMV of the model has a fused kernel (decode.cu).
+bool fused_supported(const Model* m);
 int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_logits, int* next);
 
 }  // namespace ib

@@ -14,7 +14,7 @@ int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
 // partial buffer must hold attention_partial_bytes(H, HD, max_seq - 1).
 int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st, const int* pos_dev);
+                     cudaStream_t st, const int* pos_dev, bool pdl = false);
 int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
                            cudaStream_t st);

@@ -94,7 +94,11 @@ LLAMA3_8B = LlamaConfig("llama-3-8b", 32, 4096, 32, 8, 14336, 128256, 4096, 5000
 LLAMA3_70B = LlamaConfig("llama-3-70b", 80, 8192, 64, 8, 28672, 128256, 2048, 500000.0, 1e-5,
                          embed_type=Q4_K, linear_type=Q4_K, attn_v_type=Q4_K,
                          ffn_down_type=Q4_K, output_type=Q6_K)
-CONFIGS = {c.name: c for c in (STORIES15M, TINYLLAMA, LLAMA3_8B, LLAMA3_70B)}
+# Profiling case: the Llama-3-8B layer and head shapes with 4 layers (~1 GB of
+# weights, still far larger than the 126 MB L2), small enough for detailed profiler
+# captures.
+LLAMA3_8B_4L = dataclasses.replace(LLAMA3_8B, name="llama-3-8b-4l", n_layers=4)
+CONFIGS = {c.name: c for c in (STORIES15M, TINYLLAMA, LLAMA3_8B, LLAMA3_70B, LLAMA3_8B_4L)}
 
 
 def tensor_seed(model_seed: int, name: str) -> int:

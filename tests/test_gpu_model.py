@@ -35,6 +35,19 @@ def tiny_cfgs():
     ]
 
 
+def tma_cfgs():
+    """Shapes whose rows slice into 16-byte TMA copies (K-quants: K % 2048 == 0,
+    32-element blocks: K % 1024 == 0); vocab sizes leave a ragged last row group."""
+    return [
+        gw.LlamaConfig("small-k-tma", 2, 2048, 16, 4, 4096, 1000, 64, 500000.0, 1e-5,
+                       embed_type=ib.Q4_K, linear_type=ib.Q4_K, attn_v_type=ib.Q6_K,
+                       ffn_down_type=ib.Q6_K, output_type=ib.Q6_K, q6k_alternate=True),
+        gw.LlamaConfig("small-q4_0-tma", 1, 1024, 8, 8, 2048, 520, 48, 10000.0, 1e-5,
+                       embed_type=ib.Q4_0, linear_type=ib.Q4_0, attn_v_type=ib.Q8_0,
+                       ffn_down_type=ib.Q8_0, output_type=ib.Q8_0),
+    ]
+
+
 def close_logits(a, b):
     a, b = np.atleast_2d(a), np.atleast_2d(b)
     scale = np.abs(b).max(axis=1, keepdims=True)
@@ -66,6 +79,36 @@ def test_tiny_generate_matches_oracle(cuda, port, cfg, precision):
         assert nxt == want[prompt.size + i], i
         assert close_logits(lg, want_logits[i]), i
     m.close()
+
+
+@pytest.mark.parametrize("cfg", tiny_cfgs() + tma_cfgs(), ids=lambda c: c.name)
+def test_fused_decode_matches_oracle(cuda, port, cfg):
+    """The fused decode kernels (and the separate kernels they replace) reproduce the
+    oracle's greedy tokens and per-step logits."""
+    tensors = synth(cfg, 77)
+    om = port.model(cfg, tensors)
+    a = ib.Model.from_tensors(cfg, tensors)
+    b = ib.Model.from_tensors(cfg, tensors)
+    b.set_fused(False)
+    assert not b.uses_fused()
+    # every config except the Q4_0/Q5_1 QKV mix has a fused kernel for each GEMV
+    assert a.uses_fused() == (cfg.name != "tiny-q4_0")
+    prompt = np.array([2, 9, 4, 27, 1, 8], dtype=np.int32) % cfg.vocab
+    n_new = min(24, cfg.ctx - prompt.size)
+    want, want_logits = om.generate(prompt, n_new, want_logits=True)
+    assert list(a.generate(prompt, n_new)[0]) == list(want)
+    assert list(b.generate(prompt, n_new)[0]) == list(want)
+    for i in range(1, n_new):
+        tok, p = int(want[prompt.size + i - 1]), prompt.size + i - 1
+        na, la = a.decode(tok, p, want_logits=True)
+        nb, lb = b.decode(tok, p, want_logits=True)
+        assert na == nb == want[prompt.size + i], i
+        assert close_logits(la, want_logits[i]) and close_logits(lb, want_logits[i]), i
+    assert ib.check_fault() == 0
+    if a.uses_fused():  # embed; per layer 4 limb slabs + 4 GEMVs + 2 attention; head slab + head + feedback
+        assert a.step_kernels() == 1 + 10 * cfg.n_layers + 3
+    a.close()
+    b.close()
 
 
 def test_graph_and_direct_launches_agree(cuda):
