@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "ops.cuh"
 #include "pdl.cuh"
+#include "slab.cuh"
 
 namespace ib {
 
@@ -303,6 +304,254 @@ int attention_decode(const float* q, const float* kc, const float* vc, float* ou
     IB_CUDA_CHECK(launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, pdl, part, out, HD,
                              n_chunks, ch, pos / ch + 1, pos_dev));
     IB_LAUNCH_CHECK("attention_combine_kernel");
+    return IB_OK;
+}
+
+// ---- fused decode attention ---------------------------------------------------------
+// Grid (kv head, split).  Split sp owns positions [sp * per, (sp + 1) * per) with
+// per = ceil((pos + 1) / ATT_SPLITS) rounded up to whole 32-position tiles, and runs an
+// online softmax over its tiles (K and V rows of a tile loaded together).  Partials
+// (running max, exp-sum, unnormalised P.V) go to `part`; the last CTA of each kv head
+// (atomic counter, reset after use) combines them in parallel and writes the head
+// outputs and, when `slab` is set, their limb slab for the next GEMV.
+constexpr int ATT_TILE = 32;
+constexpr int ATT_SPLITS = 64;
+
+template <int GMAX>
+__global__ void __launch_bounds__(128) attn_fused_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ part_acc, float2* __restrict__ part_ml, int* __restrict__ counters,
+    float* __restrict__ out, uint8_t* __restrict__ slab, int slab_kq, int n_heads, int n_kv_heads,
+    int head_dim, int max_seq, float scale, const int* __restrict__ pos_dev) {
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int PW = ATT_TILE / 4;  // positions per warp per tile
+    __shared__ float4 qs[GMAX][32];
+    __shared__ float sc[GMAX][ATT_TILE];
+    __shared__ float alpha[GMAX], mrun[GMAX], lrun[GMAX];
+    __shared__ float4 accs[4][GMAX][32];
+    __shared__ float wsp[GMAX][ATT_SPLITS];
+    __shared__ float linv[GMAX];
+    __shared__ __align__(16) float ovals[GMAX * 128];
+    __shared__ int is_last;
+    const int pos = *pos_dev;
+    const int G = n_heads / n_kv_heads;
+    const int hk = blockIdx.x, sp = blockIdx.y;
+    const int n_pos = pos + 1;
+    int per = (n_pos + ATT_SPLITS - 1) / ATT_SPLITS;
+    per = (per + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+    const int live = (n_pos + per - 1) / per;
+    if (sp >= live || pos >= max_seq) return;
+    const int p0 = sp * per, p1 = min(n_pos, p0 + per);
+    const int nv = head_dim >> 2;  // float4 per row
+    int lpp = 1;
+    while (lpp < nv) lpp <<= 1;  // lanes per position
+    const int ppp = 32 / lpp;    // positions per warp pass
+    const int passes = (PW + ppp - 1) / ppp;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pp = lane / lpp, li = lane % lpp;
+    const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
+    for (int i = tid; i < G * nv; i += 128) qs[i / nv][i % nv] = q4[i];
+    if (tid < G) {
+        mrun[tid] = -INFINITY;
+        lrun[tid] = 0.f;
+    }
+    __syncthreads();
+    const float4* k4 = reinterpret_cast<const float4*>(kc) + (size_t)hk * max_seq * nv;
+    const float4* v4 = reinterpret_cast<const float4*>(vc) + (size_t)hk * max_seq * nv;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 acc[GMAX];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) acc[g] = z4;
+    for (int t0 = p0; t0 < p1; t0 += ATT_TILE) {
+        const int n = min(ATT_TILE, p1 - t0);
+        float4 kr[PW], vr[PW];
+#pragma unroll
+        for (int p = 0; p < PW; ++p) {
+            const int s = warp * PW + p * ppp + pp;
+            const bool ok = p < passes && p * ppp + pp < PW && s < n && li < nv;
+            kr[p] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + li) : z4;
+            vr[p] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + li) : z4;
+        }
+#pragma unroll
+        for (int p = 0; p < PW; ++p) {
+            if (p >= passes) break;
+            const int s = warp * PW + p * ppp + pp;
+            float d[GMAX];
+#pragma unroll
+            for (int g = 0; g < GMAX; ++g) {
+                const float4 a = li < nv && g < G ? qs[g][li] : z4;
+                d[g] = a.x * kr[p].x + a.y * kr[p].y + a.z * kr[p].z + a.w * kr[p].w;
+            }
+            for (int o = 1; o < lpp; o <<= 1)
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+            if (li == 0 && p * ppp + pp < PW && s < n)
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g)
+                    if (g < G) sc[g][s] = d[g] * scale;
+        }
+        __syncthreads();
+        for (int g = warp; g < G; g += 4) {  // online softmax over the tile
+            const float a = lane < n ? sc[g][lane] : -INFINITY;
+            const float mt = wmax(a);
+            const float mo = mrun[g], mn = fmaxf(mo, mt);
+            const float e = lane < n ? expf(a - mn) : 0.f;
+            const float lt = wsum(e);
+            sc[g][lane] = e;
+            if (lane == 0) {
+                const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
+                alpha[g] = al;
+                lrun[g] = lrun[g] * al + lt;
+                mrun[g] = mn;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+            const float al = g < G ? alpha[g] : 0.f;
+            acc[g].x *= al;
+            acc[g].y *= al;
+            acc[g].z *= al;
+            acc[g].w *= al;
+        }
+#pragma unroll
+        for (int p = 0; p < PW; ++p) {
+            if (p >= passes) break;
+            const int s = warp * PW + p * ppp + pp;
+            if (p * ppp + pp < PW && s < n) {
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g) {
+                    const float w = g < G ? sc[g][s] : 0.f;
+                    acc[g].x = fmaf(w, vr[p].x, acc[g].x);
+                    acc[g].y = fmaf(w, vr[p].y, acc[g].y);
+                    acc[g].z = fmaf(w, vr[p].z, acc[g].z);
+                    acc[g].w = fmaf(w, vr[p].w, acc[g].w);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    for (int o = lpp; o < 32; o <<= 1)
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+            acc[g].x += __shfl_xor_sync(0xffffffffu, acc[g].x, o);
+            acc[g].y += __shfl_xor_sync(0xffffffffu, acc[g].y, o);
+            acc[g].z += __shfl_xor_sync(0xffffffffu, acc[g].z, o);
+            acc[g].w += __shfl_xor_sync(0xffffffffu, acc[g].w, o);
+        }
+    if (pp == 0 && li < nv)
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g)
+            if (g < G) accs[warp][g][li] = acc[g];
+    __syncthreads();
+    for (int i = tid; i < G * nv; i += 128) {
+        const int g = i / nv, l4 = i % nv;
+        float4 a = accs[0][g][l4];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            const float4 b = accs[w][g][l4];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        const size_t row = (size_t)(hk * G + g) * ATT_SPLITS + sp;
+        reinterpret_cast<float4*>(part_acc + row * head_dim)[l4] = a;
+        if (l4 == 0) part_ml[row] = make_float2(mrun[g], lrun[g]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&counters[hk], 1) == live - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // combine the live splits of this kv head
+    for (int g = warp; g < G; g += 4) {
+        const size_t r0 = (size_t)(hk * G + g) * ATT_SPLITS;
+        const float2 a = lane < live ? __ldcg(part_ml + r0 + lane) : make_float2(-INFINITY, 0.f);
+        const float2 b = lane + 32 < live ? __ldcg(part_ml + r0 + lane + 32)
+                                          : make_float2(-INFINITY, 0.f);
+        const float M = wmax(fmaxf(a.x, b.x));
+        const float wa = lane < live ? expf(a.x - M) : 0.f;
+        const float wb = lane + 32 < live ? expf(b.x - M) : 0.f;
+        const float L = wsum(wa * a.y + wb * b.y);
+        wsp[g][lane] = wa;
+        wsp[g][lane + 32] = wb;
+        if (lane == 0) linv[g] = 1.0f / L;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * nv; i += 128) {
+        const int g = i / nv, l4 = i % nv;
+        const float4* src = reinterpret_cast<const float4*>(part_acc) +
+                            ((size_t)(hk * G + g) * ATT_SPLITS) * nv + l4;
+        float4 a = z4;
+        for (int c = 0; c < live; ++c) {
+            const float w = wsp[g][c];
+            const float4 b = __ldcg(src + (size_t)c * nv);
+            a.x = fmaf(w, b.x, a.x);
+            a.y = fmaf(w, b.y, a.y);
+            a.z = fmaf(w, b.z, a.z);
+            a.w = fmaf(w, b.w, a.w);
+        }
+        const float inv = linv[g];
+        a.x *= inv;
+        a.y *= inv;
+        a.z *= inv;
+        a.w *= inv;
+        reinterpret_cast<float4*>(out + (size_t)(hk * G + g) * head_dim)[l4] = a;
+        reinterpret_cast<float4*>(ovals + g * head_dim)[l4] = a;
+    }
+    if (tid == 0) counters[hk] = 0;
+    if (!slab) return;
+    __syncthreads();
+    const int n_el = G * head_dim;
+    const int base_el = hk * n_el;
+    if (slab_kq) {
+        constexpr int GS = SlabG<true>::GS;
+        for (int gl = warp; gl < n_el / GS; gl += 4) {
+            float v[GS / 32];
+#pragma unroll
+            for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
+            slab_write_group<true>(v, (base_el + gl * GS) / GS, slab, lane);
+        }
+    } else {
+        constexpr int GS = SlabG<false>::GS;
+        for (int gl = warp; gl < n_el / GS; gl += 4) {
+            float v[GS / 32];
+#pragma unroll
+            for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
+            slab_write_group<false>(v, (base_el + gl * GS) / GS, slab, lane);
+        }
+    }
+}
+
+bool attention_fused_ok(int H, int Hkv, int HD) { return fast_ok(H, Hkv, HD); }
+
+size_t attention_fused_part_bytes(int H, int HD) {
+    return (size_t)H * ATT_SPLITS * ((size_t)HD * 4 + 8) + 256;
+}
+
+int attention_decode_fused(const float* q, const float* kc, const float* vc, float* out,
+                           uint8_t* slab, bool slab_kq, int H, int Hkv, int HD, int max_seq,
+                           float scale, float* part, int* counters, cudaStream_t st,
+                           const int* pos_dev, bool pdl) {
+    IB_REQUIRE(fast_ok(H, Hkv, HD) && pos_dev && counters && part, "fused attention: bad arguments");
+    IB_REQUIRE(((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out | (uintptr_t)part) % 16 == 0,
+               "fused attention: pointers must be 16-byte aligned");
+    const int G = H / Hkv;
+    if (slab) {
+        const int GS = slab_kq ? SlabG<true>::GS : SlabG<false>::GS;
+        IB_REQUIRE((G * HD) % GS == 0, "fused attention: head group not a whole limb group");
+    }
+    float* part_acc = part;
+    float2* part_ml = reinterpret_cast<float2*>(part + (size_t)H * ATT_SPLITS * HD);
+    const dim3 grid(Hkv, ATT_SPLITS);
+    auto kern = G <= 1 ? attn_fused_kernel<1> : G <= 2 ? attn_fused_kernel<2> :
+                G <= 4 ? attn_fused_kernel<4> : attn_fused_kernel<8>;
+    IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(128), 0, st, pdl, q, kc, vc, part_acc, part_ml,
+                             counters, out, slab, slab_kq ? 1 : 0, H, Hkv, HD, max_seq, scale,
+                             pos_dev));
     return IB_OK;
 }
 

@@ -29,6 +29,7 @@
 #include "gemv_math.cuh"
 #include "pdl.cuh"
 #include "pipeline.cuh"
+#include "slab.cuh"
 
 namespace ib {
 
@@ -47,41 +48,29 @@ struct Pair {
     static constexpr int BE = KQ ? 256 : 32;  // elements per block
     static constexpr int KB = FA::KB;         // blocks per stage per row
     static constexpr int UNIT = FA::UNIT;
-    static constexpr int SE = KB * BE;        // elements per stage = slab slice
-    static constexpr int GS = KQ ? 256 : 32;  // elements per limb scale
-    static constexpr int SLICE = ((SE * 4 + (SE / GS + SE / 32 + SE / 16) * 4) + 15) / 16 * 16;
+    static constexpr int SE = SlabG<KQ>::SE;  // elements per stage = slab slice
+    static constexpr int GS = SlabG<KQ>::GS;  // elements per limb scale
+    static constexpr int SLICE = SlabG<KQ>::SLICE;
+    static_assert(SE == KB * BE, "a pipeline stage covers one slab slice");
 };
 
 bool slab_kquant(int type) { return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K; }
 
 // ---- limb slab ----------------------------------------------------------------------
-__device__ __forceinline__ float exp2i(int e) {  // 2^e for e in [-126, 127]
-    return __uint_as_float((uint32_t)(e + 127) << 23);
-}
-
-// Smallest e >= -126 with m <= 127 * 2^e, from the exponent bits (m >= 0).
-__device__ __forceinline__ int limb_exp_bits(float m) {
-    if (!(m > 0.f)) return 0;
-    int e = (int)((__float_as_uint(m) >> 23) & 0xFFu) - 133;  // floor(log2 m) - 6
-    if (e < -126) e = -126;
-    if (m > 127.0f * exp2i(e)) ++e;
-    return e;
-}
-
 // One warp per scale group of GS elements.
-template <int GS, int SE, int SLICE>
+template <bool KQ>
 __global__ void __launch_bounds__(256) xq_slab_kernel(const float* __restrict__ x,
                                                       const float* __restrict__ norm, int K,
                                                       uint8_t* __restrict__ slab,
                                                       float* __restrict__ ssq) {
     pdl_launch_dependents();
     pdl_wait();
+    constexpr int GS = SlabG<KQ>::GS, PER = GS / 32;
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (gi * GS >= K) return;
-    constexpr int PER = GS / 32;
     float v[PER];
-    float m = 0.f, ss = 0.f;
+    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
         const int i = (gi * PER + j) * 32 + lane;
@@ -89,41 +78,13 @@ __global__ void __launch_bounds__(256) xq_slab_kernel(const float* __restrict__ 
         ss = fmaf(t, t, ss);
         if (norm) t *= norm[i];
         v[j] = t;
-        m = fmaxf(m, fabsf(t));
     }
+    if (ssq) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) ssq[gi] = ss;
     }
-    if (ssq && lane == 0) ssq[gi] = ss;
-    const int e = limb_exp_bits(m);
-    const float inv_s = exp2i(-e);
-    const int slice = (gi * GS) / SE, gl = (gi * GS - slice * SE) / GS;
-    uint8_t* base = slab + (size_t)slice * SLICE;
-    int8_t* limbs = reinterpret_cast<int8_t*>(base);
-    float* scale = reinterpret_cast<float*>(base + SE * 4);
-    float* sum32 = scale + SE / GS;
-    float* sum16 = sum32 + SE / 32;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        const int sg = gl * PER + j;  // 32-group within the slice
-        float tt = v[j] * inv_s;      // exact: |tt| <= 127
-        int8_t* o = limbs + (size_t)sg * 128;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float r = rintf(tt);
-            o[i * 32 + lane] = (int8_t)(int)r;
-            tt = (tt - r) * 128.0f;
-        }
-        float sm = v[j];
-#pragma unroll
-        for (int o2 = 8; o2 > 0; o2 >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o2);
-        if ((lane & 15) == 0) sum16[sg * 2 + (lane >> 4)] = sm;
-        sm += __shfl_xor_sync(0xffffffffu, sm, 16);
-        if (lane == 0) sum32[sg] = sm;
-    }
-    if (lane == 0) scale[gl] = exp2i(e);
+    slab_write_group<KQ>(v, gi, slab, lane);
 }
 
 int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_t* slab,
@@ -132,15 +93,12 @@ int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_
     const int GS = kquant ? 256 : 32;
     IB_REQUIRE(K % GS == 0, "xq_slab: K must be a multiple of the limb group");
     const int groups = K / GS, grid = (groups + 7) / 8;
-    if (kquant) {
-        using P = Pair<IB_TYPE_Q4_K, IB_TYPE_Q6_K>;
-        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<P::GS, P::SE, P::SLICE>, dim3(grid), dim3(256), 0,
-                                 st, pdl, x, norm, K, slab, ssq));
-    } else {
-        using P = Pair<IB_TYPE_Q4_0, IB_TYPE_Q8_0>;
-        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<P::GS, P::SE, P::SLICE>, dim3(grid), dim3(256), 0,
-                                 st, pdl, x, norm, K, slab, ssq));
-    }
+    if (kquant)
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<true>, dim3(grid), dim3(256), 0, st, pdl, x, norm,
+                                 K, slab, ssq));
+    else
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<false>, dim3(grid), dim3(256), 0, st, pdl, x, norm,
+                                 K, slab, ssq));
     return IB_OK;
 }
 

@@ -363,6 +363,12 @@ extern "C" int ib_model_finalize(void* h) {
             m->allocations.push_back(*slabs[i]);
         }
         if ((st = alloc_f(m, &m->ssq, (size_t)D / 32 + 1))) return st;
+        if (attention_fused_ok(H, Hkv, HD)) {
+            if ((st = alloc_f(m, &m->att_fpart, attention_fused_part_bytes(H, HD) / 4 + 1))) return st;
+            IB_CUDA_CHECK(cudaMalloc(&m->att_counters, (size_t)Hkv * 4 + 16));
+            m->allocations.push_back(m->att_counters);
+            IB_CUDA_CHECK(cudaMemsetAsync(m->att_counters, 0, (size_t)Hkv * 4 + 16, m->stream));
+        }
     }
     m->fused_ok = fused_supported(m);
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
@@ -490,15 +496,24 @@ static int decode_launches_fused(Model* m) {
     cudaStream_t st = m->stream;
     const int* pos = m->dev_i32 + 1;
     const float scale = 1.0f / sqrtf((float)HD);
+    const bool att_slab = m->att_counters && (H / Hkv * HD) % (kq ? 256 : 32) == 0;
     int r;
     if ((r = embed_launch(m))) return r;
     for (auto& L : m->layers) {
         if ((r = xq_slab_launch(m->x, L.attn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
         if ((r = fused_gemv_launch(fg_qkv(m, L), PRO_NORM, EPI_QKV, st, true))) return r;
-        if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
-                                  m->att_part, st, pos, true)))
-            return r;
-        if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true))) return r;
+        if (att_slab) {  // attention writes the wo input's limb slab itself
+            if ((r = attention_decode_fused(m->q, L.kc, L.vc, m->att, m->slab_att, kq, H, Hkv, HD,
+                                            c.max_seq, scale, m->att_fpart, m->att_counters, st,
+                                            pos, true)))
+                return r;
+        } else {
+            if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
+                                      m->att_part, st, pos, true)))
+                return r;
+            if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true)))
+                return r;
+        }
         if ((r = fused_gemv_launch(fg_wo(m, L), PRO_PLAIN, EPI_RESID, st, true))) return r;
         if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
         if ((r = fused_gemv_launch(fg_ffn_in(m, L), PRO_NORM, EPI_SWIGLU, st, true))) return r;

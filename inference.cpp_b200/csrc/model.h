@@ -57,6 +57,8 @@ struct Model {
     bool slab_kq = true;
     uint8_t *slab_x = nullptr, *slab_att = nullptr, *slab_h = nullptr;
     float* ssq = nullptr;
+    float* att_fpart = nullptr;   // fused attention partials
+    int* att_counters = nullptr;  // fused attention: per kv head, zero between steps
     int32_t* dev_tokens = nullptr;  // [max_seq] ids produced by decode steps, by position
     void* host_pinned = nullptr;
     // prefill scratch (grown on demand)

@@ -279,8 +279,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const void* __restrict__
                                                         const float* __restrict__ X,
                                                         float* __restrict__ Y, int T, int M,
                                                         int K) {
-    __shared__ float Ws[GB_K][GB_M + 4];
-    __shared__ float Xs[GB_K][GB_N + 4];
+    __shared__ __align__(16) float Ws[GB_K][GB_M + 4];
+    __shared__ __align__(16) float Xs[GB_K][GB_N + 4];
     const int m0 = blockIdx.x * GB_M, t0 = blockIdx.y * GB_N;
     const int tid = threadIdx.x;
     const int tm = (tid & 15) * 4, tt = (tid >> 4) * 4;

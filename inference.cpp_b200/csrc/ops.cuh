@@ -9,6 +9,15 @@ namespace ib {
 enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_SLOTS = 2 };
 int workspace_get(int slot, size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
+// Decode attention in one launch (split flash-decode, last-CTA combine); also writes
+// the output's limb slab when `slab` is set.  `counters` (n_kv_heads ints) must start
+// at zero; they are left at zero.  part: attention_fused_part_bytes(H, HD).
+bool attention_fused_ok(int H, int Hkv, int HD);
+size_t attention_fused_part_bytes(int H, int HD);
+int attention_decode_fused(const float* q, const float* kc, const float* vc, float* out,
+                           uint8_t* slab, bool slab_kq, int H, int Hkv, int HD, int max_seq,
+                           float scale, float* part, int* counters, cudaStream_t st,
+                           const int* pos_dev, bool pdl);
 int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
 // pos_dev != nullptr: the position is read on the device (graph-capturable) and the
 // partial buffer must hold attention_partial_bytes(H, HD, max_seq - 1).
