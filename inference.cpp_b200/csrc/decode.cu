@@ -253,12 +253,11 @@ __device__ __forceinline__ void stage_math(const uint8_t* base, const uint8_t* s
     if constexpr (TYPE == IB_TYPE_Q4_K) {
         const uint32_t b = smem_u32(base), x = smem_u32(slab);
         const uint32_t wa = b + (uint32_t)(ra * slot), wb = b + (uint32_t)(rb * slot);
-        const float* scale = reinterpret_cast<const float*>(slab + SE * 4);
-        const uint32_t sum32 = x + SE * 4 + (SE / GS) * 4;
+        const uint32_t scale = x + SE * 4, sum32 = scale + (SE / GS) * 4;
 #pragma unroll
         for (int kbl = warp; kbl < KB; kbl += kNWC)
             q4k_tile_lean(wa + kbl * F::BB, wb + kbl * F::BB, x + kbl * 1024, sum32 + kbl * 32,
-                          scale[kbl], c, ll, acc_a, acc_b);
+                          ldsf<0>(scale + kbl * 4), c, ll, acc_a, acc_b);
     } else {
         XLimbs xs;
         xs.limbs = (int8_t*)slab;
@@ -291,7 +290,6 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     const int stage_bytes = wbytes + P::SLICE;
     const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
     const int my_rg = (int)blockIdx.x < n_rg ? (n_rg - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int total = my_rg * spg;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -302,44 +300,59 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     __syncthreads();
     pdl_launch_dependents();
     if (warp == kNWC) {
-        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice
-        auto weights = [&](int it) {
-            const int s = it % S;
-            const int rg = blockIdx.x + (it / spg) * gridDim.x, st = it % spg;
+        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Stage slot s
+        // and its phase advance incrementally (no divisions in the loop).
+        auto limbs = [&](int slot_s, int st) {
+            if (lane == 16)
+                bulk_g2s(smem + (size_t)slot_s * stage_bytes + wbytes,
+                         p.slab + (size_t)st * P::SLICE, (uint32_t)P::SLICE, &full[slot_s]);
+        };
+        int s = 0, ph = 0, it = 0;
+        bool waited = false, ok = true;
+        for (int rgl = 0; rgl < my_rg && ok; ++rgl) {
+            const int rg = blockIdx.x + rgl * gridDim.x;
             const bool isb = group_is_b<TA, TB>(p, rg);
             const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
             const int chunk = P::KB * bb;
             const int n = group_rows(p, rg);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
-            __syncwarp();
+            const int slot = isb ? slot_b : slot_a;
+            const uint8_t* src = p.W[0];
             if (lane < n) {
                 int seg, lr;
                 tile_row(p, rg, lane, seg, lr);
-                const size_t rbytes = (size_t)nb * bb;
-                bulk_g2s(smem + (size_t)s * stage_bytes + (size_t)lane * (isb ? slot_b : slot_a),
-                         p.W[seg] + (size_t)lr * rbytes + (size_t)st * chunk, (uint32_t)chunk,
-                         &full[s]);
+                src = p.W[seg] + (size_t)lr * nb * bb;
             }
-        };
-        auto limbs = [&](int it) {
-            const int s = it % S, st = it % spg;
-            if (lane == 16)
-                bulk_g2s(smem + (size_t)s * stage_bytes + wbytes, p.slab + (size_t)st * P::SLICE,
-                         (uint32_t)P::SLICE, &full[s]);
-        };
-        const int pre = total < S ? total : S;
-        for (int it = 0; it < pre; ++it) weights(it);  // constant data: before the grid wait
-        pdl_wait();
-        for (int it = 0; it < pre; ++it) limbs(it);
-        int issued = pre;
-        for (int it = pre; it < total; ++it) {
-            if (!mbar_wait(&empty[it % S], ((it / S) - 1) & 1, &g_decode_fault, 11)) break;
-            weights(it);
-            limbs(it);
-            issued = it + 1;
+            for (int st = 0; st < spg; ++st, ++it) {
+                if (it >= S && !mbar_wait(&empty[s], ph ^ 1, &g_decode_fault, 11)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
+                __syncwarp();
+                if (lane < n)
+                    bulk_g2s(smem + (size_t)s * stage_bytes + (size_t)lane * slot,
+                             src + (size_t)st * chunk, (uint32_t)chunk, &full[s]);
+                if (waited) {
+                    limbs(s, st);
+                } else if (it == S - 1) {
+                    // weights (constant) of the first ring fill are in flight: now wait for
+                    // the previous kernel before reading its limb slab
+                    pdl_wait();
+                    waited = true;
+                    for (int j = 0; j < S; ++j) limbs(j, j % spg);
+                }
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
         }
-        for (int it = issued > S ? issued - S : 0; it < issued; ++it)
-            mbar_wait(&full[it % S], (it / S) & 1, &g_decode_fault, 12);
+        if (!waited) {
+            pdl_wait();
+            for (int j = 0; j < it; ++j) limbs(j, j % spg);
+        }
+        for (int j = it > S ? it - S : 0; j < it; ++j)  // no copy may land after exit
+            mbar_wait(&full[j % S], (j / S) & 1, &g_decode_fault, 12);
         return;
     }
     pdl_wait();
@@ -348,27 +361,32 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     const LeanLane ll = lean_lane(c);
     float acc_a = 0.f, acc_b = 0.f;
     bool ok = true;
-    for (int it = 0; it < total; ++it) {
-        const int s = it % S;
-        const int rgl = it / spg, st = it % spg;
+    int s = 0, ph = 0;
+    for (int rgl = 0; rgl < my_rg; ++rgl) {
         const int rg = blockIdx.x + rgl * gridDim.x;
-        if (ok && !mbar_wait(&full[s], (it / S) & 1, &g_decode_fault, 13)) ok = false;
-        if (ok) {
-            const uint8_t* base = smem + (size_t)s * stage_bytes;
-            const uint8_t* slab = base + wbytes;
-            const int n = group_rows(p, rg);
-            const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
-            if (group_is_b<TA, TB>(p, rg))
-                stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp,
-                                                    acc_a, acc_b);
-            else
-                stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp,
-                                                    acc_a, acc_b);
+        const bool isb = group_is_b<TA, TB>(p, rg);
+        const int n = group_rows(p, rg);
+        const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
+        for (int st = 0; st < spg; ++st) {
+            if (ok && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) ok = false;
+            if (ok) {
+                const uint8_t* base = smem + (size_t)s * stage_bytes;
+                const uint8_t* slab = base + wbytes;
+                if (isb)
+                    stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp,
+                                                        acc_a, acc_b);
+                else
+                    stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp,
+                                                        acc_a, acc_b);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                ph ^= 1;
+            }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (st == spg - 1)
-            finish_group<EPI>(p, red[rgl & 1], rg, warp, lane, c, rms, acc_a, acc_b);
+        finish_group<EPI>(p, red[rgl & 1], rg, warp, lane, c, rms, acc_a, acc_b);
     }
 }
 
