@@ -308,28 +308,34 @@ int attention_decode(const float* q, const float* kc, const float* vc, float* ou
 }
 
 // ---- fused decode attention ---------------------------------------------------------
-// Grid (kv head, split).  Split sp owns positions [sp * per, (sp + 1) * per) with
-// per = ceil((pos + 1) / ATT_SPLITS) rounded up to whole 32-position tiles, and runs an
-// online softmax over its tiles (K and V rows of a tile loaded together).  Partials
-// (running max, exp-sum, unnormalised P.V) go to `part`; the last CTA of each kv head
-// (atomic counter, reset after use) combines them in parallel and writes the head
-// outputs and, when `slab` is set, their limb slab for the next GEMV.
-constexpr int ATT_TILE = 32;
+// Grid (kv head, split), 256 threads.  Split sp owns positions [sp * per, (sp + 1) * per)
+// with per = ceil((pos + 1) / ATT_SPLITS) rounded up to whole 64-position tiles, and runs
+// an online softmax over its tiles.  In a tile each warp takes 8 positions, 2 at a time:
+// 16 lanes per position, each lane 1 or 2 float4 of the head dimension (K and V rows of
+// the warp's positions are all loaded before any arithmetic).  Partials (running max,
+// exp-sum, unnormalised P.V) go to `part`; the last CTA of each kv head (atomic
+// counter, reset after use) combines them and writes the head outputs and, when `slab`
+// is set, their limb slab for the next GEMV.
+constexpr int ATT_TILE = 64;
 constexpr int ATT_SPLITS = 64;
+constexpr int ATT_WARPS = 8;
 
 template <int GMAX>
-__global__ void __launch_bounds__(128) attn_fused_kernel(
+__global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ part_acc, float2* __restrict__ part_ml, int* __restrict__ counters,
     float* __restrict__ out, uint8_t* __restrict__ slab, int slab_kq, int n_heads, int n_kv_heads,
     int head_dim, int max_seq, float scale, const int* __restrict__ pos_dev) {
     pdl_launch_dependents();
     pdl_wait();
-    constexpr int PW = ATT_TILE / 4;  // positions per warp per tile
+    constexpr int LPP = 16, PPP = 32 / LPP;  // lanes per position, positions per pass
+    constexpr int PW = ATT_TILE / ATT_WARPS;  // positions per warp per tile
+    constexpr int PASSES = PW / PPP;
+    constexpr int NVL = 2;                    // float4 per lane (head_dim <= 128)
     __shared__ float4 qs[GMAX][32];
     __shared__ float sc[GMAX][ATT_TILE];
     __shared__ float alpha[GMAX], mrun[GMAX], lrun[GMAX];
-    __shared__ float4 accs[4][GMAX][32];
+    __shared__ float4 accs[ATT_WARPS][GMAX][32];
     __shared__ float wsp[GMAX][ATT_SPLITS];
     __shared__ float linv[GMAX];
     __shared__ __align__(16) float ovals[GMAX * 128];
@@ -344,14 +350,10 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
     if (sp >= live || pos >= max_seq) return;
     const int p0 = sp * per, p1 = min(n_pos, p0 + per);
     const int nv = head_dim >> 2;  // float4 per row
-    int lpp = 1;
-    while (lpp < nv) lpp <<= 1;  // lanes per position
-    const int ppp = 32 / lpp;    // positions per warp pass
-    const int passes = (PW + ppp - 1) / ppp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pp = lane / lpp, li = lane % lpp;
+    const int pp = lane / LPP, li = lane % LPP;
     const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
-    for (int i = tid; i < G * nv; i += 128) qs[i / nv][i % nv] = q4[i];
+    for (int i = tid; i < G * nv; i += ATT_WARPS * 32) qs[i / nv][i % nv] = q4[i];
     if (tid < G) {
         mrun[tid] = -INFINITY;
         lrun[tid] = 0.f;
@@ -360,45 +362,60 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
     const float4* k4 = reinterpret_cast<const float4*>(kc) + (size_t)hk * max_seq * nv;
     const float4* v4 = reinterpret_cast<const float4*>(vc) + (size_t)hk * max_seq * nv;
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 acc[GMAX];
+    float4 acc[GMAX][NVL];
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g) acc[g] = z4;
+    for (int g = 0; g < GMAX; ++g)
+#pragma unroll
+        for (int k = 0; k < NVL; ++k) acc[g][k] = z4;
     for (int t0 = p0; t0 < p1; t0 += ATT_TILE) {
         const int n = min(ATT_TILE, p1 - t0);
-        float4 kr[PW], vr[PW];
+        float4 kr[PASSES][NVL], vr[PASSES][NVL];
 #pragma unroll
-        for (int p = 0; p < PW; ++p) {
-            const int s = warp * PW + p * ppp + pp;
-            const bool ok = p < passes && p * ppp + pp < PW && s < n && li < nv;
-            kr[p] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + li) : z4;
-            vr[p] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + li) : z4;
+        for (int p = 0; p < PASSES; ++p) {
+            const int s = warp * PW + p * PPP + pp;
+#pragma unroll
+            for (int k = 0; k < NVL; ++k) {
+                const int c = li + LPP * k;
+                const bool ok = s < n && c < nv;
+                kr[p][k] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + c) : z4;
+                vr[p][k] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + c) : z4;
+            }
         }
 #pragma unroll
-        for (int p = 0; p < PW; ++p) {
-            if (p >= passes) break;
-            const int s = warp * PW + p * ppp + pp;
+        for (int p = 0; p < PASSES; ++p) {
+            const int s = warp * PW + p * PPP + pp;
             float d[GMAX];
 #pragma unroll
             for (int g = 0; g < GMAX; ++g) {
-                const float4 a = li < nv && g < G ? qs[g][li] : z4;
-                d[g] = a.x * kr[p].x + a.y * kr[p].y + a.z * kr[p].z + a.w * kr[p].w;
+                float t = 0.f;
+#pragma unroll
+                for (int k = 0; k < NVL; ++k) {
+                    const int c = li + LPP * k;
+                    const float4 a = c < nv && g < G ? qs[g][c] : z4;
+                    t += a.x * kr[p][k].x + a.y * kr[p][k].y + a.z * kr[p][k].z + a.w * kr[p][k].w;
+                }
+                d[g] = t;
             }
-            for (int o = 1; o < lpp; o <<= 1)
+#pragma unroll
+            for (int o = 1; o < LPP; o <<= 1)
 #pragma unroll
                 for (int g = 0; g < GMAX; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
-            if (li == 0 && p * ppp + pp < PW && s < n)
+            if (li == 0 && s < n)
 #pragma unroll
                 for (int g = 0; g < GMAX; ++g)
                     if (g < G) sc[g][s] = d[g] * scale;
         }
         __syncthreads();
-        for (int g = warp; g < G; g += 4) {  // online softmax over the tile
+        for (int g = warp; g < G; g += ATT_WARPS) {  // online softmax over the tile
             const float a = lane < n ? sc[g][lane] : -INFINITY;
-            const float mt = wmax(a);
+            const float b = lane + 32 < n ? sc[g][lane + 32] : -INFINITY;
+            const float mt = wmax(fmaxf(a, b));
             const float mo = mrun[g], mn = fmaxf(mo, mt);
-            const float e = lane < n ? expf(a - mn) : 0.f;
-            const float lt = wsum(e);
-            sc[g][lane] = e;
+            const float ea = lane < n ? expf(a - mn) : 0.f;
+            const float eb = lane + 32 < n ? expf(b - mn) : 0.f;
+            const float lt = wsum(ea + eb);
+            sc[g][lane] = ea;
+            sc[g][lane + 32] = eb;
             if (lane == 0) {
                 const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
                 alpha[g] = al;
@@ -410,46 +427,57 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
 #pragma unroll
         for (int g = 0; g < GMAX; ++g) {
             const float al = g < G ? alpha[g] : 0.f;
-            acc[g].x *= al;
-            acc[g].y *= al;
-            acc[g].z *= al;
-            acc[g].w *= al;
+#pragma unroll
+            for (int k = 0; k < NVL; ++k) {
+                acc[g][k].x *= al;
+                acc[g][k].y *= al;
+                acc[g][k].z *= al;
+                acc[g][k].w *= al;
+            }
         }
 #pragma unroll
-        for (int p = 0; p < PW; ++p) {
-            if (p >= passes) break;
-            const int s = warp * PW + p * ppp + pp;
-            if (p * ppp + pp < PW && s < n) {
+        for (int p = 0; p < PASSES; ++p) {
+            const int s = warp * PW + p * PPP + pp;
+            if (s < n) {
 #pragma unroll
                 for (int g = 0; g < GMAX; ++g) {
                     const float w = g < G ? sc[g][s] : 0.f;
-                    acc[g].x = fmaf(w, vr[p].x, acc[g].x);
-                    acc[g].y = fmaf(w, vr[p].y, acc[g].y);
-                    acc[g].z = fmaf(w, vr[p].z, acc[g].z);
-                    acc[g].w = fmaf(w, vr[p].w, acc[g].w);
+#pragma unroll
+                    for (int k = 0; k < NVL; ++k) {
+                        acc[g][k].x = fmaf(w, vr[p][k].x, acc[g][k].x);
+                        acc[g][k].y = fmaf(w, vr[p][k].y, acc[g][k].y);
+                        acc[g][k].z = fmaf(w, vr[p][k].z, acc[g][k].z);
+                        acc[g][k].w = fmaf(w, vr[p][k].w, acc[g][k].w);
+                    }
                 }
             }
         }
         __syncthreads();
     }
-    for (int o = lpp; o < 32; o <<= 1)
+    // lanes li and li + 16 hold the two position streams of the same dims
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-            acc[g].x += __shfl_xor_sync(0xffffffffu, acc[g].x, o);
-            acc[g].y += __shfl_xor_sync(0xffffffffu, acc[g].y, o);
-            acc[g].z += __shfl_xor_sync(0xffffffffu, acc[g].z, o);
-            acc[g].w += __shfl_xor_sync(0xffffffffu, acc[g].w, o);
+    for (int g = 0; g < GMAX; ++g)
+#pragma unroll
+        for (int k = 0; k < NVL; ++k) {
+            acc[g][k].x += __shfl_xor_sync(0xffffffffu, acc[g][k].x, 16);
+            acc[g][k].y += __shfl_xor_sync(0xffffffffu, acc[g][k].y, 16);
+            acc[g][k].z += __shfl_xor_sync(0xffffffffu, acc[g][k].z, 16);
+            acc[g][k].w += __shfl_xor_sync(0xffffffffu, acc[g][k].w, 16);
         }
-    if (pp == 0 && li < nv)
+    if (pp == 0)
 #pragma unroll
         for (int g = 0; g < GMAX; ++g)
-            if (g < G) accs[warp][g][li] = acc[g];
+#pragma unroll
+            for (int k = 0; k < NVL; ++k) {
+                const int c = li + LPP * k;
+                if (g < G && c < nv) accs[warp][g][c] = acc[g][k];
+            }
     __syncthreads();
-    for (int i = tid; i < G * nv; i += 128) {
+    for (int i = tid; i < G * nv; i += ATT_WARPS * 32) {
         const int g = i / nv, l4 = i % nv;
         float4 a = accs[0][g][l4];
 #pragma unroll
-        for (int w = 1; w < 4; ++w) {
+        for (int w = 1; w < ATT_WARPS; ++w) {
             const float4 b = accs[w][g][l4];
             a.x += b.x;
             a.y += b.y;
@@ -467,7 +495,7 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
     if (!is_last) return;
     __threadfence();
     // combine the live splits of this kv head
-    for (int g = warp; g < G; g += 4) {
+    for (int g = warp; g < G; g += ATT_WARPS) {
         const size_t r0 = (size_t)(hk * G + g) * ATT_SPLITS;
         const float2 a = lane < live ? __ldcg(part_ml + r0 + lane) : make_float2(-INFINITY, 0.f);
         const float2 b = lane + 32 < live ? __ldcg(part_ml + r0 + lane + 32)
@@ -481,26 +509,46 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
         if (lane == 0) linv[g] = 1.0f / L;
     }
     __syncthreads();
-    for (int i = tid; i < G * nv; i += 128) {
-        const int g = i / nv, l4 = i % nv;
+    // two threads per output float4, each over half of the splits; the loop runs on
+    // whole warps (every lane reaches the pair shuffle), lanes past the end idle
+    for (int i0 = warp * 32; i0 < 2 * G * nv; i0 += ATT_WARPS * 32) {
+        const int i = i0 + lane;
+        const bool act = i < 2 * G * nv;
+        const int pair = act ? i >> 1 : 0, half = i & 1;
+        const int g = pair / nv, l4 = pair % nv;
         const float4* src = reinterpret_cast<const float4*>(part_acc) +
                             ((size_t)(hk * G + g) * ATT_SPLITS) * nv + l4;
         float4 a = z4;
-        for (int c = 0; c < live; ++c) {
-            const float w = wsp[g][c];
-            const float4 b = __ldcg(src + (size_t)c * nv);
-            a.x = fmaf(w, b.x, a.x);
-            a.y = fmaf(w, b.y, a.y);
-            a.z = fmaf(w, b.z, a.z);
-            a.w = fmaf(w, b.w, a.w);
+        for (int c0 = half; act && c0 < live; c0 += 16) {
+            float4 b[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + 2 * u;
+                b[u] = c < live ? __ldcg(src + (size_t)c * nv) : z4;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + 2 * u;
+                const float w = c < live ? wsp[g][c] : 0.f;
+                a.x = fmaf(w, b[u].x, a.x);
+                a.y = fmaf(w, b[u].y, a.y);
+                a.z = fmaf(w, b[u].z, a.z);
+                a.w = fmaf(w, b[u].w, a.w);
+            }
         }
-        const float inv = linv[g];
-        a.x *= inv;
-        a.y *= inv;
-        a.z *= inv;
-        a.w *= inv;
-        reinterpret_cast<float4*>(out + (size_t)(hk * G + g) * head_dim)[l4] = a;
-        reinterpret_cast<float4*>(ovals + g * head_dim)[l4] = a;
+        a.x += __shfl_xor_sync(0xffffffffu, a.x, 1);
+        a.y += __shfl_xor_sync(0xffffffffu, a.y, 1);
+        a.z += __shfl_xor_sync(0xffffffffu, a.z, 1);
+        a.w += __shfl_xor_sync(0xffffffffu, a.w, 1);
+        if (act && half == 0) {
+            const float inv = linv[g];
+            a.x *= inv;
+            a.y *= inv;
+            a.z *= inv;
+            a.w *= inv;
+            reinterpret_cast<float4*>(out + (size_t)(hk * G + g) * head_dim)[l4] = a;
+            reinterpret_cast<float4*>(ovals + g * head_dim)[l4] = a;
+        }
     }
     if (tid == 0) counters[hk] = 0;
     if (!slab) return;
@@ -509,7 +557,7 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
     const int base_el = hk * n_el;
     if (slab_kq) {
         constexpr int GS = SlabG<true>::GS;
-        for (int gl = warp; gl < n_el / GS; gl += 4) {
+        for (int gl = warp; gl < n_el / GS; gl += ATT_WARPS) {
             float v[GS / 32];
 #pragma unroll
             for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
@@ -517,7 +565,7 @@ __global__ void __launch_bounds__(128) attn_fused_kernel(
         }
     } else {
         constexpr int GS = SlabG<false>::GS;
-        for (int gl = warp; gl < n_el / GS; gl += 4) {
+        for (int gl = warp; gl < n_el / GS; gl += ATT_WARPS) {
             float v[GS / 32];
 #pragma unroll
             for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
@@ -549,7 +597,7 @@ int attention_decode_fused(const float* q, const float* kc, const float* vc, flo
     const dim3 grid(Hkv, ATT_SPLITS);
     auto kern = G <= 1 ? attn_fused_kernel<1> : G <= 2 ? attn_fused_kernel<2> :
                 G <= 4 ? attn_fused_kernel<4> : attn_fused_kernel<8>;
-    IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(128), 0, st, pdl, q, kc, vc, part_acc, part_ml,
+    IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(ATT_WARPS * 32), 0, st, pdl, q, kc, vc, part_acc, part_ml,
                              counters, out, slab, slab_kq ? 1 : 0, H, Hkv, HD, max_seq, scale,
                              pos_dev));
     return IB_OK;
