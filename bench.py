@@ -130,7 +130,9 @@ def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201):
 
 
 def time_gemv(ib, cfg, seed=20261201):
-    """Q4_K GEMV ffn_gate shape over n_layers distinct weight matrices (no L2 reuse)."""
+    """The decode GEMV kernel on the ffn_gate shape (Q4_K), over min(n_layers, 32) distinct
+    weight matrices (larger than L2 together), its limb slab computed once: CUDA-graph
+    replays of the kernel alone, timed with events on the replay stream."""
     import torch
     from inference_cpp_b200 import gguf_writer as gw
     rows, cols = cfg.ffn, cfg.dim
@@ -138,20 +140,34 @@ def time_gemv(ib, cfg, seed=20261201):
     Ws = [ib.synth_device(ib.Q4_K, rows, cols, gw.tensor_seed(seed + 1, f"w{i}"), 0.02) for i in range(n)]
     x = torch.randn(cols, device="cuda")
     y = torch.empty(rows, device="cuda")
-    st = torch.cuda.current_stream()
-    for i in range(3 * n):
-        ib.gemv_q(ib.Q4_K, Ws[i % n], x, rows, cols, y=y)
+    slab = ib.limb_slab(ib.Q4_K, x, cols)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(2 * n):
+            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
+        torch.cuda.nvtx.range_push("gemv_roofline")  # a profiler's capture of this kernel
+        for i in range(n):
+            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 4 * n
-    e0.record(st)
-    for i in range(reps):
-        ib.gemv_q(ib.Q4_K, Ws[i % n], x, rows, cols, y=y)
-    e1.record(st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(reps):
+            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):  # the replay and its events on one stream
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record(s)
+        g.replay()
+        e1.record(s)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     nbytes = ib.packed_nbytes(ib.Q4_K, rows, cols) + 4 * cols + 4 * rows
-    del Ws
+    del g, Ws
     torch.cuda.empty_cache()
     return nbytes, ms, reps
 

@@ -115,6 +115,16 @@ int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float* dev_y, int
 int ib_gemv_q_noalloc(int type, const void* dev_W, const float* dev_x, float* dev_y,
                       int64_t rows, int64_t cols, void* stream);
 
+/* ib_gemv_q in two steps, for an activation shared by several GEMVs: the exact int8
+ * limb split of x ("limb slab", ib_slab_bytes bytes, 16-byte aligned) is computed once
+ * by ib_limb_slab for the weight family of `type` (K-quants or 32-element blocks), and
+ * ib_gemv_q_slab runs the GEMV kernel on it.  No counterpart in the reference (its
+ * GEMV takes FP32 x directly). */
+int ib_slab_bytes(int type, int64_t cols, size_t* bytes);
+int ib_limb_slab(int type, const float* dev_x, int64_t cols, void* dev_slab, void* stream);
+int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y, int64_t rows,
+                   int64_t cols, void* stream);
+
 /* Batched product on packed blocks: Y[T, rows] = X[T, cols] @ W^T.  Replaces
  * gemm / gemm_i16 (include/ops/cuda_backend.hpp:35-38; kernels
  * src/ops/cuda_kernels.cu:279-346). */

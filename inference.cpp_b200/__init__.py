@@ -56,6 +56,9 @@ SIGNATURES = {
     "ib_dequant_i16": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_gemv_q": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_gemv_q_noalloc": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
+    "ib_slab_bytes": [_i, _i64, _vp],
+    "ib_limb_slab": [_i, _vp, _i64, _vp, _vp],
+    "ib_gemv_q_slab": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_gemm_q": [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ib_embedding_q": [_i, _vp, _vp, _vp, _i, _i64, _i64, _vp],
     "ib_gemv": [_vp, _vp, _vp, _i, _i, _vp],
@@ -196,6 +199,25 @@ def gemv_q_noalloc(type_: int, W, x, y, rows: int, cols: int, stream=None):
     """ib_gemv_q with its scratch in a static device array: y must be given (the
     call allocates nothing); cols <= NOALLOC_MAX_COLS."""
     call("ib_gemv_q_noalloc", type_, _ptr(W), _ptr(x), _ptr(y), rows, cols, _stream(stream))
+    return y
+
+
+def limb_slab(type_: int, x, cols: int, slab=None, stream=None):
+    """Exact int8 limb split of x for GEMVs on weights of `type_`'s family."""
+    import torch
+    if slab is None:
+        n = ctypes.c_size_t()
+        call("ib_slab_bytes", type_, cols, ctypes.byref(n))
+        slab = torch.empty(n.value, dtype=torch.uint8, device=x.device)
+    call("ib_limb_slab", type_, _ptr(x), cols, _ptr(slab), _stream(stream))
+    return slab
+
+
+def gemv_q_slab(type_: int, W, slab, rows: int, cols: int, y=None, stream=None):
+    import torch
+    if y is None:
+        y = torch.empty(rows, dtype=torch.float32, device=W.device)
+    call("ib_gemv_q_slab", type_, _ptr(W), _ptr(slab), _ptr(y), rows, cols, _stream(stream))
     return y
 
 

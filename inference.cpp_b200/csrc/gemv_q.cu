@@ -387,6 +387,49 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     return IB_ERR_UNSUPPORTED;
 }
 
+extern "C" int ib_slab_bytes(int type, int64_t cols, size_t* bytes) {
+    IB_REQUIRE(bytes && cols > 0 && cols <= (1 << 30), "bad arguments");
+    if (!gemv_mma_supported(type)) {
+        set_error(std::string("ib_slab_bytes: unsupported type ") + type_name(type));
+        return IB_ERR_UNSUPPORTED;
+    }
+    *bytes = slab_total_bytes((int)cols, slab_kquant(type));
+    return IB_OK;
+}
+
+extern "C" int ib_limb_slab(int type, const float* dev_x, int64_t cols, void* dev_slab, void* stream) {
+    IB_REQUIRE(dev_x && dev_slab && cols > 0 && cols <= (1 << 30), "bad arguments");
+    IB_REQUIRE(((uintptr_t)dev_slab & 15) == 0, "slab must be 16-byte aligned");
+    if (!gemv_mma_supported(type)) {
+        set_error(std::string("ib_limb_slab: unsupported type ") + type_name(type));
+        return IB_ERR_UNSUPPORTED;
+    }
+    IB_REQUIRE(cols % block_elems(type) == 0, "cols must be a multiple of the block size");
+    return xq_slab_launch(dev_x, nullptr, (int)cols, slab_kquant(type), (uint8_t*)dev_slab,
+                          nullptr, as_stream(stream), false);
+}
+
+extern "C" int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y,
+                              int64_t rows, int64_t cols, void* stream) {
+    if (rows == 0) return IB_OK;
+    IB_REQUIRE(dev_W && dev_slab && dev_y && rows > 0 && cols > 0, "bad arguments");
+    IB_REQUIRE(cols <= (1 << 30) && rows < (1ll << 31), "bad GEMV shape");
+    FusedGemv f = {};
+    f.W[0] = (const uint8_t*)dev_W;
+    f.type[0] = type;
+    f.rows[0] = (int)rows;
+    f.n_seg = 1;
+    f.K = (int)cols;
+    f.y = dev_y;
+    f.slab = (const uint8_t*)dev_slab;
+    if (!fused_gemv_supported(f, EPI_STORE)) {
+        set_error("ib_gemv_q_slab: type, shape or alignment (16 bytes for W and the slab) "
+                  "not supported");
+        return IB_ERR_UNSUPPORTED;
+    }
+    return fused_gemv_launch(f, PRO_PLAIN, EPI_STORE, as_stream(stream), false);
+}
+
 extern "C" int ib_gemv(const float* W, const float* x, float* y, int M, int N, void* stream) {
     if (M == 0) return IB_OK;
     IB_REQUIRE(W && x && y && M > 0 && N > 0, "bad gemv arguments");

@@ -159,3 +159,23 @@ def test_bad_arguments_raise(cuda):
         ib.gemv_q(3, z, x, 2, 256)  # Q4_1 is not implemented, as in the reference
     with pytest.raises(RuntimeError):
         ib.dequantize(13, z, 1, 256)  # Q5_K
+
+
+@pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
+def test_gemv_q_slab_two_step(cuda, type_):
+    """ib_limb_slab + ib_gemv_q_slab (one slab shared by two weight matrices) agree with
+    the float64 product within the GEMV bound."""
+    torch = cuda
+    for rows, cols in [(64, 512), (4096, 4096), (1000, 14336)]:
+        if cols % ib.BLOCK_ELEMS[type_]:
+            continue
+        x = torch.randn(cols, device="cuda", dtype=torch.float32)
+        slab = ib.limb_slab(type_, x, cols)
+        for k in range(2):
+            blk = ib.synth_device(type_, rows, cols, seed=7000 + 31 * k + rows + type_)
+            y = ib.gemv_q_slab(type_, blk, slab, rows, cols)
+            W = ib.dequantize(type_, blk, rows, cols).view(rows, cols).double()
+            bound = GEMV_RTOL * (W.abs() @ x.double().abs()) + 1e-30
+            assert bool(((y.double() - W @ x.double()).abs() <= bound).all()), (rows, cols, k)
+    with pytest.raises(RuntimeError):
+        ib.limb_slab(ib.F32, torch.zeros(64, device="cuda"), 64)
