@@ -243,6 +243,42 @@ __device__ __forceinline__ void finish_group(const FusedGemv& p, float (*r)[16],
     acc_b = 0.f;
 }
 
+// finish_group with bounded mbarrier handshakes instead of a named barrier (the TMA
+// kernel's consumer warps leave their loop independently after a failed wait):
+// every warp posts its partials to red[b] and arrives on rfull[b]; warp 0 waits, reduces,
+// runs the epilogue and frees the buffer on rfree[b]; a warp reusing red[b] (two row
+// groups later) first waits for that free.  Use u = rgl >> 1 of buffer b = rgl & 1.
+template <int EPI>
+__device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*red)[kNWC][16],
+                                                  uint64_t* rfull, uint64_t* rfree, int rgl,
+                                                  int rg, int warp, int lane, const LaneCtx& c,
+                                                  float rms, float& acc_a, float& acc_b) {
+    const int b = rgl & 1, u = rgl >> 1;
+    acc_a = quad_sum(acc_a);
+    acc_b = quad_sum(acc_b);
+    if (warp != 0 && u > 0 && !mbar_wait(&rfree[b], (u - 1) & 1, &g_decode_fault, 15))
+        return false;
+    if (c.t == 0) {
+        red[b][warp][c.g] = acc_a;
+        red[b][warp][c.g + 8] = acc_b;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfull[b]);
+    acc_a = 0.f;
+    acc_b = 0.f;
+    if (warp != 0) return true;
+    if (!mbar_wait(&rfull[b], u & 1, &g_decode_fault, 16)) return false;
+    float v = 0.f;
+    if (lane < 16) {
+#pragma unroll
+        for (int w = 0; w < kNWC; ++w) v += red[b][w][lane];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rfree[b]);
+    epilogue<EPI>(p, rg, lane, v / rms);
+    return true;
+}
+
 // One stage (KB blocks of the 16 tile rows; limb slice at `slab`) for this warp's
 // share of the blocks.
 template <int TYPE, int KB, int SE, int GS>
@@ -282,35 +318,50 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     fused_tma_kernel(const FusedGemv p, int S, int slot_a, int slot_b, int wbytes) {
     using P = Pair<TA, TB>;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], rfull[2], rfree[2];
+    __shared__ int stage_rg[kMaxStages];
+    __shared__ int warps_done;
     __shared__ float red[2][kNWC][16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = p.K / P::BE;
     const int spg = nb / P::KB;
     const int stage_bytes = wbytes + P::SLICE;
     const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
-    const int my_rg = (int)blockIdx.x < n_rg ? (n_rg - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kNWC);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&rfull[b], kNWC);
+            mbar_init(&rfree[b], 1);
+        }
+        warps_done = 0;
         fence_mbar_init();
     }
     __syncthreads();
     pdl_launch_dependents();
     if (warp == kNWC) {
-        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Stage slot s
-        // and its phase advance incrementally (no divisions in the loop).
+        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Row groups come
+        // from the work counter (or the static stride); stage_rg[s] tells the consumers
+        // which row group a stage holds, -1 ends their loop.  Stage slot s and its phase
+        // advance incrementally (no divisions in the loop).
         auto limbs = [&](int slot_s, int st) {
             if (lane == 16)
                 bulk_g2s(smem + (size_t)slot_s * stage_bytes + wbytes,
                          p.slab + (size_t)st * P::SLICE, (uint32_t)P::SLICE, &full[slot_s]);
         };
-        int s = 0, ph = 0, it = 0;
+        int s = 0, ph = 0, it = 0, k = 0;
         bool waited = false, ok = true;
-        for (int rgl = 0; rgl < my_rg && ok; ++rgl) {
-            const int rg = blockIdx.x + rgl * gridDim.x;
+        for (;;) {
+            int rg = (int)blockIdx.x + k * (int)gridDim.x;
+            if (p.work) {
+                int r = 0;
+                if (lane == 0) r = atomicAdd(p.work, 1);
+                rg = __shfl_sync(0xffffffffu, r, 0);
+            }
+            ++k;
+            if (rg >= n_rg) break;
             const bool isb = group_is_b<TA, TB>(p, rg);
             const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
             const int chunk = P::KB * bb;
@@ -327,7 +378,10 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                     ok = false;
                     break;
                 }
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
+                if (lane == 0) {
+                    stage_rg[s] = rg;
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
+                }
                 __syncwarp();
                 if (lane < n)
                     bulk_g2s(smem + (size_t)s * stage_bytes + (size_t)lane * slot,
@@ -346,13 +400,20 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                     ph ^= 1;
                 }
             }
+            if (!ok) break;
         }
         if (!waited) {
             pdl_wait();
             for (int j = 0; j < it; ++j) limbs(j, j % spg);
         }
-        for (int j = it > S ? it - S : 0; j < it; ++j)  // no copy may land after exit
+        // every issued copy lands before the CTA can exit
+        for (int j = it > S ? it - S : 0; j < it; ++j)
             mbar_wait(&full[j % S], (j / S) & 1, &g_decode_fault, 12);
+        // end-of-work sentinel in the next slot (once the consumers have released it)
+        if (ok && (it < S || mbar_wait(&empty[s], ph ^ 1, &g_decode_fault, 14)) && lane == 0) {
+            stage_rg[s] = -1;
+            mbar_arrive(&full[s]);
+        }
         return;
     }
     pdl_wait();
@@ -360,25 +421,28 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     const LaneCtx c = lane_ctx();
     const LeanLane ll = lean_lane(c);
     float acc_a = 0.f, acc_b = 0.f;
+    int s = 0, ph = 0, rgl = 0;
     bool ok = true;
-    int s = 0, ph = 0;
-    for (int rgl = 0; rgl < my_rg; ++rgl) {
-        const int rg = blockIdx.x + rgl * gridDim.x;
+    while (ok) {
+        if (!mbar_wait(&full[s], ph, &g_decode_fault, 13)) break;
+        const int rg = stage_rg[s];
+        if (rg < 0) break;
         const bool isb = group_is_b<TA, TB>(p, rg);
         const int n = group_rows(p, rg);
         const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
         for (int st = 0; st < spg; ++st) {
-            if (ok && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) ok = false;
-            if (ok) {
-                const uint8_t* base = smem + (size_t)s * stage_bytes;
-                const uint8_t* slab = base + wbytes;
-                if (isb)
-                    stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp,
-                                                        acc_a, acc_b);
-                else
-                    stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp,
-                                                        acc_a, acc_b);
+            if (st > 0 && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) {
+                ok = false;
+                break;
             }
+            const uint8_t* base = smem + (size_t)s * stage_bytes;
+            const uint8_t* slab = base + wbytes;
+            if (isb)
+                stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp, acc_a,
+                                                    acc_b);
+            else
+                stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp, acc_a,
+                                                    acc_b);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (++s == S) {
@@ -386,7 +450,17 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                 ph ^= 1;
             }
         }
-        finish_group<EPI>(p, red[rgl & 1], rg, warp, lane, c, rms, acc_a, acc_b);
+        if (!ok) break;
+        if (!finish_group_mbar<EPI>(p, red, rfull, rfree, rgl, rg, warp, lane, c, rms, acc_a,
+                                    acc_b))
+            break;
+        ++rgl;
+    }
+    // the last consumer warp of the last CTA out resets the work counters
+    if (p.work && lane == 0 && atomicAdd(&warps_done, 1) == kNWC - 1 &&
+        atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+        p.work[0] = 0;
+        p.work[1] = 0;
     }
 }
 
@@ -537,8 +611,9 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
         auto kern = fused_tma_kernel<TA, TB, PRO, EPI>;
         int cap = 0;
         if ((r = max_ctas((const void*)kern, (kNWC + 1) * 32, smem, &cap))) return r;
+        // dynamic schedule: every resident slot claims row groups; static: an even split
         const int per = (n_rg + cap - 1) / cap;
-        const int grid = (n_rg + per - 1) / per;
+        const int grid = p.work ? (n_rg < cap ? n_rg : cap) : (n_rg + per - 1) / per;
         IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3((kNWC + 1) * 32), smem, st, pdl, p, S,
                                  slot_a, slot_b, wbytes));
         return IB_OK;

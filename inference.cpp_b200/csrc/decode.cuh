@@ -67,6 +67,9 @@ struct FusedGemv {
     const int* pos;     // device position of the token
     int head_dim, max_seq;
     unsigned long long* best;  // ARGMAX: max of (ordered logit << 32 | ~row)
+    // optional work counters {next row group, CTAs done}, zero between launches: row
+    // groups are then claimed dynamically (balanced over SMs); null = static schedule
+    int* work;
 };
 
 // Launches the fused GEMV; IB_ERR_UNSUPPORTED when the type mix or shapes have no

@@ -364,9 +364,16 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t a2, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// a * b + c on the FMA pipe (IMAD): the tile math is otherwise bound by the ALU pipe.
+__device__ __forceinline__ uint32_t imad(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
 // Lane constants of the lean tiles (computed once per kernel).
 struct LeanLane {
-    uint32_t bm0, bm1;  // B masks: this lane's limb word goes to K [0,16) (bm0) or [16,32) (bm1)
+    uint32_t bm0, bm1;  // 1 / 0: this lane's limb word goes to K [0,16) (bm0) or [16,32) (bm1)
     uint32_t limb_off;  // byte offset of this lane's limb word inside a 256-element block
     uint32_t sum_off;   // byte offset of this lane's sub-block sum inside a block's sum32 run
     uint32_t sh0, sh1;  // bit position of this lane's 6-bit scale for even / odd pairs
@@ -375,8 +382,8 @@ struct LeanLane {
 
 __device__ __forceinline__ LeanLane lean_lane(const LaneCtx& c) {
     LeanLane l;
-    l.bm0 = c.upper ? 0u : 0xFFFFFFFFu;
-    l.bm1 = ~l.bm0;
+    l.bm0 = c.upper ? 0u : 1u;
+    l.bm1 = 1u - l.bm0;
     l.limb_off = (uint32_t)(c.upper * 128 + c.lim * 32 + 8 * c.t);
     l.sum_off = (uint32_t)(4 * c.half);
     l.sh0 = 8u * c.half;
@@ -412,12 +419,15 @@ __device__ __forceinline__ void q4k_tile_lean(uint32_t wa, uint32_t wb, uint32_t
     float ma = 0.f, mb = 0.f;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        const uint32_t M = 0x0F0F0F0Fu, MH = 0xF0F0F0F0u;
+        const uint32_t M = 0x0F0F0F0Fu;
         int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
-        mma_u8s8(qa[p].x & M, qb[p].x & M, qa[p].x & MH, qb[p].x & MH, lx[p].x & l.bm0,
-                 lx[p].x & l.bm1, d0, d1, d2, d3);
-        mma_u8s8(qa[p].y & M, qb[p].y & M, qa[p].y & MH, qb[p].y & MH, lx[p].y & l.bm0,
-                 lx[p].y & l.bm1, d0, d1, d2, d3);
+        // low nibbles by mask (ALU); high nibbles in place as q - low (IMAD, FMA pipe);
+        // the split-column B words by a 0/1 multiplier (IMAD)
+        const uint32_t ax = qa[p].x & M, bx = qb[p].x & M, ay = qa[p].y & M, by = qb[p].y & M;
+        mma_u8s8(ax, bx, imad(ax, 0xFFFFFFFFu, qa[p].x), imad(bx, 0xFFFFFFFFu, qb[p].x),
+                 imad(lx[p].x, l.bm0, 0u), imad(lx[p].x, l.bm1, 0u), d0, d1, d2, d3);
+        mma_u8s8(ay, by, imad(ay, 0xFFFFFFFFu, qa[p].y), imad(by, 0xFFFFFFFFu, qb[p].y),
+                 imad(lx[p].y, l.bm0, 0u), imad(lx[p].y, l.bm1, 0u), d0, d1, d2, d3);
         const uint32_t sh = (p & 1) ? l.sh1 : l.sh0;
         const int sca = (int)bfe6(p < 2 ? sa_lo : sa_hi, sh);
         const int scb = (int)bfe6(p < 2 ? sb_lo : sb_hi, sh);

@@ -363,6 +363,10 @@ extern "C" int ib_model_finalize(void* h) {
             m->allocations.push_back(*slabs[i]);
         }
         if ((st = alloc_f(m, &m->ssq, (size_t)D / 32 + 1))) return st;
+        const size_t nwork = (size_t)(4 * c.n_layers + 1) * 2;
+        IB_CUDA_CHECK(cudaMalloc(&m->gemv_work, nwork * 4));
+        m->allocations.push_back(m->gemv_work);
+        IB_CUDA_CHECK(cudaMemsetAsync(m->gemv_work, 0, nwork * 4, m->stream));
         if (attention_fused_ok(H, Hkv, HD)) {
             if ((st = alloc_f(m, &m->att_fpart, attention_fused_part_bytes(H, HD) / 4 + 1))) return st;
             IB_CUDA_CHECK(cudaMalloc(&m->att_counters, (size_t)Hkv * 4 + 16));
@@ -499,9 +503,16 @@ static int decode_launches_fused(Model* m) {
     const bool att_slab = m->att_counters && (H / Hkv * HD) % (kq ? 256 : 32) == 0;
     int r;
     if ((r = embed_launch(m))) return r;
+    int* work = m->gemv_work;  // two counters per GEMV call site
     for (auto& L : m->layers) {
+        FusedGemv qkv = fg_qkv(m, L), wo = fg_wo(m, L), fin = fg_ffn_in(m, L), fout = fg_ffn_out(m, L);
+        qkv.work = work;
+        wo.work = work + 2;
+        fin.work = work + 4;
+        fout.work = work + 6;
+        work += 8;
         if ((r = xq_slab_launch(m->x, L.attn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
-        if ((r = fused_gemv_launch(fg_qkv(m, L), PRO_NORM, EPI_QKV, st, true))) return r;
+        if ((r = fused_gemv_launch(qkv, PRO_NORM, EPI_QKV, st, true))) return r;
         if (att_slab) {  // attention writes the wo input's limb slab itself
             if ((r = attention_decode_fused(m->q, L.kc, L.vc, m->att, m->slab_att, kq, H, Hkv, HD,
                                             c.max_seq, scale, m->att_fpart, m->att_counters, st,
@@ -514,14 +525,16 @@ static int decode_launches_fused(Model* m) {
             if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true)))
                 return r;
         }
-        if ((r = fused_gemv_launch(fg_wo(m, L), PRO_PLAIN, EPI_RESID, st, true))) return r;
+        if ((r = fused_gemv_launch(wo, PRO_PLAIN, EPI_RESID, st, true))) return r;
         if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
-        if ((r = fused_gemv_launch(fg_ffn_in(m, L), PRO_NORM, EPI_SWIGLU, st, true))) return r;
+        if ((r = fused_gemv_launch(fin, PRO_NORM, EPI_SWIGLU, st, true))) return r;
         if ((r = xq_slab_launch(m->gate, nullptr, F, kq, m->slab_h, nullptr, st, true))) return r;
-        if ((r = fused_gemv_launch(fg_ffn_out(m, L), PRO_PLAIN, EPI_RESID, st, true))) return r;
+        if ((r = fused_gemv_launch(fout, PRO_PLAIN, EPI_RESID, st, true))) return r;
     }
     if ((r = xq_slab_launch(m->x, m->out_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
-    if ((r = fused_gemv_launch(fg_head(m), PRO_NORM, EPI_ARGMAX, st, true))) return r;
+    FusedGemv head = fg_head(m);
+    head.work = work;
+    if ((r = fused_gemv_launch(head, PRO_NORM, EPI_ARGMAX, st, true))) return r;
     feedback_best_kernel<<<1, 1, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq);
     IB_LAUNCH_CHECK("decode step");
     return IB_OK;

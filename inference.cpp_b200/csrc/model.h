@@ -57,6 +57,7 @@ struct Model {
     bool slab_kq = true;
     uint8_t *slab_x = nullptr, *slab_att = nullptr, *slab_h = nullptr;
     float* ssq = nullptr;
+    int* gemv_work = nullptr;     // fused GEMV work counters, two per call site of a step
     float* att_fpart = nullptr;   // fused attention partials
     int* att_counters = nullptr;  // fused attention: per kv head, zero between steps
     int32_t* dev_tokens = nullptr;  // [max_seq] ids produced by decode steps, by position
