@@ -242,6 +242,32 @@ int ib_model_step_kernels(void* model, int* n_kernels);
 /* Bytes of weights held on the device. */
 int ib_model_weight_bytes(void* model, size_t* bytes);
 
+/* ---- tensor parallelism (no counterpart in the reference, which runs on one GPU) ----
+ * One process per GPU.  Rank 0 creates an id (ib_comm_unique_id), every rank receives
+ * it out of band and calls ib_comm_init.  NCCL (libnccl.so.2) is opened at run time;
+ * without it these calls return IB_ERR_COMM and the rest of the library works. */
+int ib_comm_unique_id(uint8_t* id128);
+int ib_comm_init(int rank, int world, const uint8_t* id128, int device, void** comm);
+/* In-place sum over the ranks (FP32), on `stream`. */
+int ib_comm_allreduce_f32(void* comm, float* dev_buf, int64_t n, void* stream);
+int ib_comm_free(void* comm);
+/* Host-side shard of a packed [rows, cols] tensor: axis 0 = the rank's contiguous
+ * rows/world rows, axis 1 = the rank's contiguous (cols/block)/world blocks of every
+ * row (the split of an input dimension on block boundaries). */
+int ib_tp_shard(int type, const void* host_src, int64_t rows, int64_t cols, int axis, int rank,
+                int world, void* host_dst);
+/* A model whose layers are split over the communicator's ranks (Megatron split):
+ * attn_q/k/v, ffn_gate/up and output rows by head / FFN column / vocabulary row,
+ * attn_output and ffn_down input columns on block boundaries, token_embd and the
+ * norms whole.  cfg and ib_model_set_tensor take the WHOLE model's shapes and
+ * tensors; each rank uploads only its shard.  n_kv_heads, ffn and vocab must divide
+ * by the world size.  Every rank makes the same calls in the same order (prefill,
+ * decode, generate), including the same host_logits null-ness, since the steps hold
+ * collectives; each rank then gets the same ids and logits. */
+int ib_model_create_tp(const ib_model_config* cfg, int device, void* comm, void** model);
+int ib_model_load_gguf_tp(const char* path, int precision, int device, int max_seq, void* comm,
+                          void** model);
+
 /* ---- seeded synthetic weights (test and benchmark data, not a timed path) ---
  * Fills a [rows, cols] tensor of `type` with blocks encoding N(0, std) values
  * drawn from a counter-based stream keyed by `seed`.  The host and device

@@ -59,6 +59,11 @@ SIGNATURES = {
     "ib_slab_bytes": [_i, _i64, _vp],
     "ib_limb_slab": [_i, _vp, _i64, _vp, _vp],
     "ib_gemv_q_slab": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
+    "ib_comm_unique_id": [_vp],
+    "ib_comm_init": [_i, _i, _vp, _i, _vp],
+    "ib_comm_allreduce_f32": [_vp, _vp, _i64, _vp],
+    "ib_comm_free": [_vp],
+    "ib_tp_shard": [_i, _vp, _i64, _i64, _i, _i, _i, _vp],
     "ib_gemm_q": [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ib_embedding_q": [_i, _vp, _vp, _vp, _i, _i64, _i64, _vp],
     "ib_gemv": [_vp, _vp, _vp, _i, _i, _vp],
@@ -221,6 +226,41 @@ def gemv_q_slab(type_: int, W, slab, rows: int, cols: int, y=None, stream=None):
     return y
 
 
+def tp_shard(type_: int, data, rows: int, cols: int, axis: int, rank: int, world: int):
+    """Host shard of a packed [rows, cols] tensor (numpy uint8/float32 array)."""
+    import numpy as np
+    src = np.ascontiguousarray(data)
+    n = packed_nbytes(type_, rows, cols) // world
+    dst = np.empty(n, dtype=np.uint8)
+    call("ib_tp_shard", type_, src.ctypes.data, rows, cols, axis, rank, world, dst.ctypes.data)
+    return dst
+
+
+class Comm:
+    """NCCL communicator for tensor parallelism (one process per GPU)."""
+
+    def __init__(self, rank: int, world: int, uid: bytes, device: int = 0):
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        h = ctypes.c_void_p()
+        call("ib_comm_init", rank, world, buf, device, ctypes.byref(h))
+        self.h, self.rank, self.world = h, rank, world
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        call("ib_comm_unique_id", buf)
+        return bytes(buf)
+
+    def allreduce(self, t, stream=None):
+        call("ib_comm_allreduce_f32", self.h, _ptr(t), t.numel(), _stream(stream))
+        return t
+
+    def close(self):
+        if self.h:
+            call("ib_comm_free", self.h)
+            self.h = None
+
+
 def gemm_q(type_: int, W, X, T: int, rows: int, cols: int, Y=None, stream=None):
     import torch
     if Y is None:
@@ -377,6 +417,8 @@ class GenerationStats(ctypes.Structure):
 
 SIGNATURES.update({
     "ib_model_create": [_vp, _i, _vp],
+    "ib_model_create_tp": [_vp, _i, _vp, _vp],
+    "ib_model_load_gguf_tp": [_c.c_char_p, _i, _i, _i, _vp, _vp],
     "ib_model_set_tensor": [_vp, _c.c_char_p, _i, _i64, _i64, _vp, _i],
     "ib_model_finalize": [_vp],
     "ib_model_load_gguf": [_c.c_char_p, _i, _i, _i, _vp],
@@ -402,27 +444,37 @@ class Model:
         self.vocab = vocab
 
     @classmethod
-    def create(cls, cfg, precision: int = NATIVE, device: int = 0, max_seq: int | None = None):
+    def create(cls, cfg, precision: int = NATIVE, device: int = 0, max_seq: int | None = None,
+               comm: "Comm | None" = None):
+        """comm: split the model over the communicator's ranks (tensor parallelism)."""
         c = ModelConfig(cfg.n_layers, cfg.dim, cfg.n_heads, cfg.n_kv_heads, cfg.ffn, cfg.vocab,
                         max_seq or cfg.ctx, cfg.rope_theta, cfg.rms_eps, precision)
         h = ctypes.c_void_p()
-        call("ib_model_create", ctypes.byref(c), device, ctypes.byref(h))
+        if comm is None:
+            call("ib_model_create", ctypes.byref(c), device, ctypes.byref(h))
+        else:
+            call("ib_model_create_tp", ctypes.byref(c), device, comm.h, ctypes.byref(h))
         return cls(h.value, cfg.vocab)
 
     @classmethod
     def from_tensors(cls, cfg, tensors: dict, precision: int = NATIVE, device: int = 0,
-                     max_seq: int | None = None):
+                     max_seq: int | None = None, comm: "Comm | None" = None):
         """tensors: {gguf name: (type, rows, cols, numpy bytes or CUDA tensor)}."""
-        m = cls.create(cfg, precision, device, max_seq)
+        m = cls.create(cfg, precision, device, max_seq, comm)
         for name, (t, r, c, data) in tensors.items():
             m.set_tensor(name, t, r, c, data)
         m.finalize()
         return m
 
     @classmethod
-    def from_gguf(cls, path: str, precision: int = NATIVE, device: int = 0, max_seq: int = 0):
+    def from_gguf(cls, path: str, precision: int = NATIVE, device: int = 0, max_seq: int = 0,
+                  comm: "Comm | None" = None):
         h = ctypes.c_void_p()
-        call("ib_model_load_gguf", path.encode(), precision, device, max_seq, ctypes.byref(h))
+        if comm is None:
+            call("ib_model_load_gguf", path.encode(), precision, device, max_seq, ctypes.byref(h))
+        else:
+            call("ib_model_load_gguf_tp", path.encode(), precision, device, max_seq, comm.h,
+                 ctypes.byref(h))
         from .gguf_writer import _read_vocab  # type: ignore
         return cls(h.value, _read_vocab(path))
 

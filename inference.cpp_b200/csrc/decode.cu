@@ -202,7 +202,8 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
             if (!(v != v)) {  // NaN never wins (the argmax kernel compares with >)
                 const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
                 const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-                key = ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)R);
+                key = ((unsigned long long)o << 32) |
+                      (unsigned long long)(0xFFFFFFFFu - (uint32_t)(p.row_base + R));
             }
         }
 #pragma unroll

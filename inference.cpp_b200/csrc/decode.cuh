@@ -66,7 +66,8 @@ struct FusedGemv {
     const float* rope;  // [max_seq][head_dim / 2][cos, sin]
     const int* pos;     // device position of the token
     int head_dim, max_seq;
-    unsigned long long* best;  // ARGMAX: max of (ordered logit << 32 | ~row)
+    unsigned long long* best;  // ARGMAX: max of (ordered logit << 32 | ~(row_base + row))
+    int row_base;              // ARGMAX: global index of this kernel's first row
     // optional work counters {next row group, CTAs done}, zero between launches: row
     // groups are then claimed dynamically (balanced over SMs); null = static schedule
     int* work;

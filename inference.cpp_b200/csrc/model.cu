@@ -20,6 +20,7 @@
 #include <string>
 #include <vector>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "decode.cuh"
 #include "gguf_reader.h"
@@ -61,6 +62,32 @@ __global__ void feedback_best_kernel(unsigned long long* best, int32_t* dev_i32,
 __global__ void add_vec_kernel(float* __restrict__ a, const float* __restrict__ b, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         a[i] += b[i];
+}
+
+// The output head as this rank sees it: its vocabulary rows (the tied embedding's rows
+// through a non-owning view under tensor parallelism).
+static const Linear& head_linear(const Model* m) {
+    if (m->has_output) return m->out;
+    return m->tp_size > 1 ? m->head_view : m->tok;
+}
+
+// Residual update after a row-split projection: rank 0 adds its partial to x, the other
+// ranks store theirs, and the allreduce then leaves x + sum of partials on every rank.
+static int tp_residual(Model* m, float* x, const float* part, size_t n, cudaStream_t st) {
+    if (m->tp_rank == 0) {
+        const int g = (int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+        add_vec_kernel<<<g, 256, 0, st>>>(x, part, (int)n);
+        IB_LAUNCH_CHECK("add_vec_kernel");
+    } else {
+        IB_CUDA_CHECK(cudaMemcpyAsync(x, part, n * 4, cudaMemcpyDeviceToDevice, st));
+    }
+    return comm_allreduce_sum_f32(m->comm, x, n, st);
+}
+
+// logits (vocab) <- every rank's head rows; a copy without tensor parallelism.
+static int gather_logits(Model* m, cudaStream_t st) {
+    if (m->tp_size == 1) return IB_OK;
+    return comm_allgather_f32(m->comm, m->logits_local, m->logits, (size_t)m->vocab_local, st);
 }
 
 static double now_ms() {
@@ -116,25 +143,49 @@ Model::~Model() {
 
 using namespace ib;
 
+// Uploads this rank's shard of a [rows, cols] tensor: axis -1 whole, 0 = the rank's
+// rows/tp_size rows, 1 = the rank's cols/tp_size columns of every row (whole blocks).
 static int set_linear(Model* m, Linear& L, int type, int64_t rows, int64_t cols,
-                      const void* data, int on_device) {
+                      const void* data, int on_device, int axis = -1) {
     if (!is_block_quant(type) && type != IB_TYPE_F32 && type != IB_TYPE_F16) {
         set_error(std::string("model: unsupported tensor type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }
+    const int N = m->tp_size, rk = m->tp_rank;
+    const int64_t be = is_block_quant(type) ? block_elems(type) : 1;
+    const int64_t eb = is_block_quant(type) ? block_bytes(type) : (type == IB_TYPE_F32 ? 4 : 2);
+    const int64_t row_bytes = cols / be * eb;
+    int64_t lrows = rows, lcols = cols, off = 0;
+    if (N > 1 && axis == 0) {
+        if (rows % N) {
+            set_error("model: tensor rows not divisible by the tensor-parallel size");
+            return IB_ERR_INVALID;
+        }
+        lrows = rows / N;
+        off = lrows * rk * row_bytes;
+    } else if (N > 1 && axis == 1) {
+        if ((cols / be) % N) {
+            set_error("model: tensor blocks per row not divisible by the tensor-parallel size");
+            return IB_ERR_INVALID;
+        }
+        lcols = cols / N;
+        off = lcols / be * eb * rk;
+    }
+    const int64_t lrow_bytes = lcols / be * eb;
     L.release();
     L.type = type;
-    L.rows = rows;
-    L.cols = cols;
-    const int64_t nbytes = type == IB_TYPE_F32   ? rows * cols * 4
-                           : type == IB_TYPE_F16 ? rows * cols * 2
-                                                 : packed_bytes(type, rows, cols);
+    L.rows = lrows;
+    L.cols = lcols;
+    rows = lrows;
+    cols = lcols;
+    const int64_t nbytes = lrows * lrow_bytes;
     void* dev = nullptr;
     // +16 so 16-byte vector loads of the last block never leave the allocation
     IB_CUDA_CHECK(cudaMalloc(&dev, (size_t)nbytes + 16));
-    IB_CUDA_CHECK(cudaMemcpyAsync(dev, data, (size_t)nbytes,
-                                  on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                                  m->stream));
+    IB_CUDA_CHECK(cudaMemcpy2DAsync(dev, (size_t)lrow_bytes, (const uint8_t*)data + off,
+                                    (size_t)row_bytes, (size_t)lrow_bytes, (size_t)lrows,
+                                    on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                    m->stream));
     const bool packed_ok = is_block_quant(type) && m->cfg.precision == IB_PRECISION_NATIVE;
     if (packed_ok) {
         L.repr = REPR_PACKED;
@@ -191,7 +242,7 @@ static int set_vector(Model* m, float** dst, int type, int64_t n, const void* da
     return IB_ERR_UNSUPPORTED;
 }
 
-extern "C" int ib_model_create(const ib_model_config* cfg, int device, void** out) {
+static int model_create(const ib_model_config* cfg, int device, Comm* comm, void** out) {
     IB_REQUIRE(cfg && out, "null pointer argument");
     *out = nullptr;
     IB_REQUIRE(cfg->n_layers >= 0 && cfg->dim > 0 && cfg->n_heads > 0 && cfg->n_kv_heads > 0 &&
@@ -200,16 +251,37 @@ extern "C" int ib_model_create(const ib_model_config* cfg, int device, void** ou
                "model: invalid configuration");
     IB_REQUIRE(cfg->precision >= 0 && cfg->precision <= 2, "model: precision must be 0, 1 or 2");
     IB_REQUIRE((cfg->dim / cfg->n_heads) % 2 == 0, "model: head_dim must be even");
+    const int N = comm_world(comm);
+    IB_REQUIRE(cfg->n_kv_heads % N == 0 && cfg->ffn % N == 0 && cfg->vocab % N == 0,
+               "model: n_kv_heads, ffn and vocab must be divisible by the tensor-parallel size");
     int st = ib_init(device);
     if (st != IB_OK) return st;
     auto m = std::make_unique<Model>();
+    m->full = *cfg;
     m->cfg = *cfg;
+    m->cfg.n_heads = cfg->n_heads / N;
+    m->cfg.n_kv_heads = cfg->n_kv_heads / N;
+    m->cfg.ffn = cfg->ffn / N;
+    m->comm = comm;
+    m->tp_size = N;
+    m->tp_rank = comm_rank(comm);
+    m->vocab_local = cfg->vocab / N;
+    m->vocab_base = m->vocab_local * m->tp_rank;
     m->device = device;
     m->HD = cfg->dim / cfg->n_heads;
     IB_CUDA_CHECK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     m->layers.resize(cfg->n_layers);
     *out = m.release();
     return IB_OK;
+}
+
+extern "C" int ib_model_create(const ib_model_config* cfg, int device, void** out) {
+    return model_create(cfg, device, nullptr, out);
+}
+
+extern "C" int ib_model_create_tp(const ib_model_config* cfg, int device, void* comm, void** out) {
+    IB_REQUIRE(comm, "null communicator");
+    return model_create(cfg, device, (Comm*)comm, out);
 }
 
 extern "C" int ib_model_free(void* h) {
@@ -228,7 +300,7 @@ extern "C" int ib_model_set_tensor(void* h, const char* name, int type, int64_t 
     IB_CUDA_CHECK(cudaSetDevice(m->device));
     IB_REQUIRE(!m->finalized, "model: tensors cannot change after finalize");
     const std::string n(name);
-    const auto& c = m->cfg;
+    const auto& c = m->full;  // shapes are checked against the whole model
     const int D = c.dim, HD = m->HD;
     auto expect = [&](int64_t r, int64_t cc) -> int {
         if (rows != r || cols != cc) {
@@ -247,7 +319,7 @@ extern "C" int ib_model_set_tensor(void* h, const char* name, int type, int64_t 
     if (n == "output.weight") {
         if ((st = expect(c.vocab, D))) return st;
         m->has_output = true;
-        return set_linear(m, m->out, type, rows, cols, data, on_device);
+        return set_linear(m, m->out, type, rows, cols, data, on_device, 0);
     }
     if (n == "output_norm.weight") {
         if ((st = expect(1, D))) return st;
@@ -261,13 +333,13 @@ extern "C" int ib_model_set_tensor(void* h, const char* name, int type, int64_t 
     }
     Layer& L = m->layers[l];
     const std::string k(kind);
-    if (k == "attn_q") { if ((st = expect((int64_t)c.n_heads * HD, D))) return st; return set_linear(m, L.wq, type, rows, cols, data, on_device); }
-    if (k == "attn_k") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wk, type, rows, cols, data, on_device); }
-    if (k == "attn_v") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wv, type, rows, cols, data, on_device); }
-    if (k == "attn_output") { if ((st = expect(D, (int64_t)c.n_heads * HD))) return st; return set_linear(m, L.wo, type, rows, cols, data, on_device); }
-    if (k == "ffn_gate") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w1, type, rows, cols, data, on_device); }
-    if (k == "ffn_down") { if ((st = expect(D, c.ffn))) return st; return set_linear(m, L.w2, type, rows, cols, data, on_device); }
-    if (k == "ffn_up") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w3, type, rows, cols, data, on_device); }
+    if (k == "attn_q") { if ((st = expect((int64_t)c.n_heads * HD, D))) return st; return set_linear(m, L.wq, type, rows, cols, data, on_device, 0); }
+    if (k == "attn_k") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wk, type, rows, cols, data, on_device, 0); }
+    if (k == "attn_v") { if ((st = expect((int64_t)c.n_kv_heads * HD, D))) return st; return set_linear(m, L.wv, type, rows, cols, data, on_device, 0); }
+    if (k == "attn_output") { if ((st = expect(D, (int64_t)c.n_heads * HD))) return st; return set_linear(m, L.wo, type, rows, cols, data, on_device, 1); }
+    if (k == "ffn_gate") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w1, type, rows, cols, data, on_device, 0); }
+    if (k == "ffn_down") { if ((st = expect(D, c.ffn))) return st; return set_linear(m, L.w2, type, rows, cols, data, on_device, 1); }
+    if (k == "ffn_up") { if ((st = expect(c.ffn, D))) return st; return set_linear(m, L.w3, type, rows, cols, data, on_device, 0); }
     if (k == "attn_norm") { if ((st = expect(1, D))) return st; return set_vector(m, &L.attn_norm, type, D, data, on_device); }
     if (k == "ffn_norm") { if ((st = expect(1, D))) return st; return set_vector(m, &L.ffn_norm, type, D, data, on_device); }
     set_error("model: unknown tensor " + n);
@@ -374,6 +446,26 @@ extern "C" int ib_model_finalize(void* h) {
             IB_CUDA_CHECK(cudaMemsetAsync(m->att_counters, 0, (size_t)Hkv * 4 + 16, m->stream));
         }
     }
+    // the head rows of this rank: logits_local; the full logits are gathered on demand
+    if (m->tp_size > 1) {
+        if ((st = alloc_f(m, &m->logits_local, (size_t)m->vocab_local))) return st;
+        if (!m->has_output) {  // tied embedding: a view of this rank's rows of the table
+            Linear& hv = m->head_view;
+            const Linear& t = m->tok;
+            hv = Linear();
+            hv.repr = t.repr;
+            hv.type = t.type;
+            hv.rows = m->vocab_local;
+            hv.cols = t.cols;
+            const int64_t vb = m->vocab_base;
+            if (t.w) hv.w = (uint8_t*)t.w + vb * packed_bytes(t.type, 1, t.cols);
+            if (t.q) hv.q = t.q + vb * t.cols;
+            if (t.s) hv.s = t.s + vb;
+            if (t.f) hv.f = t.f + vb * t.cols;
+        }
+    } else {
+        m->logits_local = m->logits;
+    }
     m->fused_ok = fused_supported(m);
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
     IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
@@ -453,18 +545,19 @@ static FusedGemv fg_ffn_out(const Model* m, const Layer& L) {
 
 static FusedGemv fg_head(const Model* m) {
     FusedGemv p = fg_common(m);
-    fg_seg(p, 0, m->has_output ? m->out : m->tok);
+    fg_seg(p, 0, head_linear(m));
     p.K = m->cfg.dim;
     p.slab = m->slab_x;
     p.ssq = m->ssq;
-    p.y = m->logits;
+    p.y = m->logits_local;
+    p.row_base = m->vocab_base;
     p.best = m->best;
     return p;
 }
 
 bool fused_supported(const Model* m) {
     const auto& c = m->cfg;
-    const Linear& O = m->has_output ? m->out : m->tok;
+    const Linear& O = head_linear(m);
     const int GS = m->slab_kq ? 256 : 32;
     if (c.dim % GS || c.ffn % GS || (c.n_heads * m->HD) % GS) return false;
     if (O.repr != REPR_PACKED || slab_kquant(O.type) != m->slab_kq ||
@@ -501,6 +594,8 @@ static int decode_launches_fused(Model* m) {
     const int* pos = m->dev_i32 + 1;
     const float scale = 1.0f / sqrtf((float)HD);
     const bool att_slab = m->att_counters && (H / Hkv * HD) % (kq ? 256 : 32) == 0;
+    // row-split projections: rank 0 adds the residual, the others store, then allreduce
+    const int resid = m->tp_rank == 0 ? EPI_RESID : EPI_STORE;
     int r;
     if ((r = embed_launch(m))) return r;
     int* work = m->gemv_work;  // two counters per GEMV call site
@@ -525,16 +620,19 @@ static int decode_launches_fused(Model* m) {
             if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true)))
                 return r;
         }
-        if ((r = fused_gemv_launch(wo, PRO_PLAIN, EPI_RESID, st, true))) return r;
+        if ((r = fused_gemv_launch(wo, PRO_PLAIN, resid, st, true))) return r;
+        if ((r = comm_allreduce_sum_f32(m->comm, m->x, D, st))) return r;
         if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
         if ((r = fused_gemv_launch(fin, PRO_NORM, EPI_SWIGLU, st, true))) return r;
         if ((r = xq_slab_launch(m->gate, nullptr, F, kq, m->slab_h, nullptr, st, true))) return r;
-        if ((r = fused_gemv_launch(fout, PRO_PLAIN, EPI_RESID, st, true))) return r;
+        if ((r = fused_gemv_launch(fout, PRO_PLAIN, resid, st, true))) return r;
+        if ((r = comm_allreduce_sum_f32(m->comm, m->x, D, st))) return r;
     }
     if ((r = xq_slab_launch(m->x, m->out_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
     FusedGemv head = fg_head(m);
     head.work = work;
     if ((r = fused_gemv_launch(head, PRO_NORM, EPI_ARGMAX, st, true))) return r;
+    if ((r = comm_allreduce_max_u64(m->comm, m->best, 1, st))) return r;
     feedback_best_kernel<<<1, 1, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq);
     IB_LAUNCH_CHECK("decode step");
     return IB_OK;
@@ -551,7 +649,6 @@ static int decode_launches(Model* m) {
     const float scale = 1.0f / sqrtf((float)HD);
     int r;
     if ((r = embed_launch(m))) return r;
-    const int g_add = (D + 255) / 256 < 1184 ? (D + 255) / 256 : 1184;
     const int g_ffn = (F + 255) / 256 < 1184 ? (F + 255) / 256 : 1184;
     for (auto& L : m->layers) {
         if ((r = rmsnorm_launch(m->x, L.attn_norm, m->xn, 1, D, c.rms_eps, st))) return r;
@@ -564,17 +661,17 @@ static int decode_launches(Model* m) {
                                   m->att_part, st, pos)))
             return r;
         if ((r = L.wo.forward(m->att, m->proj, st))) return r;
-        add_vec_kernel<<<g_add, 256, 0, st>>>(m->x, m->proj, D);
+        if ((r = tp_residual(m, m->x, m->proj, D, st))) return r;
         if ((r = rmsnorm_launch(m->x, L.ffn_norm, m->xn, 1, D, c.rms_eps, st))) return r;
         if ((r = L.w1.forward(m->xn, m->gate, st))) return r;
         if ((r = L.w3.forward(m->xn, m->up, st))) return r;
         silu_mul_kernel<<<g_ffn, 256, 0, st>>>(m->gate, m->up, F);
         if ((r = L.w2.forward(m->gate, m->proj, st))) return r;
-        add_vec_kernel<<<g_add, 256, 0, st>>>(m->x, m->proj, D);
+        if ((r = tp_residual(m, m->x, m->proj, D, st))) return r;
     }
     if ((r = rmsnorm_launch(m->x, m->out_norm, m->xn, 1, D, c.rms_eps, st))) return r;
-    const Linear& O = m->has_output ? m->out : m->tok;
-    if ((r = O.forward(m->xn, m->logits, st))) return r;
+    if ((r = head_linear(m).forward(m->xn, m->logits_local, st))) return r;
+    if ((r = gather_logits(m, st))) return r;
     if ((r = argmax_launch(m->logits, V, m->dev_i32 + 2, st))) return r;
     feedback_kernel<<<1, 1, 0, st>>>(m->dev_i32, m->dev_tokens, c.max_seq);
     IB_LAUNCH_CHECK("decode step");
@@ -611,9 +708,13 @@ int decode_step(Model* m, int token, int pos, float* host_logits, int* next) {
         return r;
     }
     IB_CUDA_CHECK(cudaMemcpyAsync(hp + 2, m->dev_i32 + 2, 4, cudaMemcpyDeviceToHost, m->stream));
-    if (host_logits)
+    if (host_logits) {
+        // the fused step keeps each rank's head rows local; gather them here (every rank
+        // asks for logits on the same steps, so the collective matches)
+        if (m->use_fused && m->fused_ok && (r = gather_logits(m, m->stream))) return r;
         IB_CUDA_CHECK(cudaMemcpyAsync(host_logits, m->logits, (size_t)m->cfg.vocab * 4,
                                       cudaMemcpyDeviceToHost, m->stream));
+    }
     IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
     if (next) *next = hp[2];
     return IB_OK;
@@ -673,18 +774,18 @@ int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_log
                                         T, scale, st)))
             return r;
         if ((r = L.wo.forward_batch(m->pf_att, m->pf_proj, T, st))) return r;
-        if ((r = elementwise_launch(2, m->pf_x, m->pf_proj, T * D, st))) return r;
+        if ((r = tp_residual(m, m->pf_x, m->pf_proj, (size_t)T * D, st))) return r;
         if ((r = rmsnorm_launch(m->pf_x, L.ffn_norm, m->pf_xn, T, D, c.rms_eps, st))) return r;
         if ((r = L.w1.forward_batch(m->pf_xn, m->pf_gate, T, st))) return r;
         if ((r = L.w3.forward_batch(m->pf_xn, m->pf_up, T, st))) return r;
         silu_mul_kernel<<<1184, 256, 0, st>>>(m->pf_gate, m->pf_up, T * F);
         if ((r = L.w2.forward_batch(m->pf_gate, m->pf_proj, T, st))) return r;
-        if ((r = elementwise_launch(2, m->pf_x, m->pf_proj, T * D, st))) return r;
+        if ((r = tp_residual(m, m->pf_x, m->pf_proj, (size_t)T * D, st))) return r;
     }
     // logits of the last prompt position only (model_cuda.cpp:394-398)
     if ((r = rmsnorm_launch(m->pf_x + (size_t)(T - 1) * D, m->out_norm, m->xn, 1, D, c.rms_eps, st))) return r;
-    const Linear& O = m->has_output ? m->out : m->tok;
-    if ((r = O.forward(m->xn, m->logits, st))) return r;
+    if ((r = head_linear(m).forward(m->xn, m->logits_local, st))) return r;
+    if ((r = gather_logits(m, st))) return r;
     if ((r = argmax_launch(m->logits, V, m->dev_i32 + 2, st))) return r;
     int* hp = (int*)m->host_pinned;
     IB_CUDA_CHECK(cudaMemcpyAsync(hp + 2, m->dev_i32 + 2, 4, cudaMemcpyDeviceToHost, st));
@@ -855,8 +956,8 @@ extern "C" int ib_model_generate(void* h, const int32_t* prompt, int n_prompt, i
 
 // Loads a GGUF file: metadata keys as load_model_weights reads them
 // (src/models/transformer.cpp:139-154), tensors copied to HBM in their GGUF form.
-extern "C" int ib_model_load_gguf(const char* path, int precision, int device, int max_seq,
-                                  void** out) {
+static int load_gguf(const char* path, int precision, int device, int max_seq, Comm* comm,
+                     void** out) {
     IB_REQUIRE(path && out, "null pointer argument");
     *out = nullptr;
     try {
@@ -880,7 +981,7 @@ extern "C" int ib_model_load_gguf(const char* path, int precision, int device, i
         const auto* g = f.find("blk.0.ffn_gate.weight");
         c.ffn = g && g->dims.size() == 2 ? (int)g->dims[1] : (int)f.get_int("llama.feed_forward_length", 0);
         void* h = nullptr;
-        int st = ib_model_create(&c, device, &h);
+        int st = model_create(&c, device, comm, &h);
         if (st) return st;
         for (const auto& t : f.tensors()) {
             int64_t cols = t.dims.empty() ? 0 : t.dims[0];
@@ -914,6 +1015,17 @@ extern "C" int ib_model_load_gguf(const char* path, int precision, int device, i
         set_error(e.what());
         return IB_ERR_INVALID;
     }
+}
+
+extern "C" int ib_model_load_gguf(const char* path, int precision, int device, int max_seq,
+                                  void** out) {
+    return load_gguf(path, precision, device, max_seq, nullptr, out);
+}
+
+extern "C" int ib_model_load_gguf_tp(const char* path, int precision, int device, int max_seq,
+                                     void* comm, void** out) {
+    IB_REQUIRE(comm, "null communicator");
+    return load_gguf(path, precision, device, max_seq, (Comm*)comm, out);
 }
 
 extern "C" int ib_model_weight_bytes(void* h, size_t* bytes) {

@@ -9,6 +9,8 @@
 
 namespace ib {
 
+struct Comm;
+
 enum Repr { REPR_NONE = 0, REPR_PACKED = 1, REPR_I16 = 2, REPR_F32 = 3 };
 
 // One weight matrix [rows, cols]: GGUF blocks (packed), INT16 + row scale, or FP32.
@@ -34,7 +36,15 @@ struct Layer {
 };
 
 struct Model {
+    // With tensor parallelism cfg holds this rank's share (n_heads, n_kv_heads, ffn
+    // divided by the TP size; dim and vocab whole) and `full` the model's configuration.
     ib_model_config cfg{};
+    ib_model_config full{};
+    Comm* comm = nullptr;  // not owned
+    int tp_rank = 0, tp_size = 1;
+    int vocab_local = 0, vocab_base = 0;  // output head rows of this rank
+    Linear head_view;                     // tied embedding: this rank's head rows (not owned)
+    float* logits_local = nullptr;        // == logits without TP
     int device = 0;
     int HD = 0;
     bool finalized = false;
