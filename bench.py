@@ -20,8 +20,11 @@ roofline: the dominant kernel, the Q4_K fused dequant-GEMV of ffn_gate/ffn_up
 cpu_baseline / --impl reference: the reference's own CPU matvec (oracle/_ref, or
         the C restatement where it was not built) on a bounded sample: one layer's
         seven projections plus 1/16 of the output head, extrapolated per token.
-With torchrun (N > 1) every rank decodes its own replica (no collective on the
-data path yet); value is the sum over ranks, timed as the max over ranks.
+With torchrun (N > 1) every rank decodes its own replica by default (no collective
+on the data path; value is the sum over ranks, timed as the max over ranks).  With
+--tp the N ranks hold one tensor-parallel model instead (Megatron split, NCCL
+allreduce after attn_output and ffn_down, cross-rank argmax of the head): value is
+that single sequence's tok/s (strong scaling).
 """
 from __future__ import annotations
 
@@ -112,11 +115,20 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201):
+def make_comm(ib, world, rank, local):
+    """NCCL communicator of the tensor-parallel model; the id travels over the process
+    group that torchrun set up."""
+    import torch.distributed as dist
+    uid = [ib.Comm.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    return ib.Comm(rank, world, uid[0], device=local)
+
+
+def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201, comm=None):
     import torch
     from inference_cpp_b200 import gguf_writer as gw
     max_seq = prompt_len + warmup + 2 * steps + 16
-    m = ib.Model.create(cfg, precision=ib.NATIVE, device=device, max_seq=max_seq)
+    m = ib.Model.create(cfg, precision=ib.NATIVE, device=device, max_seq=max_seq, comm=comm)
     for name, t, rows, cols in cfg.tensor_specs():
         if name.endswith("norm.weight"):
             data = torch.ones(cols, dtype=torch.float32, device="cuda")
@@ -258,6 +270,9 @@ def main():
                          "range named decode_step (for profiler launch lists)")
     ap.add_argument("--decode-path", default="fused", choices=["fused", "separate"],
                     help="fused decode kernels (default) or the separate per-op kernels")
+    ap.add_argument("--tp", action="store_true",
+                    help="with N > 1: one tensor-parallel model over the N GPUs instead of "
+                         "N replicas")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -280,7 +295,9 @@ def main():
     import torch
     torch.cuda.set_device(local)
     ib.init(local)
-    m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local)
+    tp = args.tp and world > 1
+    comm = make_comm(ib, world, rank, local) if tp else None
+    m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
     m.set_fused(args.decode_path == "fused")
     rng = np.random.default_rng(42)
     prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
@@ -333,7 +350,8 @@ def main():
     achieved = nbytes / (gemv_ms * 1e-3) / 1e9
     weight_bytes = m.weight_bytes()
 
-    value = world * args.steps / (dev_ms * 1e-3)
+    seqs = 1 if tp else world  # sequences decoded side by side
+    value = seqs * args.steps / (dev_ms * 1e-3)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -349,24 +367,25 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{cfg.name}-q4k-decode", "model": cfg.name,
-                       "prompt": args.prompt, "global_batch": world, "seq_len": pos,
-                       "parallelism": f"replica{world}" if world > 1 else "single",
+                       "prompt": args.prompt, "global_batch": seqs, "seq_len": pos,
+                       "parallelism": (f"tp{world}" if tp else f"replica{world}") if world > 1
+                       else "single",
                        "weights": "Q4_K linears, Q6_K attn_v/ffn_down/output (synthetic)",
                        "decode_path": "fused" if m.uses_fused() else "separate",
                        "l2": "inputs larger than L2 (weights per step >> 126 MB)"},
-            "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tok/s",
+            "e2e": {"value": seqs * e2e_steps / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic_from_profile(),
                          "kernel": f"gemv_q Q4_K {cfg.ffn}x{cfg.dim}",
                          "bytes_per_launch": nbytes, "avg_launch_us": gemv_ms * 1e3,
                          "peak_kind": peak_kind},
-            "decode_hbm": {"weight_bytes": weight_bytes,
-                           "achieved_gbs": weight_bytes * value / world / 1e9,
-                           "frac": weight_bytes * value / world / 1e9 / peak},
+            "decode_hbm": {"weight_bytes": weight_bytes,  # this rank's share under --tp
+                           "achieved_gbs": weight_bytes * value / seqs / 1e9,
+                           "frac": weight_bytes * value / seqs / 1e9 / peak},
             "prefill": {"tokens": args.prompt, "ms": prefill_ms,
                         "tok_s": args.prompt / (prefill_ms * 1e-3)},
             "cpu_baseline": cpu,
@@ -384,6 +403,8 @@ def main():
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
     m.close()
+    if comm is not None:
+        comm.close()
     if world > 1:
         import torch.distributed as dist
         barrier(world)

@@ -10,6 +10,7 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "comm.cuh"
 #include "common.cuh"
@@ -88,6 +89,68 @@ int comm_allreduce_max_u64(Comm* c, unsigned long long* buf, size_t n, cudaStrea
     if (r) return r;
     return nccl_check(nc, nc->all_reduce(buf, buf, n, ncclUint64, ncclMax, c->nc, st),
                       "ncclAllReduce");
+}
+
+int comm_peer_alloc(Comm* c, size_t bytes, void** local, void** peers) {
+    IB_REQUIRE(c && local && peers && bytes > 0, "bad peer allocation arguments");
+    const int W = c->world;
+    *local = nullptr;
+    for (int q = 0; q < W; ++q) peers[q] = nullptr;
+    IB_CUDA_CHECK(cudaMalloc(local, bytes));
+    IB_CUDA_CHECK(cudaMemset(*local, 0, bytes));
+    if (W == 1) {
+        peers[0] = *local;
+        return IB_OK;
+    }
+    cudaIpcMemHandle_t mine;
+    IB_CUDA_CHECK(cudaIpcGetMemHandle(&mine, *local));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t* dev = nullptr;
+    IB_CUDA_CHECK(cudaMalloc(&dev, hb * (W + 1)));
+    cudaStream_t st;
+    IB_CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    int r = IB_OK;
+    Nccl* nc = nullptr;
+    if ((r = nccl_load(&nc)) == IB_OK) {
+        cudaMemcpyAsync(dev + hb * W, &mine, hb, cudaMemcpyHostToDevice, st);
+        r = nccl_check(nc, nc->all_gather(dev + hb * W, dev, hb, ncclUint8, c->nc, st),
+                       "ncclAllGather");
+        if (r == IB_OK) cudaMemcpyAsync(all.data(), dev, hb * W, cudaMemcpyDeviceToHost, st);
+        if (r == IB_OK && cudaStreamSynchronize(st) != cudaSuccess) {
+            set_error("peer memory: handle exchange failed");
+            r = IB_ERR_CUDA;
+        }
+    }
+    cudaStreamDestroy(st);
+    cudaFree(dev);
+    for (int q = 0; q < W && r == IB_OK; ++q) {
+        if (q == c->rank) {
+            peers[q] = *local;
+            continue;
+        }
+        const cudaError_t e = cudaIpcOpenMemHandle(&peers[q], all[q], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            set_error(std::string("peer memory: cannot map rank ") + std::to_string(q) +
+                      "'s buffer: " + cudaGetErrorString(e));
+            peers[q] = nullptr;
+            r = IB_ERR_CUDA;
+        }
+    }
+    if (r != IB_OK) {
+        comm_peer_free(W, *local, peers);
+        *local = nullptr;
+    }
+    return r;
+}
+
+void comm_peer_free(int world, void* local, void** peers) {
+    const int W = world;
+    for (int q = 0; q < W; ++q) {
+        if (peers[q] && peers[q] != local) cudaIpcCloseMemHandle(peers[q]);
+        peers[q] = nullptr;
+    }
+    if (local) cudaFree(local);
 }
 
 int comm_allgather_f32(Comm* c, const float* send, float* recv, size_t n_per_rank,

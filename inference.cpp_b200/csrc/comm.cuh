@@ -16,4 +16,13 @@ int comm_allreduce_max_u64(Comm* c, unsigned long long* buf, size_t n, cudaStrea
 int comm_allgather_f32(Comm* c, const float* send, float* recv, size_t n_per_rank,
                        cudaStream_t st);
 
+// Peer memory: every rank allocates `bytes` (zeroed) of device memory and maps every
+// other rank's allocation into its address space (CUDA IPC handles exchanged over the
+// communicator; NVLink peer access).  peers[q] = rank q's allocation as seen here
+// (peers[rank] = *local).  Collective: every rank calls it with the same size.
+int comm_peer_alloc(Comm* c, size_t bytes, void** local, void** peers);
+// Unmaps the peers' allocations and frees this rank's (peers as filled above, world
+// entries; the communicator itself is not needed).
+void comm_peer_free(int world, void* local, void** peers);
+
 }  // namespace ib

@@ -56,25 +56,152 @@ struct Pair {
 
 bool slab_kquant(int type) { return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K; }
 
+// ---- tensor-parallel exchange ----------------------------------------------------------
+// Every exchanged 32-bit word travels as one 64-bit store of (tag << 32 | word), tag =
+// exchange number + 1: the receiver polls each word until its tag matches, so no fence,
+// flag or counter orders the data (a 64-bit aligned store is single-copy atomic).  A
+// rank that never sends (it died, or took another path) costs the waiting rank at most
+// this long; the wait then records fault 21 and the step's results are invalid.
+constexpr unsigned long long kExchangeTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_tagged(uint64_t* a, uint32_t tag, uint32_t word) {
+    const uint64_t v = ((uint64_t)tag << 32) | word;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* a) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// Waits for the word at a to carry `tag`; false (fault 21) once the deadline passes.
+__device__ __forceinline__ bool wait_tagged(const uint64_t* a, uint32_t tag, uint32_t& word,
+                                            unsigned long long& t0) {
+    for (uint32_t i = 0;; ++i) {
+        const uint64_t v = ld_relaxed_sys(a);
+        if ((uint32_t)(v >> 32) == tag) {
+            word = (uint32_t)v;
+            return true;
+        }
+        if (i == 0 && t0 == 0ull) t0 = globaltimer_ns();
+        if (i >= 32) {
+            if (globaltimer_ns() - t0 > kExchangeTimeoutNs) {
+                atomicCAS(&g_decode_fault, 0, 21);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
+__device__ __forceinline__ uint8_t* tp_region(const TpExchange& x, int q) {
+    uint8_t* r = x.region[0];
+#pragma unroll
+    for (int i = 1; i < kMaxRanks; ++i)
+        if (q == i) r = x.region[i];
+    return r;
+}
+
+// True when the kernel instance ends with an exchange.
+template <int EPI>
+__device__ __forceinline__ bool tp_exchanges(const FusedGemv& p) {
+    return EPI == EPI_ALLRED || (EPI == EPI_ARGMAX && p.tp.world > 1);
+}
+
+// Run once by the last CTA out, after every CTA's rows are pushed: sends this rank's
+// key (ARGMAX; the CTAs' atomicMax are fenced before their arrival) and advances the
+// exchange counter the pushes and the receivers derive their tag from.
+template <int EPI>
+__device__ __forceinline__ void tp_finish(const FusedGemv& p) {
+    const TpExchange& x = p.tp;
+    const uint32_t e = __ldcg(x.seq);
+    if (EPI == EPI_ARGMAX) {
+        const unsigned long long key = atomicAdd(p.best, 0ull);
+        const size_t at = ((size_t)(e & 1u) * x.world + x.rank) * 2;
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < x.world) {
+                uint64_t* k = (uint64_t*)(x.region[q] + tp_keys_offset(x.world, x.stride)) + at;
+                st_tagged(k, e + 1, (uint32_t)key);
+                st_tagged(k + 1, e + 1, (uint32_t)(key >> 32));
+            }
+    }
+    *x.seq = e + 1;
+}
+
+// After a head GEMV with an ARGMAX exchange: *best <- the maximum key over the ranks.
+__global__ void tp_key_max_kernel(const TpExchange x, unsigned long long* best) {
+    const uint32_t e1 = __ldcg(x.seq);
+    const uint64_t* keys = (const uint64_t*)(tp_region(x, x.rank) + tp_keys_offset(x.world, x.stride)) +
+                           (size_t)((e1 - 1u) & 1u) * x.world * 2;
+    unsigned long long b = 0ull, t0 = 0ull;
+    for (int src = 0; src < x.world; ++src) {
+        uint32_t lo, hi;
+        if (!wait_tagged(keys + 2 * src, e1, lo, t0) || !wait_tagged(keys + 2 * src + 1, e1, hi, t0))
+            return;
+        const unsigned long long k = ((unsigned long long)hi << 32) | lo;
+        b = k > b ? k : b;
+    }
+    *best = b;
+}
+
 // ---- limb slab ----------------------------------------------------------------------
-// One warp per scale group of GS elements.
-template <bool KQ>
-__global__ void __launch_bounds__(256) xq_slab_kernel(const float* __restrict__ x,
+// One warp per scale group of GS elements.  TP: x is first completed with the rows of
+// the exchange that produced it, x[i] += sum over the ranks in rank order (the same
+// values on every rank), and written back.
+template <bool KQ, bool TP>
+__global__ void __launch_bounds__(256) xq_slab_kernel(float* __restrict__ x,
                                                       const float* __restrict__ norm, int K,
                                                       uint8_t* __restrict__ slab,
-                                                      float* __restrict__ ssq) {
+                                                      float* __restrict__ ssq,
+                                                      const TpExchange tp) {
     pdl_launch_dependents();
     pdl_wait();
     constexpr int GS = SlabG<KQ>::GS, PER = GS / 32;
+    const uint64_t* parts = nullptr;
+    uint32_t tag = 0;
+    if constexpr (TP) {
+        tag = __ldcg(tp.seq);  // the exchange that produced x's rows: number tag - 1
+        parts = (const uint64_t*)tp_region(tp, tp.rank) + (size_t)((tag - 1u) & 1u) * tp.world * tp.stride;
+    }
     const int lane = threadIdx.x & 31;
     const int gi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (gi * GS >= K) return;
     float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) v[j] = x[(gi * PER + j) * 32 + lane];
+    if constexpr (TP) {
+        // x += every rank's rows in rank order; a rank's PER words are loaded together
+        // (one round trip when they have landed), then any stragglers are polled
+        unsigned long long t0 = 0ull;
+        bool ok = true;
+        for (int q = 0; q < tp.world && ok; ++q) {
+            const uint64_t* src = parts + (size_t)q * tp.stride + gi * GS + lane;
+            uint64_t wv[PER];
+#pragma unroll
+            for (int j = 0; j < PER; ++j) wv[j] = ld_relaxed_sys(src + j * 32);
+#pragma unroll
+            for (int j = 0; j < PER; ++j) {
+                uint32_t w = (uint32_t)wv[j];
+                if ((uint32_t)(wv[j] >> 32) != tag && ok) ok = wait_tagged(src + j * 32, tag, w, t0);
+                v[j] += __uint_as_float(w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PER; ++j) x[(gi * PER + j) * 32 + lane] = v[j];
+    }
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
         const int i = (gi * PER + j) * 32 + lane;
-        float t = x[i];
+        float t = v[j];
         ss = fmaf(t, t, ss);
         if (norm) t *= norm[i];
         v[j] = t;
@@ -88,17 +215,36 @@ __global__ void __launch_bounds__(256) xq_slab_kernel(const float* __restrict__ 
 }
 
 int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_t* slab,
-                   float* ssq, cudaStream_t st, bool pdl) {
+                   float* ssq, cudaStream_t st, bool pdl, const TpExchange* tp) {
     IB_REQUIRE(x && slab && K > 0, "xq_slab: bad arguments");
     const int GS = kquant ? 256 : 32;
     IB_REQUIRE(K % GS == 0, "xq_slab: K must be a multiple of the limb group");
     const int groups = K / GS, grid = (groups + 7) / 8;
-    if (kquant)
-        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<true>, dim3(grid), dim3(256), 0, st, pdl, x, norm,
-                                 K, slab, ssq));
+    float* xw = const_cast<float*>(x);  // written back only when completing an exchange
+    const bool ex = tp && tp->world > 1;
+    IB_REQUIRE(!ex || (tp->world <= kMaxRanks && K <= tp->stride && tp->seq),
+               "xq_slab: bad exchange");
+    const TpExchange none{};
+    const TpExchange& t = ex ? *tp : none;
+    if (kquant && ex)
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<true, true>, dim3(grid), dim3(256), 0, st, pdl, xw,
+                                 norm, K, slab, ssq, t));
+    else if (kquant)
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<true, false>, dim3(grid), dim3(256), 0, st, pdl, xw,
+                                 norm, K, slab, ssq, t));
+    else if (ex)
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<false, true>, dim3(grid), dim3(256), 0, st, pdl, xw,
+                                 norm, K, slab, ssq, t));
     else
-        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<false>, dim3(grid), dim3(256), 0, st, pdl, x, norm,
-                                 K, slab, ssq));
+        IB_CUDA_CHECK(launch_pdl(xq_slab_kernel<false, false>, dim3(grid), dim3(256), 0, st, pdl,
+                                 xw, norm, K, slab, ssq, t));
+    return IB_OK;
+}
+
+int tp_key_max_launch(const TpExchange& x, unsigned long long* best, cudaStream_t st) {
+    IB_REQUIRE(best && x.world > 1 && x.world <= kMaxRanks && x.seq, "tp key max: bad arguments");
+    tp_key_max_kernel<<<1, 1, 0, st>>>(x, best);
+    IB_CUDA_CHECK(cudaGetLastError());
     return IB_OK;
 }
 
@@ -194,6 +340,16 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
     } else if (EPI == EPI_SWIGLU) {
         const float u = __shfl_down_sync(FULL, v, 8);
         if (lane < 8) p.y[rg * 8 + lane] = v * (1.0f / (1.0f + expf(-v))) * u;
+    } else if (EPI == EPI_ALLRED) {
+        const int R = rg * 16 + lane;
+        if (live) {  // this rank's row R into slot row [rank] of every rank's region
+            const TpExchange& x = p.tp;
+            const uint32_t e = __ldcg(x.seq);
+            const size_t at = ((size_t)(e & 1u) * x.world + x.rank) * x.stride + R;
+#pragma unroll
+            for (int q = 0; q < kMaxRanks; ++q)
+                if (q < x.world) st_tagged((uint64_t*)x.region[q] + at, e + 1, __float_as_uint(v));
+        }
     } else if (EPI == EPI_ARGMAX) {
         const int R = rg * 16 + lane;
         unsigned long long key = 0ull;
@@ -457,9 +613,12 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
             break;
         ++rgl;
     }
-    // the last consumer warp of the last CTA out resets the work counters
+    // the last consumer warp of the last CTA out resets the work counters (and ends the
+    // exchange: its key and the exchange counter)
+    if (EPI == EPI_ARGMAX && tp_exchanges<EPI>(p) && warp == 0) __threadfence();
     if (p.work && lane == 0 && atomicAdd(&warps_done, 1) == kNWC - 1 &&
         atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+        if (tp_exchanges<EPI>(p)) tp_finish<EPI>(p);
         p.work[0] = 0;
         p.work[1] = 0;
     }
@@ -505,6 +664,15 @@ __global__ void __launch_bounds__(kNWC * 32) fused_direct_kernel(const FusedGemv
                                              xs, c, acc_a, acc_b);
         }
         finish_group<EPI>(p, red[k & 1], rg, warp, lane, c, rms, acc_a, acc_b);
+    }
+    if (tp_exchanges<EPI>(p)) {  // as in fused_tma_kernel; every thread gets here
+        if (EPI == EPI_ARGMAX) __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+            tp_finish<EPI>(p);
+            p.work[0] = 0;
+            p.work[1] = 0;
+        }
     }
 }
 
@@ -587,6 +755,15 @@ bool fused_gemv_supported(const FusedGemv& p, int epi) {
                            p.rows[1] != p.rows[2] || !p.pos || !p.rope || !p.q || !p.kc || !p.vc))
         return false;
     if (epi == EPI_ARGMAX && !p.best) return false;
+    if (epi == EPI_ALLRED || (epi == EPI_ARGMAX && p.tp.world > 1)) {
+        const TpExchange& x = p.tp;
+        if (x.world < 2 || x.world > kMaxRanks || x.rank < 0 || x.rank >= x.world || !x.seq ||
+            !p.work || p.paired)
+            return false;
+        if (epi == EPI_ALLRED && p.rows[0] + p.rows[1] + p.rows[2] > x.stride) return false;
+        for (int q = 0; q < x.world; ++q)
+            if (!x.region[q]) return false;
+    }
     if (!p.y && epi != EPI_QKV) return false;
     return true;
 }
@@ -634,6 +811,7 @@ static int launch_pair(const FusedGemv& p, int pro, int epi, cudaStream_t st, bo
     if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_inst<TA, TB, PRO_NORM, EPI_SWIGLU>(p, st, pdl);
     if (pro == PRO_NORM && epi == EPI_ARGMAX) return launch_inst<TA, TB, PRO_NORM, EPI_ARGMAX>(p, st, pdl);
     if (pro == PRO_PLAIN && epi == EPI_STORE) return launch_inst<TA, TB, PRO_PLAIN, EPI_STORE>(p, st, pdl);
+    if (pro == PRO_PLAIN && epi == EPI_ALLRED) return launch_inst<TA, TB, PRO_PLAIN, EPI_ALLRED>(p, st, pdl);
     set_error("fused GEMV: unsupported prologue/epilogue combination");
     return IB_ERR_UNSUPPORTED;
 }

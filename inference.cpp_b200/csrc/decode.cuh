@@ -13,7 +13,30 @@
 namespace ib {
 
 enum { PRO_PLAIN = 0, PRO_NORM = 1 };
-enum { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_ALLRED = 5 };
+
+// Tensor-parallel exchange over peer memory (NVLink): each rank owns a region that
+// every rank maps; region[q] is rank q's as seen from this rank.  Region layout:
+// tagged rows u64 [2][world][stride] | tagged keys u64 [2][world][2].  Exchange e
+// (counted by *seq, identical on every rank since every rank runs the same steps)
+// uses slot e & 1: each rank stores its rows, as (e + 1) << 32 | float bits, into slot
+// row [rank] of every region; a receiver polls the words of its own region until their
+// tags read e + 1 and sums the rows in rank order.  A slot is rewritten two exchanges
+// later, after every rank has produced the exchange in between, which it does only
+// once its reads of the earlier one are done.
+constexpr int kMaxRanks = 8;
+struct TpExchange {
+    uint8_t* region[kMaxRanks];
+    uint32_t* seq;  // this rank's exchange counter (device)
+    int rank, world, stride;
+};
+
+__host__ __device__ inline size_t tp_keys_offset(int world, int stride) {
+    return (size_t)2 * world * stride * 8;
+}
+__host__ __device__ inline size_t tp_region_bytes(int world, int stride) {
+    return (tp_keys_offset(world, stride) + (size_t)2 * world * 2 * 8 + 255) / 256 * 256;
+}
 
 struct SlabGeom {
     int SE;           // elements per slice
@@ -41,8 +64,12 @@ bool slab_kquant(int type);
 // slab <- limbs of x (norm == nullptr) or of x * norm; ssq[g] <- sum of x^2 over scale
 // group g (when ssq != nullptr; the RMSNorm of x is then applied in the GEMV
 // epilogue as 1 / sqrt(sum(ssq) / K + eps)).  K must be a multiple of GS.
+// With an exchange (tp, world > 1): x (K <= stride) is first completed with the latest
+// exchange's rows, x[i] += their sum over the ranks, and written back.
 int xq_slab_launch(const float* x, const float* norm, int K, bool kquant, uint8_t* slab,
-                   float* ssq, cudaStream_t st, bool pdl);
+                   float* ssq, cudaStream_t st, bool pdl, const TpExchange* tp = nullptr);
+// After a head GEMV with an ARGMAX exchange: *best <- the maximum key over the ranks.
+int tp_key_max_launch(const TpExchange& x, unsigned long long* best, cudaStream_t st);
 
 struct FusedGemv {
     // Weight rows: segments concatenated in row order (row groups of 16), or, with
@@ -59,7 +86,9 @@ struct FusedGemv {
     const float* ssq;
     float eps;
     // epilogue
-    float* y;  // STORE / ARGMAX: y[row]; RESID: y[row] += ; SWIGLU: y[i] = silu(g_i) * u_i
+    // STORE / ARGMAX: y[row]; RESID: y[row] += ; SWIGLU: y[i] = silu(g_i) * u_i;
+    // ALLRED: y[row] += the sum over the ranks of their rows (tp exchange)
+    float* y;
     float* q;  // QKV: segment 0 after RoPE -> q; segment 1 -> kc; segment 2 -> vc
     float* kc;
     float* vc;
@@ -68,6 +97,9 @@ struct FusedGemv {
     int head_dim, max_seq;
     unsigned long long* best;  // ARGMAX: max of (ordered logit << 32 | ~(row_base + row))
     int row_base;              // ARGMAX: global index of this kernel's first row
+    // ALLRED, and ARGMAX with tp.world > 1 (the key maximum over the ranks): the exchange;
+    // both need `work` (its second counter finds the last CTA, which exchanges)
+    TpExchange tp;
     // optional work counters {next row group, CTAs done}, zero between launches: row
     // groups are then claimed dynamically (balanced over SMs); null = static schedule
     int* work;

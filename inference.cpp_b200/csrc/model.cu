@@ -137,6 +137,7 @@ Model::~Model() {
     }
     for (void* p : allocations) cudaFree(p);
     if (host_pinned) cudaFreeHost(host_pinned);
+    if (tp_local) comm_peer_free(tp_size, tp_local, tp_peers);
 }
 
 }  // namespace ib
@@ -466,6 +467,28 @@ extern "C" int ib_model_finalize(void* h) {
     } else {
         m->logits_local = m->logits;
     }
+    if (m->tp_size > 1) {
+        // the fused step's row-split GEMVs exchange their rows over peer memory
+        const int W = m->tp_size;
+        if (W > kMaxRanks) {
+            set_error("model: at most 8 tensor-parallel ranks");
+            return IB_ERR_UNSUPPORTED;
+        }
+        void* local = nullptr;
+        if ((st = comm_peer_alloc(m->comm, tp_region_bytes(W, c.dim), &local, m->tp_peers)))
+            return st;
+        m->tp_local = (uint8_t*)local;
+        uint32_t* seq = nullptr;
+        IB_CUDA_CHECK(cudaMalloc(&seq, 16));
+        IB_CUDA_CHECK(cudaMemset(seq, 0, 16));
+        m->allocations.push_back(seq);
+        TpExchange& x = m->tpx;
+        for (int q = 0; q < W; ++q) x.region[q] = (uint8_t*)m->tp_peers[q];
+        x.seq = seq;
+        x.rank = m->tp_rank;
+        x.world = W;
+        x.stride = c.dim;
+    }
     m->fused_ok = fused_supported(m);
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
     IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
@@ -519,6 +542,7 @@ static FusedGemv fg_wo(const Model* m, const Layer& L) {
     p.K = (int)L.wo.cols;
     p.slab = m->slab_att;
     p.y = m->x;
+    p.tp = m->tpx;
     return p;
 }
 
@@ -540,6 +564,7 @@ static FusedGemv fg_ffn_out(const Model* m, const Layer& L) {
     p.K = (int)L.w2.cols;
     p.slab = m->slab_h;
     p.y = m->x;
+    p.tp = m->tpx;
     return p;
 }
 
@@ -552,6 +577,12 @@ static FusedGemv fg_head(const Model* m) {
     p.y = m->logits_local;
     p.row_base = m->vocab_base;
     p.best = m->best;
+    p.tp = m->tpx;
+    return p;
+}
+
+static FusedGemv with_work(FusedGemv p, int* work) {
+    p.work = work;
     return p;
 }
 
@@ -560,16 +591,21 @@ bool fused_supported(const Model* m) {
     const Linear& O = head_linear(m);
     const int GS = m->slab_kq ? 256 : 32;
     if (c.dim % GS || c.ffn % GS || (c.n_heads * m->HD) % GS) return false;
+    // the call sites get their work counters at launch (checked here with a stand-in)
+    int* work = m->gemv_work;
+    const int res_epi = m->tp_size > 1 ? EPI_ALLRED : EPI_RESID;
+    FusedGemv head = fg_head(m);
+    head.work = work;
     if (O.repr != REPR_PACKED || slab_kquant(O.type) != m->slab_kq ||
-        !fused_gemv_supported(fg_head(m), EPI_ARGMAX))
+        !fused_gemv_supported(head, EPI_ARGMAX))
         return false;
     for (const Layer& L : m->layers) {
         for (const Linear* l : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3})
             if (l->repr != REPR_PACKED || slab_kquant(l->type) != m->slab_kq) return false;
         if (!fused_gemv_supported(fg_qkv(m, L), EPI_QKV) ||
-            !fused_gemv_supported(fg_wo(m, L), EPI_RESID) ||
+            !fused_gemv_supported(with_work(fg_wo(m, L), work), res_epi) ||
             !fused_gemv_supported(fg_ffn_in(m, L), EPI_SWIGLU) ||
-            !fused_gemv_supported(fg_ffn_out(m, L), EPI_RESID))
+            !fused_gemv_supported(with_work(fg_ffn_out(m, L), work), res_epi))
             return false;
     }
     return true;
@@ -594,11 +630,14 @@ static int decode_launches_fused(Model* m) {
     const int* pos = m->dev_i32 + 1;
     const float scale = 1.0f / sqrtf((float)HD);
     const bool att_slab = m->att_counters && (H / Hkv * HD) % (kq ? 256 : 32) == 0;
-    // row-split projections: rank 0 adds the residual, the others store, then allreduce
-    const int resid = m->tp_rank == 0 ? EPI_RESID : EPI_STORE;
+    // row-split projections under TP: the GEMV adds every rank's rows (peer exchange)
+    const int resid = m->tp_size > 1 ? EPI_ALLRED : EPI_RESID;
+    // the slab kernel after such a GEMV completes x with the ranks' rows
+    const TpExchange* tx = m->tp_size > 1 ? &m->tpx : nullptr;
     int r;
     if ((r = embed_launch(m))) return r;
     int* work = m->gemv_work;  // two counters per GEMV call site
+    bool first = true;
     for (auto& L : m->layers) {
         FusedGemv qkv = fg_qkv(m, L), wo = fg_wo(m, L), fin = fg_ffn_in(m, L), fout = fg_ffn_out(m, L);
         qkv.work = work;
@@ -606,7 +645,10 @@ static int decode_launches_fused(Model* m) {
         fin.work = work + 4;
         fout.work = work + 6;
         work += 8;
-        if ((r = xq_slab_launch(m->x, L.attn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+        if ((r = xq_slab_launch(m->x, L.attn_norm, D, kq, m->slab_x, m->ssq, st, true,
+                                first ? nullptr : tx)))
+            return r;
+        first = false;
         if ((r = fused_gemv_launch(qkv, PRO_NORM, EPI_QKV, st, true))) return r;
         if (att_slab) {  // attention writes the wo input's limb slab itself
             if ((r = attention_decode_fused(m->q, L.kc, L.vc, m->att, m->slab_att, kq, H, Hkv, HD,
@@ -621,18 +663,18 @@ static int decode_launches_fused(Model* m) {
                 return r;
         }
         if ((r = fused_gemv_launch(wo, PRO_PLAIN, resid, st, true))) return r;
-        if ((r = comm_allreduce_sum_f32(m->comm, m->x, D, st))) return r;
-        if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+        if ((r = xq_slab_launch(m->x, L.ffn_norm, D, kq, m->slab_x, m->ssq, st, true, tx))) return r;
         if ((r = fused_gemv_launch(fin, PRO_NORM, EPI_SWIGLU, st, true))) return r;
         if ((r = xq_slab_launch(m->gate, nullptr, F, kq, m->slab_h, nullptr, st, true))) return r;
         if ((r = fused_gemv_launch(fout, PRO_PLAIN, resid, st, true))) return r;
-        if ((r = comm_allreduce_sum_f32(m->comm, m->x, D, st))) return r;
     }
-    if ((r = xq_slab_launch(m->x, m->out_norm, D, kq, m->slab_x, m->ssq, st, true))) return r;
+    if ((r = xq_slab_launch(m->x, m->out_norm, D, kq, m->slab_x, m->ssq, st, true,
+                            m->layers.empty() ? nullptr : tx)))
+        return r;
     FusedGemv head = fg_head(m);
     head.work = work;
     if ((r = fused_gemv_launch(head, PRO_NORM, EPI_ARGMAX, st, true))) return r;
-    if ((r = comm_allreduce_max_u64(m->comm, m->best, 1, st))) return r;
+    if (tx && (r = tp_key_max_launch(*tx, m->best, st))) return r;
     feedback_best_kernel<<<1, 1, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq);
     IB_LAUNCH_CHECK("decode step");
     return IB_OK;

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "../../include/ib_cuda.h"
+#include "decode.cuh"
 
 namespace ib {
 
@@ -45,6 +46,10 @@ struct Model {
     int vocab_local = 0, vocab_base = 0;  // output head rows of this rank
     Linear head_view;                     // tied embedding: this rank's head rows (not owned)
     float* logits_local = nullptr;        // == logits without TP
+    // fused TP decode: the peer-memory exchange of the row-split GEMVs (decode.cuh)
+    TpExchange tpx{};
+    uint8_t* tp_local = nullptr;       // this rank's exchange region (owned)
+    void* tp_peers[kMaxRanks] = {};    // every rank's region, mapped here
     int device = 0;
     int HD = 0;
     bool finalized = false;

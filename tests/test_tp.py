@@ -35,6 +35,19 @@ def tp_cfgs():
     ]
 
 
+def tp_tma_cfgs():
+    """Shapes whose per-rank GEMVs take the TMA-ring kernel (K-quant rows of 2048-column
+    slices, 32-element blocks of 1024-column slices) on two ranks."""
+    return [
+        gw.LlamaConfig("tp-k-tma", 1, 4096, 32, 8, 8192, 10000, 40, 500000.0, 1e-5,
+                       embed_type=ib.Q4_K, linear_type=ib.Q4_K, attn_v_type=ib.Q6_K,
+                       ffn_down_type=ib.Q6_K, output_type=ib.Q6_K),
+        gw.LlamaConfig("tp-q32-tma", 1, 2048, 16, 8, 4096, 520, 40, 10000.0, 1e-5,
+                       embed_type=ib.Q8_0, linear_type=ib.Q4_0, attn_v_type=ib.Q8_0,
+                       ffn_down_type=ib.Q8_0, output_type=ib.Q8_0),
+    ]
+
+
 def synth(cfg, seed=7):
     return {n: (t, r, c, d) for n, t, r, c, d in gw.synth_tensors(cfg, seed, ib.synth_host)}
 
@@ -275,7 +288,7 @@ def _two_gpus():
 @pytest.mark.gpu
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
 @pytest.mark.parametrize("fused", [True, False], ids=["fused", "separate"])
-@pytest.mark.parametrize("cfg", tp_cfgs(), ids=lambda c: c.name)
+@pytest.mark.parametrize("cfg", tp_cfgs() + tp_tma_cfgs(), ids=lambda c: c.name)
 def test_tp_generate_matches_oracle_2gpu(port, cfg, fused):
     import torch.multiprocessing as mp
     world = 2
@@ -298,5 +311,5 @@ def test_tp_generate_matches_oracle_2gpu(port, cfg, fused):
         assert got == list(want), rank
         scale = np.abs(want_logits).max(axis=1, keepdims=True)
         assert np.all(np.abs(logits - want_logits) <= LOGIT_RTOL * scale), rank
-        if fused and cfg.name == "tp-k":
+        if fused and cfg.name != "tp-q32-tied":
             assert uses_fused, rank
