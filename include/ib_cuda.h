@@ -130,6 +130,10 @@ int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev
  * src/ops/cuda_kernels.cu:279-346). */
 int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float* dev_Y, int64_t T,
               int64_t rows, int64_t cols, void* stream);
+/* Which kernel ib_gemm_q runs (process-wide): 0 = tcgen05 tensor cores with FP32
+ * accumulation in tensor memory, operands as FP16 hi/lo pairs (default; used when
+ * cols % 64 == 0, else 1); 1 = CUDA-core FP32 tiles.  No counterpart in the reference. */
+int ib_gemm_set_path(int path);
 
 /* Embedding gather with dequantisation: out[t, :] = dequant(table[ids[t], :]).
  * Replaces embedding / embedding_batch (include/ops/cuda_backend.hpp:44-50) for a

@@ -65,6 +65,7 @@ SIGNATURES = {
     "ib_comm_free": [_vp],
     "ib_tp_shard": [_i, _vp, _i64, _i64, _i, _i, _i, _vp],
     "ib_gemm_q": [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ib_gemm_set_path": [_i],
     "ib_embedding_q": [_i, _vp, _vp, _vp, _i, _i64, _i64, _vp],
     "ib_gemv": [_vp, _vp, _vp, _i, _i, _vp],
     "ib_gemv_i16": [_vp, _vp, _vp, _vp, _i, _i, _vp],
@@ -267,6 +268,15 @@ def gemm_q(type_: int, W, X, T: int, rows: int, cols: int, Y=None, stream=None):
         Y = torch.empty(T * rows, dtype=torch.float32, device=X.device)
     call("ib_gemm_q", type_, _ptr(W), _ptr(X), _ptr(Y), T, rows, cols, _stream(stream))
     return Y
+
+
+GEMM_TENSOR_CORES, GEMM_CUDA_CORES = 0, 1
+
+
+def gemm_set_path(path: int) -> None:
+    """Kernel behind gemm_q (process-wide): GEMM_TENSOR_CORES (tcgen05, default) or
+    GEMM_CUDA_CORES."""
+    call("ib_gemm_set_path", path)
 
 
 def embedding_q(type_: int, table, ids, vocab: int, dim: int, out=None, stream=None):

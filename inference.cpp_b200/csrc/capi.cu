@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "gemv_mma.cuh"
+#include "ops.cuh"
 
 namespace ib {
 
@@ -140,6 +141,8 @@ extern "C" int ib_check_fault(int* code) {
     int st = gemv_fault_take(code);
     if (st != IB_OK) return st;
     if ((st = decode_fault_take(&c2)) != IB_OK) return st;
+    if (!*code) *code = c2;
+    if ((st = gemm_fault_take(&c2)) != IB_OK) return st;
     if (!*code) *code = c2;
     if (*code) {
         set_error("CUDA: a pipeline wait expired in a GEMV kernel (code " + std::to_string(*code) +

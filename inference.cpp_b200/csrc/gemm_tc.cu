@@ -1,0 +1,375 @@
+// Prefill GEMM on the 5th-generation tensor cores: Y[T, rows] = X[T, cols] . W^T with W
+// in its packed GGUF blocks -- the B200 counterpart of the reference's batched GPU
+// matmul (src/ops/cuda_backend.cpp gemm kernels, called from prefill in
+// src/models/model_cuda.cpp:293-368).
+//
+// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64.  Eight
+// producer warps stage, per 256 columns, the tile rows' packed blocks in shared memory
+// with coalesced 16-byte loads; per 64-column step they dequantise them (the
+// bit-exact element expressions of quant.cuh) and copy the 128 tokens x 64 columns of
+// X, each value split into an FP16 pair v = hi + lo (hi = fp16(v), lo = fp16(v - hi)),
+// into 128-byte-swizzled K-major tiles.  One thread issues, per 16-column slice,
+// tcgen05.mma kind::f16 for hi.hi + hi.lo + lo.hi into an FP32 accumulator of 128
+// lanes x 128 columns in tensor memory, and tcgen05.commit releases the stage to the
+// producers.  The three products keep each term to about 2^-21 of its value, so the
+// GEMM matches an FP32 matmul to rounding (the dropped lo.lo term is below 2^-22).
+// The epilogue warps read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+// 32(w%4).. = tile rows, columns 64(w/4)..) and store Y.  Every mbarrier wait is
+// bounded (fault word, as in the other pipelines) and the producers' named barriers
+// are reached by every producer on every step whatever failed; the MMA thread always
+// ends with a commit the epilogue waits for, so tensor memory is released only after
+// the last MMA has finished.
+#include <cuda_fp16.h>
+
+#include <string>
+
+#include "common.cuh"
+#include "ops.cuh"
+#include "pipeline.cuh"
+#include "quant.cuh"
+
+namespace ib {
+
+static __device__ int g_gemm_fault;
+
+constexpr int TC_M = 128;      // weight rows per tile (MMA M)
+constexpr int TC_N = 128;      // tokens per tile (MMA N)
+constexpr int TC_BK = 64;      // columns per stage (one 128-byte swizzle row of fp16)
+constexpr int TC_SEGC = 256;   // columns per staged run of packed blocks
+constexpr int TC_STAGES = 2;
+constexpr int TC_TILE = TC_M * TC_BK * 2;  // bytes of one fp16 operand tile (16 KB)
+constexpr int TC_STAGE = 4 * TC_TILE;      // A hi, A lo, B hi, B lo
+constexpr int TC_PROD = 256;               // producer / epilogue threads (8 warps)
+constexpr int TC_THREADS = TC_PROD + 32;   // + the MMA warp
+
+// Packed bytes of 256 columns of a row, and their row stride in shared memory (16 x an
+// odd number, so 16-byte loads of 8 consecutive rows hit distinct bank groups; Q6_K's
+// 210-byte runs start 2-byte aligned and are staged from the 16-byte boundary below).
+template <int TYPE>
+struct RawSeg {
+    static constexpr int BE = (TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K) ? 256 : 32;
+    static constexpr int BB = TYPE == IB_TYPE_Q4_0 ? 18 : TYPE == IB_TYPE_Q5_0 ? 22 :
+                              TYPE == IB_TYPE_Q5_1 ? 24 : TYPE == IB_TYPE_Q8_0 ? 34 :
+                              TYPE == IB_TYPE_Q4_K ? 144 : 210;
+    static constexpr int SEG = TC_SEGC / BE * BB;
+    static constexpr int NCH = (SEG + 15) / 16 + (SEG % 16 ? 1 : 0);  // chunks, worst case
+    static constexpr int RS = ((NCH & 1) ? NCH : NCH + 1) * 16;
+};
+
+template <int TYPE>
+constexpr size_t tc_smem_bytes() {
+    return (size_t)TC_STAGES * TC_STAGE + (size_t)TC_M * RawSeg<TYPE>::RS + 1024;
+}
+
+// ---- tcgen05 building blocks (inline PTX) ----------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes
+// apart (leading offset unused for this layout, 1 by convention), sm_100 version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D FP32, A and B FP16, both K-major, M x N.
+constexpr uint32_t tc_idesc(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                       uint32_t accumulate) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+          "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+          "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+          "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r in a K-major 128B-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+// Eight FP32 values -> their FP16 hi/lo pairs (two 16-byte chunks).
+__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half h0 = __float2half_rn(v[2 * i]), h1 = __float2half_rn(v[2 * i + 1]);
+        const __half l0 = __float2half_rn(v[2 * i] - __half2float(h0));
+        const __half l1 = __float2half_rn(v[2 * i + 1] - __half2float(h1));
+        h[i] = pack_h2(h0, h1);
+        l[i] = pack_h2(l0, l1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bar_producers() {
+    asm volatile("bar.sync 1, %0;" ::"r"(TC_PROD) : "memory");
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const uint8_t* __restrict__ W, const __half* __restrict__ Xh,
+                   const __half* __restrict__ Xl, float* __restrict__ Y, int T, int rows, int cols,
+                   int64_t row_bytes) {
+    using R = RawSeg<TYPE>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], acc_full;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5, tid = threadIdx.x;
+    const int m0 = blockIdx.x * TC_M, n0 = blockIdx.y * TC_N;
+    const int n_k = cols / TC_BK;
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t* const raw = smem_raw + (base - smem_u32(smem_raw)) + TC_STAGES * TC_STAGE;
+    if (tid == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            mbar_init(&full[s], TC_PROD);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 8) {  // tensor-memory accumulator: 128 lanes x TC_N FP32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_base)),
+                     "r"(TC_N)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp < 8) {
+        const int r = tid & 127, h = tid >> 7;  // dequant: tile row r, columns 32h..32h+31
+        const int row = m0 + r;
+        bool ok = true;
+        for (int kt = 0; kt < n_k; ++kt) {
+            const int s = kt % TC_STAGES, u = kt / TC_STAGES, sub = kt % (TC_SEGC / TC_BK);
+            const int k0 = kt * TC_BK;
+            if (sub == 0) {
+                // stage the packed bytes of columns [k0, k0 + 256) of the 128 tile rows
+                bar_producers();  // everyone is done with the previous run
+                const int64_t seg = k0 / TC_SEGC;
+                for (int i = tid; i < TC_M * R::NCH; i += TC_PROD) {
+                    const int rr = i / R::NCH, c = i - rr * R::NCH;
+                    if (m0 + rr >= rows) continue;
+                    const int64_t start = (int64_t)(m0 + rr) * row_bytes + seg * R::SEG;
+                    const int64_t a0 = start & ~(int64_t)15;
+                    if (a0 + 16 * c >= start + R::SEG) continue;  // beyond this run
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(W + a0) + c);
+                    *reinterpret_cast<uint4*>(raw + rr * R::RS + 16 * c) = v;
+                }
+                bar_producers();
+            }
+            if (u > 0 && ok && !mbar_wait(&empty[s], (u - 1) & 1, &g_gemm_fault, 31)) ok = false;
+            const uint32_t st = base + (uint32_t)(s * TC_STAGE);
+            if (ok) {
+                // A: 32 columns of tile row r from the staged run
+                if (row < rows) {
+                    const int64_t start = (int64_t)row * row_bytes + (int64_t)(k0 / TC_SEGC) * R::SEG;
+                    const uint8_t* run = raw + r * R::RS + (int)(start & 15);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int kc = sub * TC_BK + 32 * h + 8 * i;  // column within the run
+                        float v[8];
+                        deq8<TYPE, GenericBytes>(run + (kc / R::BE) * R::BB, (kc % R::BE) >> 3, v);
+                        uint4 hi, lo;
+                        split8(v, hi, lo);
+                        sts128(st + sw128_off(r, 4 * h + i), hi);
+                        sts128(st + TC_TILE + sw128_off(r, 4 * h + i), lo);
+                    }
+                } else {
+                    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        sts128(st + sw128_off(r, 4 * h + i), z);
+                        sts128(st + TC_TILE + sw128_off(r, 4 * h + i), z);
+                    }
+                }
+                // B: both planes of X, 16-byte chunks; consecutive threads take consecutive
+                // chunks of a token row
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int idx = tid + TC_PROD * i, plane = idx >> 10, rem = idx & 1023;
+                    const int t = rem >> 3, c = rem & 7;
+                    const __half* X = plane ? Xl : Xh;
+                    uint4 v = make_uint4(0, 0, 0, 0);
+                    if (n0 + t < T) v = __ldg(reinterpret_cast<const uint4*>(X + (size_t)(n0 + t) * cols + k0) + c);
+                    sts128(st + (2 + plane) * TC_TILE + sw128_off(t, c), v);
+                }
+            }
+            // the tensor core reads these tiles through the async proxy
+            fence_proxy_async_smem();
+            mbar_arrive(&full[s]);
+        }
+        // ---- epilogue: TMEM lanes 32 (warp % 4) .. = tile rows, columns 64 (warp / 4) ..
+        // tcgen05.ld is warp-collective: the whole warp takes the same branch
+        const bool have = __all_sync(0xffffffffu, mbar_wait(&acc_full, 0, &g_gemm_fault, 33));
+        tc_fence_after();
+        if (have) {
+            const int q = warp & 3, orow = m0 + 32 * q + (tid & 31);
+            for (int c0 = 64 * (warp >> 2); c0 < 64 * (warp >> 2) + 64; c0 += 32) {
+                uint32_t v[32];
+                tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+                if (orow < rows) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int t = n0 + c0 + j;
+                        if (t < T) Y[(size_t)t * rows + orow] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+        }
+    } else if (tid == TC_PROD) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = tc_idesc(TC_M, TC_N);
+        bool ok = true;
+        for (int kt = 0; kt < n_k && ok; ++kt) {
+            const int s = kt % TC_STAGES, u = kt / TC_STAGES;
+            if (!mbar_wait(&full[s], u & 1, &g_gemm_fault, 32)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t st = base + (uint32_t)(s * TC_STAGE);
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                const uint32_t off = (uint32_t)kk * 32;  // 16 fp16 columns
+                const uint64_t ah = sw128_desc(st + off), al = sw128_desc(st + TC_TILE + off);
+                const uint64_t bh = sw128_desc(st + 2 * TC_TILE + off);
+                const uint64_t bl = sw128_desc(st + 3 * TC_TILE + off);
+                tc_mma(tmem, ah, bh, idesc, (kt | kk) != 0);
+                tc_mma(tmem, ah, bl, idesc, 1u);
+                tc_mma(tmem, al, bh, idesc, 1u);
+            }
+            tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        tc_commit(&acc_full);  // completes after every MMA issued above
+    }
+    // every thread's tensor-memory use is over before the allocation is returned
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_N)
+                     : "memory");
+    }
+}
+
+// X (FP32) -> FP16 hi/lo planes.
+__global__ void split_x_kernel(const float* __restrict__ X, __half* __restrict__ Xh,
+                               __half* __restrict__ Xl, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float v = X[i];
+        const __half h = __float2half_rn(v);
+        Xh[i] = h;
+        Xl[i] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+template <int TYPE>
+static int launch_tc(const void* W, const float* X, float* Y, int T, int rows, int cols,
+                     cudaStream_t st) {
+    const size_t n = (size_t)T * cols;
+    void* ws = nullptr;
+    int r = workspace_get(WS_GEMM, 2 * n * sizeof(__half) + 256, &ws);
+    if (r) return r;
+    __half* Xh = (__half*)ws;
+    __half* Xl = Xh + n;
+    const int g = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    split_x_kernel<<<g, 256, 0, st>>>(X, Xh, Xl, n);
+    IB_LAUNCH_CHECK("split_x_kernel");
+    auto kern = gemm_tc_kernel<TYPE>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    IB_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 64 && !attr_set[dev]) {
+        IB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)tc_smem_bytes<TYPE>()));
+        attr_set[dev] = true;
+    }
+    const dim3 grid((rows + TC_M - 1) / TC_M, (T + TC_N - 1) / TC_N);
+    IB_REQUIRE(grid.y <= 65535, "gemm: too many tokens");
+    const int64_t row_bytes = packed_bytes(TYPE, 1, cols);
+    kern<<<grid, TC_THREADS, tc_smem_bytes<TYPE>(), st>>>((const uint8_t*)W, Xh, Xl, Y, T, rows, cols,
+                                                           row_bytes);
+    IB_LAUNCH_CHECK("gemm_tc_kernel");
+    return IB_OK;
+}
+
+// Runs of 256 columns; Q6_K rows must end on 16-byte boundaries (cols % 2048 == 0) so the
+// 16-byte staging loads stay inside the weights.
+bool gemm_tc_supported(int type, int64_t T, int64_t rows, int64_t cols) {
+    return is_block_quant(type) && T >= 1 && rows >= 1 && cols % TC_SEGC == 0 &&
+           (type != IB_TYPE_Q6_K || cols % 2048 == 0) && T * cols < (1ll << 31) &&
+           rows < (1ll << 31);
+}
+
+int gemm_q_tc(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
+              cudaStream_t st) {
+    switch (type) {
+        case IB_TYPE_Q4_0: return launch_tc<IB_TYPE_Q4_0>(W, X, Y, T, rows, cols, st);
+        case IB_TYPE_Q5_0: return launch_tc<IB_TYPE_Q5_0>(W, X, Y, T, rows, cols, st);
+        case IB_TYPE_Q5_1: return launch_tc<IB_TYPE_Q5_1>(W, X, Y, T, rows, cols, st);
+        case IB_TYPE_Q8_0: return launch_tc<IB_TYPE_Q8_0>(W, X, Y, T, rows, cols, st);
+        case IB_TYPE_Q4_K: return launch_tc<IB_TYPE_Q4_K>(W, X, Y, T, rows, cols, st);
+        case IB_TYPE_Q6_K: return launch_tc<IB_TYPE_Q6_K>(W, X, Y, T, rows, cols, st);
+    }
+    set_error("gemm: unsupported type");
+    return IB_ERR_UNSUPPORTED;
+}
+
+int gemm_fault_take(int* code) {
+    int v = 0, z = 0;
+    IB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_gemm_fault, sizeof(int)));
+    if (v) IB_CUDA_CHECK(cudaMemcpyToSymbol(g_gemm_fault, &z, sizeof(int)));
+    *code = v;
+    return IB_OK;
+}
+
+}  // namespace ib

@@ -594,6 +594,15 @@ extern "C" int ib_gemm_i16(const int16_t* W, const float* row_scale, const float
     return launch_gemm<IB_TYPE_I16>(W, row_scale, X, Y, T, M, K, as_stream(stream));
 }
 
+// 0: tensor-core GEMM where the shape allows (default); 1: the CUDA-core tiles.
+static int g_gemm_path = 0;
+
+extern "C" int ib_gemm_set_path(int path) {
+    IB_REQUIRE(path == 0 || path == 1, "gemm path must be 0 (tensor cores) or 1 (CUDA cores)");
+    g_gemm_path = path;
+    return IB_OK;
+}
+
 extern "C" int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float* dev_Y,
                          int64_t T, int64_t rows, int64_t cols, void* stream) {
     if (T == 0 || rows == 0) return IB_OK;
@@ -604,5 +613,7 @@ extern "C" int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float*
         return IB_ERR_UNSUPPORTED;
     }
     IB_REQUIRE(cols % block_elems(type) == 0, "cols must be a multiple of the block size");
+    if (gemm_tc_supported(type, T, rows, cols) && g_gemm_path == 0)
+        return gemm_q_tc(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, as_stream(stream));
     return gemm_q_simt(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, as_stream(stream));
 }

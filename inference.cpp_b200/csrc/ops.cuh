@@ -6,7 +6,7 @@
 
 namespace ib {
 
-enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_SLOTS = 2 };
+enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_GEMM = 2, WS_SLOTS = 3 };
 int workspace_get(int slot, size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
 // Decode attention in one launch (split flash-decode, last-CTA combine); also writes
@@ -36,6 +36,11 @@ int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hk
 int argmax_launch(const float* x, int n, int32_t* out, cudaStream_t st);
 // op: 0 silu(a), 1 a *= b, 2 a += b
 int elementwise_launch(int op, float* a, const float* b, int n, cudaStream_t st);
+// Prefill GEMM on the tensor cores (gemm_tc.cu): packed weights, cols % 64 == 0.
+bool gemm_tc_supported(int type, int64_t T, int64_t rows, int64_t cols);
+int gemm_q_tc(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
+              cudaStream_t st);
+int gemm_fault_take(int* code);
 int gemm_q_simt(int type, const void* W, const float* X, float* Y, int T, int M, int K,
                 cudaStream_t st);
 

@@ -130,6 +130,28 @@ def test_gemm_q_vs_oracle(cuda, port, type_):
 
 
 @pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
+@pytest.mark.parametrize("path", [ib.GEMM_TENSOR_CORES, ib.GEMM_CUDA_CORES], ids=["tcgen05", "simt"])
+def test_gemm_q_paths_vs_oracle(cuda, port, type_, path):
+    """Both prefill GEMM kernels against the oracle's FP32 dequantisation: tiles with
+    ragged edges in rows and tokens, K running through every pipeline stage many times."""
+    rng = np.random.default_rng(700 + type_)
+    try:
+        ib.gemm_set_path(path)
+        for T, rows, cols in [(257, 300, 2048), (128, 128, 4096), (17, 513, 1536)]:
+            blk = ib.synth_host(type_, rows, cols, seed=7000 + T + rows + type_)
+            X = rng.standard_normal((T, cols)).astype(np.float32)
+            W = port.dequantize(type_, blk, rows * cols).reshape(rows, cols)
+            Y_ref = X.astype(np.float64) @ W.T.astype(np.float64)
+            Y = ib.gemm_q(type_, to_dev(cuda, blk), to_dev(cuda, X), T, rows, cols).cpu().numpy()
+            Y = Y.reshape(T, rows)
+            bound = GEMV_RTOL * (np.abs(X.astype(np.float64)) @ np.abs(W.T.astype(np.float64))) + 1e-30
+            assert np.all(np.abs(Y - Y_ref) <= bound), (T, rows, cols)
+        assert ib.check_fault() == 0
+    finally:
+        ib.gemm_set_path(ib.GEMM_TENSOR_CORES)
+
+
+@pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
 def test_embedding_q(cuda, port, type_):
     vocab, dim = 300, 512
     blk = ib.synth_host(type_, vocab, dim, seed=6000 + type_)
