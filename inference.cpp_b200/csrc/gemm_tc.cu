@@ -3,7 +3,7 @@
 // matmul (src/ops/cuda_backend.cpp gemm kernels, called from prefill in
 // src/models/model_cuda.cpp:293-368).
 //
-// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64.  Eight
+// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64.  Sixteen
 // producer warps stage, per 256 columns, the tile rows' packed blocks in shared memory
 // with coalesced 16-byte loads; per 64-column step they dequantise them (the
 // bit-exact element expressions of quant.cuh) and copy the 128 tokens x 64 columns of
@@ -14,7 +14,7 @@
 // producers.  The three products keep each term to about 2^-21 of its value, so the
 // GEMM matches an FP32 matmul to rounding (the dropped lo.lo term is below 2^-22).
 // The epilogue warps read the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32(w%4).. = tile rows, columns 64(w/4)..) and store Y.  Every mbarrier wait is
+// 32(w%4).. = tile rows, columns 32(w/4)..) and store Y.  Every mbarrier wait is
 // bounded (fault word, as in the other pipelines) and the producers' named barriers
 // are reached by every producer on every step whatever failed; the MMA thread always
 // ends with a commit the epilogue waits for, so tensor memory is released only after
@@ -39,8 +39,9 @@ constexpr int TC_SEGC = 256;   // columns per staged run of packed blocks
 constexpr int TC_STAGES = 2;
 constexpr int TC_TILE = TC_M * TC_BK * 2;  // bytes of one fp16 operand tile (16 KB)
 constexpr int TC_STAGE = 4 * TC_TILE;      // A hi, A lo, B hi, B lo
-constexpr int TC_PROD = 256;               // producer / epilogue threads (8 warps)
+constexpr int TC_PROD = 512;               // producer / epilogue threads (16 warps)
 constexpr int TC_THREADS = TC_PROD + 32;   // + the MMA warp
+static_assert(TC_PROD % 128 == 0 && 2048 % TC_PROD == 0, "producer mapping");
 
 // Packed bytes of 256 columns of a row, and their row stride in shared memory (16 x an
 // odd number, so 16-byte loads of 8 consecutive rows hit distinct bank groups; Q6_K's
@@ -57,8 +58,8 @@ struct RawSeg {
 };
 
 template <int TYPE>
-constexpr size_t tc_smem_bytes() {
-    return (size_t)TC_STAGES * TC_STAGE + (size_t)TC_M * RawSeg<TYPE>::RS + 1024;
+constexpr size_t tc_smem_bytes() {  // fp16 stages, two staged runs, alignment slack
+    return (size_t)TC_STAGES * TC_STAGE + 2 * (size_t)TC_M * RawSeg<TYPE>::RS + 1024;
 }
 
 // ---- tcgen05 building blocks (inline PTX) ----------------------------------------------
@@ -145,6 +146,21 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                  : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (zero-filled when !valid); completion is
+// tracked through cp_async_arrive on an mbarrier.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+// Arrives on bar once every cp.async this thread issued so far has landed (the arrival
+// is counted in the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void bar_producers() {
     asm volatile("bar.sync 1, %0;" ::"r"(TC_PROD) : "memory");
 }
@@ -155,23 +171,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                    const __half* __restrict__ Xl, float* __restrict__ Y, int T, int rows, int cols,
                    int64_t row_bytes) {
     using R = RawSeg<TYPE>;
+    constexpr int RUN = TC_SEGC / TC_BK;  // 64-column steps per staged run
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], acc_full;
+    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], rawfull[2], acc_full;
     __shared__ uint32_t tmem_base;
     const int warp = threadIdx.x >> 5, tid = threadIdx.x;
     const int m0 = blockIdx.x * TC_M, n0 = blockIdx.y * TC_N;
-    const int n_k = cols / TC_BK;
+    const int n_k = cols / TC_BK, n_run = cols / TC_SEGC;
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-    uint8_t* const raw = smem_raw + (base - smem_u32(smem_raw)) + TC_STAGES * TC_STAGE;
+    const uint32_t raw_s = base + TC_STAGES * TC_STAGE;  // two runs of 128 x RS bytes
+    uint8_t* const raw = smem_raw + (raw_s - smem_u32(smem_raw));
     if (tid == 0) {
         for (int s = 0; s < TC_STAGES; ++s) {
-            mbar_init(&full[s], TC_PROD);
+            mbar_init(&full[s], 2 * TC_PROD);  // dequant arrivals + B-copy arrivals
             mbar_init(&empty[s], 1);
         }
+        for (int b = 0; b < 2; ++b) mbar_init(&rawfull[b], TC_PROD);
         mbar_init(&acc_full, 1);
         fence_mbar_init();
     }
-    if (warp == 8) {  // tensor-memory accumulator: 128 lanes x TC_N FP32 columns
+    if (warp == TC_PROD / 32) {  // tensor-memory accumulator: 128 lanes x TC_N FP32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&tmem_base)),
                      "r"(TC_N)
@@ -183,87 +202,97 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base;
 
-    if (warp < 8) {
-        const int r = tid & 127, h = tid >> 7;  // dequant: tile row r, columns 32h..32h+31
+    if (warp < TC_PROD / 32) {
+        // packed bytes of columns [256 j, 256 j + 256) of the tile rows -> run buffer j & 1
+        auto stage_run = [&](int j) {
+            const uint32_t dst = raw_s + (uint32_t)((j & 1) * TC_M * R::RS);
+            for (int i = tid; i < TC_M * R::NCH; i += TC_PROD) {
+                const int rr = i / R::NCH, c = i - rr * R::NCH;
+                if (m0 + rr >= rows) continue;
+                const int64_t start = (int64_t)(m0 + rr) * row_bytes + (int64_t)j * R::SEG;
+                const int64_t a0 = start & ~(int64_t)15;
+                if (a0 + 16 * c >= start + R::SEG) continue;  // beyond this run
+                cp_async16(dst + (uint32_t)(rr * R::RS + 16 * c), W + a0 + 16 * c, true);
+            }
+            cp_async_arrive(&rawfull[j & 1]);
+        };
+        const int r = tid & 127, h = tid >> 7;  // dequant: tile row r, columns 16h..16h+15
         const int row = m0 + r;
         bool ok = true;
+        stage_run(0);
         for (int kt = 0; kt < n_k; ++kt) {
-            const int s = kt % TC_STAGES, u = kt / TC_STAGES, sub = kt % (TC_SEGC / TC_BK);
+            const int s = kt % TC_STAGES, u = kt / TC_STAGES, sub = kt % RUN, j = kt / RUN;
             const int k0 = kt * TC_BK;
             if (sub == 0) {
-                // stage the packed bytes of columns [k0, k0 + 256) of the 128 tile rows
-                bar_producers();  // everyone is done with the previous run
-                const int64_t seg = k0 / TC_SEGC;
-                for (int i = tid; i < TC_M * R::NCH; i += TC_PROD) {
-                    const int rr = i / R::NCH, c = i - rr * R::NCH;
-                    if (m0 + rr >= rows) continue;
-                    const int64_t start = (int64_t)(m0 + rr) * row_bytes + seg * R::SEG;
-                    const int64_t a0 = start & ~(int64_t)15;
-                    if (a0 + 16 * c >= start + R::SEG) continue;  // beyond this run
-                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(W + a0) + c);
-                    *reinterpret_cast<uint4*>(raw + rr * R::RS + 16 * c) = v;
-                }
-                bar_producers();
+                bar_producers();  // everyone is done with run j - 1: its buffer takes run j + 1
+                if (j + 1 < n_run) stage_run(j + 1);
+                if (ok && !mbar_wait(&rawfull[j & 1], (j >> 1) & 1, &g_gemm_fault, 34)) ok = false;
             }
             if (u > 0 && ok && !mbar_wait(&empty[s], (u - 1) & 1, &g_gemm_fault, 31)) ok = false;
             const uint32_t st = base + (uint32_t)(s * TC_STAGE);
             if (ok) {
-                // A: 32 columns of tile row r from the staged run
-                if (row < rows) {
-                    const int64_t start = (int64_t)row * row_bytes + (int64_t)(k0 / TC_SEGC) * R::SEG;
-                    const uint8_t* run = raw + r * R::RS + (int)(start & 15);
+                // B: both planes of X, asynchronously; consecutive threads take consecutive
+                // 16-byte chunks of a token row
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int kc = sub * TC_BK + 32 * h + 8 * i;  // column within the run
+                for (int i = 0; i < 2048 / TC_PROD; ++i) {
+                    const int idx = tid + TC_PROD * i, plane = idx >> 10, rem = idx & 1023;
+                    const int t = rem >> 3, c = rem & 7;
+                    const __half* X = plane ? Xl : Xh;
+                    const bool valid = n0 + t < T;
+                    const __half* src = X + (size_t)(valid ? n0 + t : 0) * cols + k0 + 8 * c;
+                    cp_async16(st + (2 + plane) * TC_TILE + sw128_off(t, c), src, valid);
+                }
+            }
+            cp_async_arrive(&full[s]);
+            if (ok) {
+                // A: 16 columns of tile row r from the staged run
+                constexpr int CPT = TC_BK / 8 / (TC_PROD / TC_M);  // 16-byte chunks per thread
+                if (row < rows) {
+                    const int64_t start = (int64_t)row * row_bytes + (int64_t)j * R::SEG;
+                    const uint8_t* run = raw + (j & 1) * TC_M * R::RS + r * R::RS + (int)(start & 15);
+#pragma unroll
+                    for (int i = 0; i < CPT; ++i) {
+                        const int kc = sub * TC_BK + 8 * (CPT * h + i);  // column within the run
                         float v[8];
                         deq8<TYPE, GenericBytes>(run + (kc / R::BE) * R::BB, (kc % R::BE) >> 3, v);
                         uint4 hi, lo;
                         split8(v, hi, lo);
-                        sts128(st + sw128_off(r, 4 * h + i), hi);
-                        sts128(st + TC_TILE + sw128_off(r, 4 * h + i), lo);
+                        sts128(st + sw128_off(r, CPT * h + i), hi);
+                        sts128(st + TC_TILE + sw128_off(r, CPT * h + i), lo);
                     }
                 } else {
                     const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        sts128(st + sw128_off(r, 4 * h + i), z);
-                        sts128(st + TC_TILE + sw128_off(r, 4 * h + i), z);
+                    for (int i = 0; i < CPT; ++i) {
+                        sts128(st + sw128_off(r, CPT * h + i), z);
+                        sts128(st + TC_TILE + sw128_off(r, CPT * h + i), z);
                     }
-                }
-                // B: both planes of X, 16-byte chunks; consecutive threads take consecutive
-                // chunks of a token row
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int idx = tid + TC_PROD * i, plane = idx >> 10, rem = idx & 1023;
-                    const int t = rem >> 3, c = rem & 7;
-                    const __half* X = plane ? Xl : Xh;
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (n0 + t < T) v = __ldg(reinterpret_cast<const uint4*>(X + (size_t)(n0 + t) * cols + k0) + c);
-                    sts128(st + (2 + plane) * TC_TILE + sw128_off(t, c), v);
                 }
             }
             // the tensor core reads these tiles through the async proxy
             fence_proxy_async_smem();
             mbar_arrive(&full[s]);
         }
-        // ---- epilogue: TMEM lanes 32 (warp % 4) .. = tile rows, columns 64 (warp / 4) ..
+        // ---- epilogue: TMEM lanes 32 (warp % 4) .. = tile rows, columns 32 (warp / 4) ..
         // tcgen05.ld is warp-collective: the whole warp takes the same branch
         const bool have = __all_sync(0xffffffffu, mbar_wait(&acc_full, 0, &g_gemm_fault, 33));
         tc_fence_after();
         if (have) {
             const int q = warp & 3, orow = m0 + 32 * q + (tid & 31);
-            for (int c0 = 64 * (warp >> 2); c0 < 64 * (warp >> 2) + 64; c0 += 32) {
+            for (int c0 = 32 * (warp >> 2); c0 < TC_N; c0 += 32 * (TC_PROD / 128)) {
                 uint32_t v[32];
                 tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
                 if (orow < rows) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int t = n0 + c0 + j;
-                        if (t < T) Y[(size_t)t * rows + orow] = __uint_as_float(v[j]);
+                    for (int jj = 0; jj < 32; ++jj) {
+                        const int t = n0 + c0 + jj;
+                        if (t < T) Y[(size_t)t * rows + orow] = __uint_as_float(v[jj]);
                     }
                 }
             }
         }
+        // no copy of this thread may still be landing when the CTA ends
+        asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (tid == TC_PROD) {
         // ---- MMA issuer
         constexpr uint32_t idesc = tc_idesc(TC_M, TC_N);
@@ -274,6 +303,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 ok = false;
                 break;
             }
+            // the B tiles came through cp.async, the A tiles through stores: both reach the
+            // tensor core's (async) proxy through this fence
+            fence_proxy_async_smem();
             tc_fence_after();
             const uint32_t st = base + (uint32_t)(s * TC_STAGE);
 #pragma unroll
@@ -293,7 +325,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // every thread's tensor-memory use is over before the allocation is returned
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == TC_PROD / 32) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_N)
                      : "memory");
