@@ -184,6 +184,44 @@ def time_gemv(ib, cfg, seed=20261201):
     return nbytes, ms, reps
 
 
+def time_gemm(ib, cfg, T, seed=20261201):
+    """The prefill GEMM (tcgen05) on the ffn_gate shape: Y[T, ffn] = X[T, dim] . W^T with
+    Q4_K weights, timed with events on its stream over 3 launches after one warm-up; one
+    more launch sits in an NVTX range named gemm_roofline (for a profiler)."""
+    import torch
+    from inference_cpp_b200 import gguf_writer as gw
+    rows, cols = cfg.ffn, cfg.dim
+    W = ib.synth_device(ib.Q4_K, rows, cols, gw.tensor_seed(seed + 2, "gemm"), 0.02)
+    X = torch.randn(T * cols, device="cuda")
+    Y = torch.empty(T * rows, device="cuda")
+    s = torch.cuda.current_stream()
+    ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record(s)
+    for _ in range(reps):
+        ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    torch.cuda.nvtx.range_push("gemm_roofline")
+    ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    del W, X, Y
+    torch.cuda.empty_cache()
+    return 2.0 * T * rows * cols, ms
+
+
+def measured_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), "measured"
+    return 1590.0, "fallback"
+
+
 def traffic_from_profile():
     p = os.path.join(ROOT, "profiles", "gemv_q4k_14336x4096_traffic.json")
     if os.path.exists(p):
@@ -346,6 +384,8 @@ def main():
 
     kernels_per_step = m.step_kernels()
     nbytes, gemv_ms, gemv_reps = time_gemv(ib, cfg)
+    gemm_flops, gemm_ms = time_gemm(ib, cfg, args.prompt)
+    tpeak, tpeak_kind = measured_tensor_peak()
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (gemv_ms * 1e-3) / 1e9
     weight_bytes = m.weight_bytes()
@@ -387,7 +427,13 @@ def main():
                            "achieved_gbs": weight_bytes * value / seqs / 1e9,
                            "frac": weight_bytes * value / seqs / 1e9 / peak},
             "prefill": {"tokens": args.prompt, "ms": prefill_ms,
-                        "tok_s": args.prompt / (prefill_ms * 1e-3)},
+                        "tok_s": args.prompt / (prefill_ms * 1e-3),
+                        "gemm": {"kernel": f"gemm_tc Q4_K {cfg.ffn}x{cfg.dim}, T={args.prompt}",
+                                 "ms": gemm_ms, "tflops": gemm_flops / (gemm_ms * 1e-3) / 1e12,
+                                 "peak": tpeak, "peak_kind": tpeak_kind,
+                                 "frac": gemm_flops / (gemm_ms * 1e-3) / 1e12 / tpeak,
+                                 "note": "useful flops 2*T*rows*cols; the kernel issues 3 fp16 "
+                                         "MMAs per product (hi/lo operand pairs)"}},
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": kernels_per_step * args.steps,

@@ -161,6 +161,78 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
                  : "memory");
 }
 
+// ---- 16-element decoders for blocks staged in shared memory --------------------------
+// The element expressions are deq8's (bit-exact); the bytes come from 16-byte loads.
+
+// Byte k of the 12 scale bytes held in three words.
+__device__ __forceinline__ int scale_byte(uint32_t s0, uint32_t s1, uint32_t s2, int k) {
+    const uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
+    return (int)((w >> (8 * (k & 3))) & 0xFFu);
+}
+
+// Q4_K elements e0..e0+15 (e0 % 16 == 0) of a 16-byte-aligned block.
+__device__ __forceinline__ void deq16_q4k(const uint8_t* blk, int e0, float* y) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+    const int sb = e0 >> 5, p = sb >> 1, h = sb & 1, l0 = e0 & 31;
+    const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * p + l0);
+    const float d = h2f(hd.x & 0xFFFFu), dmin = h2f(hd.x >> 16);
+    int sc, m;  // get_scale_min_k4(sb)
+    if (sb < 4) {
+        sc = scale_byte(hd.y, hd.z, hd.w, sb) & 63;
+        m = scale_byte(hd.y, hd.z, hd.w, sb + 4) & 63;
+    } else {
+        sc = (scale_byte(hd.y, hd.z, hd.w, sb + 4) & 0xF) | ((scale_byte(hd.y, hd.z, hd.w, sb - 4) >> 6) << 4);
+        m = (scale_byte(hd.y, hd.z, hd.w, sb + 4) >> 4) | ((scale_byte(hd.y, hd.z, hd.w, sb) >> 6) << 4);
+    }
+    const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int v = (int)((w[i >> 2] >> (8 * (i & 3) + 4 * h)) & 0xFu);
+        y[i] = __fsub_rn(__fmul_rn(d1, (float)v), m1);
+    }
+}
+
+// 16 bytes at byte offset off (even) of a 16-byte-aligned staged row, as four words;
+// the offset's position within 16 bytes is the same for every thread of the warp.
+__device__ __forceinline__ void lds16_at(const uint8_t* row, int off, uint32_t (&o)[4]) {
+    const int a = off & ~15, sh = off & 15;
+    const uint4 x = *reinterpret_cast<const uint4*>(row + a);
+    const uint4 z = *reinterpret_cast<const uint4*>(row + a + 16);
+    const uint32_t w[8] = {x.x, x.y, x.z, x.w, z.x, z.y, z.z, z.w};
+    const uint32_t bs = (uint32_t)(sh & 3) * 8;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t lo, hi;
+        switch (sh >> 2) {  // warp-uniform
+            case 0: lo = w[k]; hi = w[k + 1]; break;
+            case 1: lo = w[k + 1]; hi = w[k + 2]; break;
+            case 2: lo = w[k + 2]; hi = w[k + 3]; break;
+            default: lo = w[k + 3]; hi = w[k + 4]; break;
+        }
+        o[k] = __funnelshift_r(lo, hi, bs);
+    }
+}
+
+// Q6_K elements e0..e0+15 (e0 % 16 == 0) of the block at byte offset o (even, < 16)
+// of a 16-byte-aligned staged row.
+__device__ __forceinline__ void deq16_q6k(const uint8_t* row, int o, int e0, float* y) {
+    const int c = e0 >> 7, r = e0 & 127, gg = r >> 5, l0 = r & 31;
+    uint32_t ql[4], qh[4];
+    lds16_at(row, o + 64 * c + 32 * (gg & 1) + l0, ql);
+    lds16_at(row, o + 128 + 32 * c + l0, qh);
+    const float d = h2f(*reinterpret_cast<const unsigned short*>(row + o + 208));
+    const int sc = (int)(int8_t)row[o + 192 + 8 * c + 2 * gg + (l0 >> 4)];
+    const float ds = __fmul_rn(d, (float)sc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int lo = (int)((ql[i >> 2] >> (8 * (i & 3) + 4 * (gg >> 1))) & 0xFu);
+        const int hi = (int)((qh[i >> 2] >> (8 * (i & 3) + 2 * gg)) & 3u);
+        const int q = (int)(int8_t)(lo | (hi << 4)) - 32;
+        y[i] = __fmul_rn(ds, (float)q);
+    }
+}
+
 __device__ __forceinline__ void bar_producers() {
     asm volatile("bar.sync 1, %0;" ::"r"(TC_PROD) : "memory");
 }
@@ -249,16 +321,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 constexpr int CPT = TC_BK / 8 / (TC_PROD / TC_M);  // 16-byte chunks per thread
                 if (row < rows) {
                     const int64_t start = (int64_t)row * row_bytes + (int64_t)j * R::SEG;
-                    const uint8_t* run = raw + (j & 1) * TC_M * R::RS + r * R::RS + (int)(start & 15);
+                    const uint8_t* srow = raw + (j & 1) * TC_M * R::RS + r * R::RS;
+                    const int o = (int)(start & 15);
+                    if constexpr (TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K) {
+                        static_assert(CPT == 2, "16 columns per thread");
+                        float v[16];
+                        if constexpr (TYPE == IB_TYPE_Q4_K) deq16_q4k(srow, sub * TC_BK + 16 * h, v);
+                        else deq16_q6k(srow, o, sub * TC_BK + 16 * h, v);
 #pragma unroll
-                    for (int i = 0; i < CPT; ++i) {
-                        const int kc = sub * TC_BK + 8 * (CPT * h + i);  // column within the run
-                        float v[8];
-                        deq8<TYPE, GenericBytes>(run + (kc / R::BE) * R::BB, (kc % R::BE) >> 3, v);
-                        uint4 hi, lo;
-                        split8(v, hi, lo);
-                        sts128(st + sw128_off(r, CPT * h + i), hi);
-                        sts128(st + TC_TILE + sw128_off(r, CPT * h + i), lo);
+                        for (int i = 0; i < 2; ++i) {
+                            uint4 hi, lo;
+                            split8(v + 8 * i, hi, lo);
+                            sts128(st + sw128_off(r, 2 * h + i), hi);
+                            sts128(st + TC_TILE + sw128_off(r, 2 * h + i), lo);
+                        }
+                    } else {
+                        const uint8_t* run = srow + o;
+#pragma unroll
+                        for (int i = 0; i < CPT; ++i) {
+                            const int kc = sub * TC_BK + 8 * (CPT * h + i);  // column within the run
+                            float v[8];
+                            deq8<TYPE, GenericBytes>(run + (kc / R::BE) * R::BB, (kc % R::BE) >> 3, v);
+                            uint4 hi, lo;
+                            split8(v, hi, lo);
+                            sts128(st + sw128_off(r, CPT * h + i), hi);
+                            sts128(st + TC_TILE + sw128_off(r, CPT * h + i), lo);
+                        }
                     }
                 } else {
                     const uint4 z = make_uint4(0, 0, 0, 0);
