@@ -619,4 +619,211 @@ int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos) {
     return IB_OK;
 }
 
+// ---- prefill attention: causal, GQA, FP32 flash attention ---------------------------
+// One CTA per (kv head, 64 query rows): rows r = g * QT + tq are (query head g of the
+// group, query q0 + tq), QT = 64 / G, so the group's heads share every K/V tile.  K and
+// V tiles of 32 positions arrive by cp.async, double-buffered.  Thread (ty, tx) of the
+// 16 x 16 grid holds S for rows ty + 16i, columns tx + 16j (K rows of neighbouring
+// threads are neighbours: conflict-free 16-byte loads with the 4-float row pad), the
+// online-softmax state of its four rows (reduced over the 16 lanes sharing them), and
+// O for the same rows, columns 4 tx + 64 j.  Scores are dot * scale as the reference
+// (src/ops/cuda_kernels.cu attention_batch_kernel); the softmax is rescaled per tile.
+constexpr int AP_BQ = 64, AP_BK = 32;
+
+template <int HD>
+constexpr size_t attn_prefill_smem() {
+    return ((size_t)AP_BQ * (HD + 4) + 2 * (size_t)AP_BK * (HD + 4) + 2 * (size_t)AP_BK * HD +
+            (size_t)AP_BQ * (AP_BK + 4)) * sizeof(float);
+}
+
+__device__ __forceinline__ void ap_cp16(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256, 2)
+    attn_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                        const float* __restrict__ vc, float* __restrict__ out, int H, int Hkv,
+                        int max_seq, int start, int T, float scale) {
+    constexpr int QS = HD + 4, PS = AP_BK + 4, OC = HD / 64;
+    extern __shared__ __align__(16) float apsm[];
+    float* Qs = apsm;                   // [64][QS]
+    float* Ks = Qs + AP_BQ * QS;        // [2][32][QS]
+    float* Vs = Ks + 2 * AP_BK * QS;    // [2][32][HD]
+    float* Ps = Vs + 2 * AP_BK * HD;    // [64][PS]
+    const int G = H / Hkv, QT = AP_BQ / G;
+    const int hk = blockIdx.y;
+    const int q0 = (gridDim.x - 1 - blockIdx.x) * QT;  // the longest rows first
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    for (int i = tid; i < AP_BQ * HD / 4; i += 256) {
+        const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+        const int t = q0 + r % QT;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < T)
+            v = *reinterpret_cast<const float4*>(q + ((size_t)t * H + hk * G + r / QT) * HD + 4 * c4);
+        *reinterpret_cast<float4*>(Qs + r * QS + 4 * c4) = v;
+    }
+    const int kv_end = start + (q0 + QT < T ? q0 + QT : T);  // positions [0, kv_end)
+    const int n_tiles = (kv_end + AP_BK - 1) / AP_BK;
+    const float* kh = kc + (size_t)hk * max_seq * HD;
+    const float* vh = vc + (size_t)hk * max_seq * HD;
+    auto load_kv = [&](int tile, int buf) {
+        for (int i = tid; i < AP_BK * HD / 4; i += 256) {
+            const int rr = i / (HD / 4), c4 = i - rr * (HD / 4);
+            const int pos = tile * AP_BK + rr;
+            const bool valid = pos < kv_end;
+            const size_t off = (size_t)(valid ? pos : 0) * HD + 4 * c4;
+            ap_cp16(Ks + (buf * AP_BK + rr) * QS + 4 * c4, kh + off, valid);
+            ap_cp16(Vs + (buf * AP_BK + rr) * HD + 4 * c4, vh + off, valid);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    int qp[4];
+    float m[4], l[4];
+    float4 o[4][OC];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        qp[i] = start + q0 + (ty + 16 * i) % QT;
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < OC; ++j) o[i][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    load_kv(0, 0);
+    for (int tile = 0; tile < n_tiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < n_tiles) {
+            load_kv(tile + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const float* Kb = Ks + buf * AP_BK * QS;
+        const float* Vb = Vs + buf * AP_BK * HD;
+        float sc[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = 0.f;
+#pragma unroll 4
+        for (int k = 0; k < HD; k += 4) {
+            float4 qv[4], kv[2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (ty + 16 * i) * QS + k);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) kv[j] = *reinterpret_cast<const float4*>(Kb + (tx + 16 * j) * QS + k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+                    sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int pos = tile * AP_BK + tx + 16 * j;
+                float v = sc[i][j] * scale;
+                if (pos > qp[i] || pos >= kv_end) v = -INFINITY;
+                sc[i][j] = v;
+                mx = fmaxf(mx, v);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[i], mx);  // finite: position 0 is in every row's range
+            const float alpha = expf(m[i] - mn);
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float pv = expf(sc[i][j] - mn);
+                Ps[(ty + 16 * i) * PS + tx + 16 * j] = pv;
+                sum += pv;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            l[i] = l[i] * alpha + sum;
+            m[i] = mn;
+#pragma unroll
+            for (int j = 0; j < OC; ++j) {
+                o[i][j].x *= alpha;
+                o[i][j].y *= alpha;
+                o[i][j].z *= alpha;
+                o[i][j].w *= alpha;
+            }
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int sp = 0; sp < AP_BK; ++sp) {
+            float4 vv[OC];
+#pragma unroll
+            for (int j = 0; j < OC; ++j) vv[j] = *reinterpret_cast<const float4*>(Vb + sp * HD + 4 * tx + 64 * j);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pv = Ps[(ty + 16 * i) * PS + sp];
+#pragma unroll
+                for (int j = 0; j < OC; ++j) {
+                    o[i][j].x = fmaf(pv, vv[j].x, o[i][j].x);
+                    o[i][j].y = fmaf(pv, vv[j].y, o[i][j].y);
+                    o[i][j].z = fmaf(pv, vv[j].z, o[i][j].z);
+                    o[i][j].w = fmaf(pv, vv[j].w, o[i][j].w);
+                }
+            }
+        }
+        __syncthreads();  // this buffer is refilled two tiles on
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = ty + 16 * i, t = q0 + r % QT;
+        if (t >= T) continue;
+        const float inv = 1.0f / l[i];
+        float* dst = out + ((size_t)t * H + hk * G + r / QT) * HD + 4 * tx;
+#pragma unroll
+        for (int j = 0; j < OC; ++j)
+            *reinterpret_cast<float4*>(dst + 64 * j) =
+                make_float4(o[i][j].x * inv, o[i][j].y * inv, o[i][j].z * inv, o[i][j].w * inv);
+    }
+}
+
+bool attention_prefill_ok(int H, int Hkv, int HD) {
+    if (Hkv <= 0 || H % Hkv) return false;
+    const int G = H / Hkv;
+    return (HD == 64 || HD == 128) && G >= 1 && G <= 64 && AP_BQ % G == 0;
+}
+
+template <int HD>
+static int launch_prefill(const float* q, const float* kc, const float* vc, float* out, int H,
+                          int Hkv, int max_seq, int start, int T, float scale, cudaStream_t st) {
+    static bool attr[64] = {};
+    int dev = 0;
+    IB_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        IB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)attn_prefill_smem<HD>()));
+        attr[dev] = true;
+    }
+    const int QT = AP_BQ / (H / Hkv);
+    const dim3 grid((T + QT - 1) / QT, Hkv);
+    IB_REQUIRE(grid.x <= 0x7FFFFFFF && Hkv <= 65535, "attention: too many rows");
+    attn_prefill_kernel<HD><<<grid, 256, attn_prefill_smem<HD>(), st>>>(q, kc, vc, out, H, Hkv,
+                                                                        max_seq, start, T, scale);
+    IB_LAUNCH_CHECK("attn_prefill_kernel");
+    return IB_OK;
+}
+
+int attention_prefill(const float* q, const float* kc, const float* vc, float* out, int H, int Hkv,
+                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st) {
+    IB_REQUIRE(attention_prefill_ok(H, Hkv, HD), "attention: unsupported shape for the prefill kernel");
+    IB_REQUIRE(T > 0 && start >= 0 && start + T <= max_seq, "attention: positions beyond the cache");
+    if (HD == 128) return launch_prefill<128>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
+    return launch_prefill<64>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
+}
+
 }  // namespace ib

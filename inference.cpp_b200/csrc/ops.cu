@@ -428,6 +428,8 @@ int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hk
 int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
                            cudaStream_t st) {
+    if (attention_prefill_ok(H, Hkv, HD) && T > 0)
+        return attention_prefill(q, kc, vc, out, H, Hkv, HD, max_seq, start, T, scale, st);
     const size_t smem = (size_t)(start + T) * sizeof(float);
     if (smem > 48 * 1024) {
         IB_CUDA_CHECK(cudaFuncSetAttribute(attn_batch_kernel,

@@ -24,6 +24,11 @@ int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
 int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
                      cudaStream_t st, const int* pos_dev, bool pdl = false);
+// Prefill attention as flash attention over K/V tiles (attention.cu): head_dim 64 or 128,
+// H a multiple of Hkv with H / Hkv dividing 64.
+bool attention_prefill_ok(int H, int Hkv, int HD);
+int attention_prefill(const float* q, const float* kc, const float* vc, float* out, int H, int Hkv,
+                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st);
 int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
                            cudaStream_t st);
