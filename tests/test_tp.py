@@ -277,6 +277,31 @@ def _gpu_rank(rank, world, port_no, cfg, prompt, n_new, fused, q):
         dist.destroy_process_group()
 
 
+def _n_gpus() -> int:
+    try:
+        import torch
+        return torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:
+        return 0
+
+
+def _run_tp_ranks(cfg, world, fused, n_new=12):
+    import torch.multiprocessing as mp
+    prompt = np.array([1, 17, 5, 99, 3, 42, 7, 11], dtype=np.int32) % cfg.vocab
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port_no = free_port()
+    procs = [ctx.Process(target=_gpu_rank,
+                         args=(r, world, port_no, cfg, prompt, n_new, fused, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    return prompt, results
+
+
 def _two_gpus():
     try:
         import torch
@@ -312,4 +337,25 @@ def test_tp_generate_matches_oracle_2gpu(port, cfg, fused):
         scale = np.abs(want_logits).max(axis=1, keepdims=True)
         assert np.all(np.abs(logits - want_logits) <= LOGIT_RTOL * scale), rank
         if fused and cfg.name != "tp-q32-tied":
+            assert uses_fused, rank
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "separate"])
+def test_tp_wide_matches_oracle(port, world, fused):
+    """Four or eight ranks (when the machine has them): every rank exchanges with every
+    other over peer memory; tokens and logits as on one GPU."""
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    cfg = tp_tma_cfgs()[0]  # 8 kv heads, vocab 10000: shards evenly over 8 ranks
+    prompt, results = _run_tp_ranks(cfg, world, fused)
+    n_new = 12
+    want, want_logits = port.model(cfg, synth(cfg)).generate(prompt, n_new, want_logits=True)
+    for rank, got, logits, uses_fused in results:
+        assert logits is not None, got
+        assert got == list(want), rank
+        scale = np.abs(want_logits).max(axis=1, keepdims=True)
+        assert np.all(np.abs(logits - want_logits) <= LOGIT_RTOL * scale), rank
+        if fused:
             assert uses_fused, rank
