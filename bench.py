@@ -222,8 +222,10 @@ def measured_tensor_peak():
     return 1590.0, "fallback"
 
 
-def traffic_from_profile():
-    p = os.path.join(ROOT, "profiles", "gemv_q4k_14336x4096_traffic.json")
+def traffic_from_profile(rows, cols):
+    """DRAM bytes per launch of the roofline GEMV from the committed capture of the same
+    shape (profiles/gemv_q4k_<rows>x<cols>_traffic.json), else None."""
+    p = os.path.join(ROOT, "profiles", f"gemv_q4k_{rows}x{cols}_traffic.json")
     if os.path.exists(p):
         try:
             return json.load(open(p)).get("dram_bytes_per_launch")
@@ -419,7 +421,7 @@ def main():
             "e2e": {"value": seqs * e2e_steps / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic_from_profile(),
+                         "frac": achieved / peak, "traffic": traffic_from_profile(cfg.ffn, cfg.dim),
                          "kernel": f"gemv_q Q4_K {cfg.ffn}x{cfg.dim}",
                          "bytes_per_launch": nbytes, "avg_launch_us": gemv_ms * 1e3,
                          "peak_kind": peak_kind},
