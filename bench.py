@@ -89,7 +89,7 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -144,7 +144,10 @@ def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201, comm=
 def time_gemv(ib, cfg, seed=20261201):
     """The decode GEMV kernel on the ffn_gate shape (Q4_K), over min(n_layers, 32) distinct
     weight matrices (larger than L2 together), its limb slab computed once: CUDA-graph
-    replays of the kernel alone, timed with events on the replay stream."""
+    replays of the kernel alone, timed with events on the replay stream.  Returns the
+    per-launch time as a chain with programmatic dependent launch (how the decode step
+    runs it: each launch streams its weights while the previous one finishes) and as
+    standalone launches."""
     import torch
     from inference_cpp_b200 import gguf_writer as gw
     rows, cols = cfg.ffn, cfg.dim
@@ -165,23 +168,26 @@ def time_gemv(ib, cfg, seed=20261201):
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     reps = 4 * n
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
-        for i in range(reps):
-            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):  # the replay and its events on one stream
-        g.replay()
+    out = {}
+    for chained in (True, False):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y, chained=chained)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):  # the replay and its events on one stream
+            g.replay()
+            torch.cuda.synchronize()
+            e0.record(s)
+            g.replay()
+            e1.record(s)
         torch.cuda.synchronize()
-        e0.record(s)
-        g.replay()
-        e1.record(s)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+        out[chained] = e0.elapsed_time(e1) / reps
+        del g
     nbytes = ib.packed_nbytes(ib.Q4_K, rows, cols) + 4 * cols + 4 * rows
-    del g, Ws
+    del Ws
     torch.cuda.empty_cache()
-    return nbytes, ms, reps
+    return nbytes, out[True], out[False], reps
 
 
 def time_gemm(ib, cfg, T, seed=20261201):
@@ -299,7 +305,7 @@ def run_reference(args, cfg, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama-3-8b")
@@ -385,7 +391,7 @@ def main():
     clk = clocks.stop()
 
     kernels_per_step = m.step_kernels()
-    nbytes, gemv_ms, gemv_reps = time_gemv(ib, cfg)
+    nbytes, gemv_ms, gemv_solo_ms, gemv_reps = time_gemv(ib, cfg)
     gemm_flops, gemm_ms = time_gemm(ib, cfg, args.prompt)
     tpeak, tpeak_kind = measured_tensor_peak()
     peak, peak_kind = measured_peaks()
@@ -424,6 +430,10 @@ def main():
                          "frac": achieved / peak, "traffic": traffic_from_profile(cfg.ffn, cfg.dim),
                          "kernel": f"gemv_q Q4_K {cfg.ffn}x{cfg.dim}",
                          "bytes_per_launch": nbytes, "avg_launch_us": gemv_ms * 1e3,
+                         "timing": "back-to-back launches chained by programmatic dependent "
+                                   "launch, as in the decode step",
+                         "standalone_us": gemv_solo_ms * 1e3,
+                         "standalone_frac": nbytes / (gemv_solo_ms * 1e-3) / 1e9 / peak,
                          "peak_kind": peak_kind},
             "decode_hbm": {"weight_bytes": weight_bytes,  # this rank's share under --tp
                            "achieved_gbs": weight_bytes * value / seqs / 1e9,

@@ -124,6 +124,12 @@ int ib_slab_bytes(int type, int64_t cols, size_t* bytes);
 int ib_limb_slab(int type, const float* dev_x, int64_t cols, void* dev_slab, void* stream);
 int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y, int64_t rows,
                    int64_t cols, void* stream);
+/* ib_gemv_q_slab launched as a link of a chain (programmatic dependent launch): it may
+ * start, and stream its weights, while the previous kernel on the stream still runs;
+ * it reads the slab and writes y only after that kernel has completed.  For chains
+ * whose weights no earlier kernel on the stream writes (the decode step's case). */
+int ib_gemv_q_slab_chained(int type, const void* dev_W, const void* dev_slab, float* dev_y,
+                           int64_t rows, int64_t cols, void* stream);
 
 /* Batched product on packed blocks: Y[T, rows] = X[T, cols] @ W^T.  Replaces
  * gemm / gemm_i16 (include/ops/cuda_backend.hpp:35-38; kernels

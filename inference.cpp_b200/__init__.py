@@ -59,6 +59,7 @@ SIGNATURES = {
     "ib_slab_bytes": [_i, _i64, _vp],
     "ib_limb_slab": [_i, _vp, _i64, _vp, _vp],
     "ib_gemv_q_slab": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
+    "ib_gemv_q_slab_chained": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_comm_unique_id": [_vp],
     "ib_comm_init": [_i, _i, _vp, _i, _vp],
     "ib_comm_allreduce_f32": [_vp, _vp, _i64, _vp],
@@ -219,11 +220,15 @@ def limb_slab(type_: int, x, cols: int, slab=None, stream=None):
     return slab
 
 
-def gemv_q_slab(type_: int, W, slab, rows: int, cols: int, y=None, stream=None):
+def gemv_q_slab(type_: int, W, slab, rows: int, cols: int, y=None, stream=None,
+                chained: bool = False):
+    """chained: ib_gemv_q_slab_chained (the launch may stream its weights while the
+    previous kernel on the stream runs; no earlier kernel may write W)."""
     import torch
     if y is None:
         y = torch.empty(rows, dtype=torch.float32, device=W.device)
-    call("ib_gemv_q_slab", type_, _ptr(W), _ptr(slab), _ptr(y), rows, cols, _stream(stream))
+    call("ib_gemv_q_slab_chained" if chained else "ib_gemv_q_slab", type_, _ptr(W), _ptr(slab),
+         _ptr(y), rows, cols, _stream(stream))
     return y
 
 

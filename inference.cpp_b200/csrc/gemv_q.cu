@@ -409,8 +409,8 @@ extern "C" int ib_limb_slab(int type, const float* dev_x, int64_t cols, void* de
                           nullptr, as_stream(stream), false);
 }
 
-extern "C" int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y,
-                              int64_t rows, int64_t cols, void* stream) {
+static int gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y,
+                       int64_t rows, int64_t cols, void* stream, bool chained) {
     if (rows == 0) return IB_OK;
     IB_REQUIRE(dev_W && dev_slab && dev_y && rows > 0 && cols > 0, "bad arguments");
     IB_REQUIRE(cols <= (1 << 30) && rows < (1ll << 31), "bad GEMV shape");
@@ -427,7 +427,17 @@ extern "C" int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab,
                   "not supported");
         return IB_ERR_UNSUPPORTED;
     }
-    return fused_gemv_launch(f, PRO_PLAIN, EPI_STORE, as_stream(stream), false);
+    return fused_gemv_launch(f, PRO_PLAIN, EPI_STORE, as_stream(stream), chained);
+}
+
+extern "C" int ib_gemv_q_slab(int type, const void* dev_W, const void* dev_slab, float* dev_y,
+                              int64_t rows, int64_t cols, void* stream) {
+    return gemv_q_slab(type, dev_W, dev_slab, dev_y, rows, cols, stream, false);
+}
+
+extern "C" int ib_gemv_q_slab_chained(int type, const void* dev_W, const void* dev_slab,
+                                      float* dev_y, int64_t rows, int64_t cols, void* stream) {
+    return gemv_q_slab(type, dev_W, dev_slab, dev_y, rows, cols, stream, true);
 }
 
 extern "C" int ib_gemv(const float* W, const float* x, float* y, int M, int N, void* stream) {

@@ -195,7 +195,8 @@ def test_gemv_q_slab_two_step(cuda, type_):
         slab = ib.limb_slab(type_, x, cols)
         for k in range(2):
             blk = ib.synth_device(type_, rows, cols, seed=7000 + 31 * k + rows + type_)
-            y = ib.gemv_q_slab(type_, blk, slab, rows, cols)
+            # the second product runs as a link of a chain (programmatic dependent launch)
+            y = ib.gemv_q_slab(type_, blk, slab, rows, cols, chained=k == 1)
             W = ib.dequantize(type_, blk, rows, cols).view(rows, cols).double()
             bound = GEMV_RTOL * (W.abs() @ x.double().abs()) + 1e-30
             assert bool(((y.double() - W @ x.double()).abs() <= bound).all()), (rows, cols, k)
