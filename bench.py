@@ -284,7 +284,9 @@ def run_reference(args, cfg, world, rank):
     if rank != 0:
         return 0
     t0 = time.perf_counter()
-    tps, kind, per = cpu_reference_sample(cfg, args.steps, args.warmup)
+    # bounded sample: at most 32 timed samples (about half a second each) so the arm ends
+    # within a few minutes whatever --steps is
+    tps, kind, per = cpu_reference_sample(cfg, min(args.steps, 32), min(args.warmup, 3))
     cores = 1
     line = {"metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps,
@@ -293,9 +295,10 @@ def run_reference(args, cfg, world, rank):
             "config": {"workload": f"{cfg.name}-q4k-decode", "prompt": args.prompt,
                        "parallelism": "cpu-1-thread"},
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
-                             "sample": "per step: one layer's 7 projections + 1/16 of the output "
-                                       "head with the reference matvec (FP32 host weights), "
-                                       f"extrapolated to {cfg.n_layers} layers + full head"},
+                             "sample": f"{len(per)} samples, each one layer's 7 projections + "
+                                       "1/16 of the output head with the reference matvec (FP32 "
+                                       f"host weights), extrapolated to {cfg.n_layers} layers + "
+                                       "full head"},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "host_cores": os.cpu_count(), "wall_s": time.perf_counter() - t0}
     print(json.dumps(line), flush=True)
