@@ -58,6 +58,26 @@ def test_argument_validation_without_gpu():
     assert L.ib_available() in (0, 1)
 
 
+def test_new_entry_points_validate_without_gpu():
+    """Entry points added beside the reference's interface reject bad arguments before
+    any device or NCCL call."""
+    L = ib.lib()
+    assert L.ib_gemm_set_path(2) == 1                      # only 0 and 1
+    assert L.ib_gemm_set_path(0) == 0
+    cfg = ib.ModelConfig(1, 256, 4, 2, 512, 300, 64, 10000.0, 1e-5, 0)
+    h = ctypes.c_void_p()
+    assert L.ib_model_create_tp(ctypes.byref(cfg), 0, None, ctypes.byref(h)) == 1
+    assert "communicator" in ib.last_error()
+    assert L.ib_model_load_gguf_tp(b"/nonexistent.gguf", 0, 0, 0, None, ctypes.byref(h)) == 1
+    idb = (ctypes.c_uint8 * 128)()
+    comm = ctypes.c_void_p()
+    assert L.ib_comm_init(2, 2, idb, 0, ctypes.byref(comm)) == 1   # rank >= world
+    assert L.ib_comm_init(0, 0, idb, 0, ctypes.byref(comm)) == 1   # empty world
+    assert L.ib_comm_allreduce_f32(None, None, 4, None) == 1
+    assert L.ib_comm_free(None) == 0
+    assert L.ib_gemv_q_slab_chained(ib.Q4_K, None, None, None, 4, 256, None) == 1
+
+
 @pytest.mark.parametrize("type_", ib.QUANT_TYPES)
 def test_synth_deterministic(type_):
     a = ib.synth_host(type_, 8, 512, seed=5, threads=1)
