@@ -305,6 +305,95 @@ def run_reference(args, cfg, world, rank):
     return 0
 
 
+def run_sweep(ib, args):
+    """Per-format decode GEMV and dequantisation GB/s over the op-sweep shapes, with the
+    reference's own CPU dequantisation and matvec (oracle/_ref, one thread) on the
+    4096x4096 shape beside them; one JSON line per (format, shape)."""
+    import math
+    import numpy as np
+    import torch
+    from inference_cpp_b200 import gguf_writer as gw
+    peak, peak_kind = measured_peaks()
+    names = {ib.Q4_0: "Q4_0", ib.Q5_0: "Q5_0", ib.Q5_1: "Q5_1", ib.Q8_0: "Q8_0",
+             ib.Q4_K: "Q4_K", ib.Q6_K: "Q6_K"}
+    shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+    ref = None
+    if not args.no_cpu_baseline:
+        try:
+            sys.path.insert(0, ROOT)
+            import __graft_entry__ as ge
+            orc = ge.oracle()
+            ref = orc.Ref() if orc.Ref.available() else orc.Port()
+            ref_kind = "reference" if orc.Ref.available() else "port"
+        except Exception:
+            ref = None
+    s = torch.cuda.Stream()
+    for t, fname in names.items():
+        for rows, cols in shapes:
+            packed = ib.packed_nbytes(t, rows, cols)
+            n = max(2, math.ceil(260e6 / packed))  # distinct copies: > 2x L2 per replay
+            Ws = [ib.synth_device(t, rows, cols, gw.tensor_seed(7, f"sweep{t}_{i}"), 0.02)
+                  for i in range(n)]
+            x = torch.randn(cols, device="cuda")
+            y = torch.empty(rows, device="cuda")
+            slab = ib.limb_slab(t, x, cols)
+            reps = max(4 * n, 16)
+            res = {}
+            s.wait_stream(torch.cuda.current_stream())
+            for chained in (True, False):
+                with torch.cuda.stream(s):
+                    for i in range(n):
+                        ib.gemv_q_slab(t, Ws[i], slab, rows, cols, y=y, chained=chained)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for i in range(reps):
+                        ib.gemv_q_slab(t, Ws[i % n], slab, rows, cols, y=y, chained=chained)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(s):
+                    g.replay()
+                    torch.cuda.synchronize()
+                    e0.record(s)
+                    g.replay()
+                    e1.record(s)
+                torch.cuda.synchronize()
+                res[chained] = e0.elapsed_time(e1) / reps
+                del g
+            nbytes = packed + 4 * cols + 4 * rows
+            # dequantisation to FP32 (bytes: packed in + 4 per element out)
+            out = torch.empty(rows * cols, device="cuda")
+            ib.dequantize(t, Ws[0], rows, cols, out=out)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(4):
+                ib.dequantize(t, Ws[i % n], rows, cols, out=out)
+            e1.record()
+            torch.cuda.synchronize()
+            dq_ms = e0.elapsed_time(e1) / 4
+            line = {"sweep": "gemv", "format": fname, "rows": rows, "cols": cols,
+                    "gemv_bytes": nbytes, "gemv_us_chained": res[True] * 1e3,
+                    "gemv_gbs_chained": nbytes / (res[True] * 1e-3) / 1e9,
+                    "gemv_us_standalone": res[False] * 1e3,
+                    "gemv_gbs_standalone": nbytes / (res[False] * 1e-3) / 1e9,
+                    "dequant_f32_gbs": (packed + 4 * rows * cols) / (dq_ms * 1e-3) / 1e9,
+                    "peak_gbs": peak, "peak_kind": peak_kind}
+            if ref is not None and (rows, cols) == (4096, 4096):
+                blk = Ws[0].cpu().numpy()
+                xs = np.random.default_rng(0).standard_normal(cols).astype(np.float32)
+                t0 = time.perf_counter()
+                Wf = ref.dequantize(t, blk, rows * cols)
+                t1 = time.perf_counter()
+                ref.matvec_f32(Wf, xs, rows, cols)
+                t2 = time.perf_counter()
+                line["cpu"] = {"kind": ref_kind, "cores": 1,
+                               "dequant_f32_gbs": (packed + 4 * rows * cols) / (t1 - t0) / 1e9,
+                               "matvec_f32_gbs": (4 * rows * cols) / (t2 - t1) / 1e9}
+            print(json.dumps(line), flush=True)
+            del Ws, out, slab
+            torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -319,6 +408,9 @@ def main():
                          "range named decode_step (for profiler launch lists)")
     ap.add_argument("--decode-path", default="fused", choices=["fused", "separate"],
                     help="fused decode kernels (default) or the separate per-op kernels")
+    ap.add_argument("--sweep", action="store_true",
+                    help="per-format GEMV / dequantisation GB/s over the op-sweep shapes "
+                         "(one JSON line each) instead of the decode benchmark")
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1: one tensor-parallel model over the N GPUs instead of "
                          "N replicas")
@@ -344,6 +436,8 @@ def main():
     import torch
     torch.cuda.set_device(local)
     ib.init(local)
+    if args.sweep:
+        return run_sweep(ib, args) if rank == 0 else 0
     tp = args.tp and world > 1
     comm = make_comm(ib, world, rank, local) if tp else None
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
