@@ -275,6 +275,11 @@ int ib_tp_shard(int type, const void* host_src, int64_t rows, int64_t cols, int 
  * decode, generate), including the same host_logits null-ness, since the steps hold
  * collectives; each rank then gets the same ids and logits. */
 int ib_model_create_tp(const ib_model_config* cfg, int device, void* comm, void** model);
+/* Self-test of the exchange's bounded wait on one GPU: rank 0 and a stand-in rank 1
+ * whose rows are sent only when peer_sends != 0.  *fault = 0 and *x_out = 0.75 when
+ * they arrive; otherwise the receiving kernel gives up after 2 s and *fault = 21 (the
+ * code ib_check_fault would report), and the context stays usable. */
+int ib_tp_wait_selftest(int peer_sends, int* fault, float* x_out);
 int ib_model_load_gguf_tp(const char* path, int precision, int device, int max_seq, void* comm,
                           void** model);
 

@@ -433,6 +433,7 @@ class GenerationStats(ctypes.Structure):
 SIGNATURES.update({
     "ib_model_create": [_vp, _i, _vp],
     "ib_model_create_tp": [_vp, _i, _vp, _vp],
+    "ib_tp_wait_selftest": [_i, _vp, _vp],
     "ib_model_load_gguf_tp": [_c.c_char_p, _i, _i, _i, _vp, _vp],
     "ib_model_set_tensor": [_vp, _c.c_char_p, _i, _i64, _i64, _vp, _i],
     "ib_model_finalize": [_vp],

@@ -833,6 +833,71 @@ int fused_gemv_launch(const FusedGemv& p, int pro, int epi, cudaStream_t st, boo
     return IB_ERR_UNSUPPORTED;
 }
 
+// ---- self-test of the exchange's bounded wait -----------------------------------------
+// Writes the tagged rows rank `src` contributes to exchange 0 (slot 0) of a region.
+__global__ void tp_selftest_push_kernel(uint64_t* region, int world, int stride, int src, int n) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        st_tagged(region + (size_t)src * stride + i, 1u, __float_as_uint(0.25f * (float)(src + 1)));
+}
+
+}  // namespace ib
+
+// One exchange on this GPU between rank 0 and a stand-in rank 1 whose rows arrive only
+// when `peer_sends` != 0.  The receiving slab kernel either completes x (+0.25 + 0.5 per
+// element) or gives up after its bounded wait (2 s), recording fault 21; *fault gets
+// the recorded code (0 = none) and *x_out one completed element.  No counterpart in the
+// reference: it exercises the failure path of the tensor-parallel exchange without a
+// second GPU and without faulting the device.
+extern "C" int ib_tp_wait_selftest(int peer_sends, int* fault, float* x_out) {
+    using namespace ib;
+    IB_REQUIRE(fault && x_out, "null pointer argument");
+    const int K = 256, W = 2;
+    const size_t rb = tp_region_bytes(W, K);
+    uint8_t* region = nullptr;
+    uint32_t* seq = nullptr;
+    float* x = nullptr;
+    uint8_t* slab = nullptr;
+    IB_CUDA_CHECK(cudaMalloc(&region, rb));
+    IB_CUDA_CHECK(cudaMalloc(&seq, 16));
+    IB_CUDA_CHECK(cudaMalloc(&x, K * 4));
+    IB_CUDA_CHECK(cudaMalloc(&slab, slab_total_bytes(K, true) + 16));
+    int r = IB_OK;
+    do {
+        if (cudaMemset(region, 0, rb) != cudaSuccess || cudaMemset(x, 0, K * 4) != cudaSuccess) {
+            r = IB_ERR_CUDA;
+            break;
+        }
+        const uint32_t one = 1;  // the producing GEMV has advanced the counter past exchange 0
+        if (cudaMemcpy(seq, &one, 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            r = IB_ERR_CUDA;
+            break;
+        }
+        tp_selftest_push_kernel<<<1, 256>>>((uint64_t*)region, W, K, 0, K);
+        if (peer_sends) tp_selftest_push_kernel<<<1, 256>>>((uint64_t*)region, W, K, 1, K);
+        TpExchange t{};
+        t.region[0] = region;
+        t.region[1] = region;  // the stand-in peer shares this GPU's region
+        t.seq = seq;
+        t.rank = 0;
+        t.world = W;
+        t.stride = K;
+        if ((r = xq_slab_launch(x, nullptr, K, true, slab, nullptr, nullptr, false, &t))) break;
+        if (cudaDeviceSynchronize() != cudaSuccess) {
+            r = IB_ERR_CUDA;
+            break;
+        }
+        if ((r = decode_fault_take(fault))) break;
+        if (cudaMemcpy(x_out, x, 4, cudaMemcpyDeviceToHost) != cudaSuccess) r = IB_ERR_CUDA;
+    } while (false);
+    cudaFree(region);
+    cudaFree(seq);
+    cudaFree(x);
+    cudaFree(slab);
+    return r;
+}
+
+namespace ib {
+
 int decode_fault_take(int* code) {
     int v = 0, z = 0;
     IB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_decode_fault, sizeof(int)));

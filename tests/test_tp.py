@@ -359,3 +359,28 @@ def test_tp_wide_matches_oracle(port, world, fused):
         assert np.all(np.abs(logits - want_logits) <= LOGIT_RTOL * scale), rank
         if fused:
             assert uses_fused, rank
+
+
+@pytest.mark.gpu
+def test_exchange_wait_is_bounded(cuda):
+    """The exchange's receiving wait gives up when a peer never sends: the kernel records
+    fault 21 after its 2 s limit and returns, and the GPU stays usable.  One GPU: the
+    stand-in peer shares the device (no kernel waits on another kernel of this GPU)."""
+    import ctypes
+    import time
+    torch = cuda
+    fault, x = ctypes.c_int(-1), ctypes.c_float(0.0)
+    ib.call("ib_tp_wait_selftest", 1, ctypes.byref(fault), ctypes.byref(x))
+    assert fault.value == 0 and x.value == 0.75
+    t0 = time.perf_counter()
+    ib.call("ib_tp_wait_selftest", 0, ctypes.byref(fault), ctypes.byref(x))
+    waited = time.perf_counter() - t0
+    assert fault.value == 21
+    assert 1.5 < waited < 60
+    # the context still works
+    blk = ib.synth_device(ib.Q4_K, 64, 512, seed=3)
+    v = torch.randn(512, device="cuda")
+    y = ib.gemv_q(ib.Q4_K, blk, v, 64, 512)
+    W = ib.dequantize(ib.Q4_K, blk, 64, 512).view(64, 512).double()
+    assert bool(((y.double() - W @ v.double()).abs() <= 2e-5 * (W.abs() @ v.double().abs()) + 1e-30).all())
+    assert ib.check_fault() == 0
