@@ -1,6 +1,8 @@
 // Non-GEMV operators of the Llama forward pass with the reference's argument
 // meaning (include/ops/cuda_backend.hpp:39-64; kernels src/ops/cuda_kernels.cu),
-// plus batched GEMM (prefill) on FP32, INT16 and packed weights.
+// plus the CUDA-core batched GEMM on FP32, INT16 and packed weights.  Prefill on
+// packed weights normally runs on the tensor cores (gemm_tc.cu) and its attention
+// as flash attention (attention.cu, attention_prefill).
 //
 // Attention for one query position is a split-K "flash decode": CTA (kv head,
 // position chunk) scores the whole GQA group against its chunk of the KV cache,
@@ -246,10 +248,12 @@ __global__ void argmax_kernel(const float* __restrict__ x, int n, int32_t* __res
     }
 }
 
-// ---- batched GEMM, SIMT: Y[T, M] = X[T, K] @ W[M, K]^T ---------------------------
+// ---- batched GEMM on the CUDA cores: Y[T, M] = X[T, K] @ W[M, K]^T ---------------
 // Tile 64 (W rows) x 64 (tokens) x 32 (K); 256 threads, 4x4 outputs each.
 // The W tile is produced by a loader: FP32 copy, INT16 (scaled in the epilogue),
-// or exact dequantisation of GGUF blocks (deq8).
+// or exact dequantisation of GGUF blocks (deq8).  Serves ib_gemm and ib_gemm_i16,
+// and ib_gemm_q for shapes the tensor-core kernel (gemm_tc.cu) does not take or
+// when ib_gemm_set_path(1) asks for it.
 constexpr int GB_M = 64, GB_N = 64, GB_K = 32;
 
 template <int TYPE>
