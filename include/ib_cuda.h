@@ -183,6 +183,20 @@ int ib_attention_batch(const float* q, const float* kc, const float* vc, float* 
                        int n_heads, int n_kv_heads, int head_dim, int max_seq, int start,
                        int T, float scale, void* stream);
 
+/* Decode attention as the native runner's decode step runs it: one kernel of
+ * (kv head, split) CTAs whose last CTA per kv head combines the splits, with the
+ * position read from device memory (*pos_dev) so the call can sit in a CUDA graph.
+ * Same result contract as ib_attention (reference attention_kernel,
+ * src/ops/cuda_kernels.cu:216-267).  Needs head_dim % 4 == 0, head_dim <= 128,
+ * n_heads / n_kv_heads <= 8 and 16-byte aligned q, kc, vc, out.  part: scratch of
+ * ib_attention_split_part_bytes(n_heads, head_dim) bytes; counters: n_kv_heads
+ * int32 that are zero on entry and are left at zero. */
+size_t ib_attention_split_part_bytes(int n_heads, int head_dim);
+int ib_attention_split(const float* q, const float* kc, const float* vc, float* out,
+                       int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                       const int32_t* pos_dev, float scale, float* part, int32_t* counters,
+                       void* stream);
+
 /* Index of the first maximum of x[0..n) (reference sample_argmax,
  * src/ops/ops.cpp:424-438), written to *dev_out. */
 int ib_argmax(const float* x, int n, int32_t* dev_out, void* stream);

@@ -86,12 +86,14 @@ SIGNATURES = {
     "ib_rope_batch": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp],
     "ib_attention": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp],
     "ib_attention_batch": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp],
+    "ib_attention_split_part_bytes": [_i, _i],
+    "ib_attention_split": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _f, _vp, _vp, _vp],
     "ib_argmax": [_vp, _i, _vp, _vp],
     "ib_synth_host": [_i, _i64, _i64, _u64, _f, _vp, _i],
     "ib_synth_device": [_i, _i64, _i64, _u64, _f, _vp, _vp],
     "ib_synth_values_host": [_i64, _u64, _f, _vp],
 }
-_RESTYPE = {"ib_last_error": _c.c_char_p}
+_RESTYPE = {"ib_last_error": _c.c_char_p, "ib_attention_split_part_bytes": _c.c_size_t}
 
 _lib = None
 
@@ -366,6 +368,19 @@ def rope_batch(q, k, table, n_heads, n_kv_heads, head_dim, start, T, stream=None
 def attention(q, kc, vc, out, n_heads, n_kv_heads, head_dim, max_seq, pos, scale, stream=None):
     call("ib_attention", _ptr(q), _ptr(kc), _ptr(vc), _ptr(out), n_heads, n_kv_heads, head_dim,
          max_seq, pos, scale, _stream(stream))
+
+
+def attention_split(q, kc, vc, out, n_heads, n_kv_heads, head_dim, max_seq, pos_dev, scale,
+                    part, counters, stream=None):
+    """Decode attention through the decode step's split kernel; the position is read
+    from the int32 device word pos_dev.  part: attention_split_part_bytes(n_heads,
+    head_dim) bytes of scratch; counters: n_kv_heads zeroed int32, left zeroed."""
+    call("ib_attention_split", _ptr(q), _ptr(kc), _ptr(vc), _ptr(out), n_heads, n_kv_heads,
+         head_dim, max_seq, _ptr(pos_dev), scale, _ptr(part), _ptr(counters), _stream(stream))
+
+
+def attention_split_part_bytes(n_heads, head_dim):
+    return lib().ib_attention_split_part_bytes(n_heads, head_dim)
 
 
 def attention_batch(q, kc, vc, out, n_heads, n_kv_heads, head_dim, max_seq, start, T, scale,

@@ -569,6 +569,24 @@ extern "C" int ib_attention(const float* q, const float* kc, const float* vc, fl
                             (float*)part, as_stream(stream), nullptr);
 }
 
+extern "C" size_t ib_attention_split_part_bytes(int n_heads, int head_dim) {
+    return n_heads > 0 && head_dim > 0 ? attention_fused_part_bytes(n_heads, head_dim) : 0;
+}
+
+extern "C" int ib_attention_split(const float* q, const float* kc, const float* vc, float* out,
+                                  int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                                  const int32_t* pos_dev, float scale, float* part,
+                                  int32_t* counters, void* stream) {
+    IB_REQUIRE(q && kc && vc && out && pos_dev && part && counters, "null pointer argument");
+    IB_REQUIRE(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0 && max_seq > 0,
+               "n_heads must be a multiple of n_kv_heads");
+    IB_REQUIRE(attention_fused_ok(n_heads, n_kv_heads, head_dim),
+               "split attention needs head_dim % 4 == 0, head_dim <= 128 and a group <= 8");
+    return attention_decode_fused(q, kc, vc, out, nullptr, false, n_heads, n_kv_heads, head_dim,
+                                  max_seq, scale, part, counters, as_stream(stream), pos_dev,
+                                  false);
+}
+
 extern "C" int ib_attention_batch(const float* q, const float* kc, const float* vc, float* out,
                                   int n_heads, int n_kv_heads, int head_dim, int max_seq,
                                   int start, int T, float scale, void* stream) {

@@ -75,6 +75,46 @@ def test_attention_decode_shapes(cuda, H, Hkv, HD, pos):
     assert np.all(np.abs(out.cpu().numpy() - ref) <= 2e-5 * (1 + np.abs(ref)))
 
 
+# The decode step's split kernel: positions 0 and 1 (one split), 2600 (41 splits: the
+# combine's second batch of loads), 4095 (all 64 splits), 5000 and 9000 (two and three
+# 64-position tiles per split), group sizes 1, 2, 4 and 8, head_dim 128 and 64 (half
+# the lanes idle), and a second call at the next position (the counters come back at
+# zero).
+@pytest.mark.parametrize("H,Hkv,HD,pos", [(32, 8, 128, 2600), (64, 8, 128, 5000),
+                                          (8, 8, 128, 4095), (8, 4, 64, 300),
+                                          (32, 8, 128, 0), (4, 1, 128, 1),
+                                          (16, 2, 128, 9000)])
+def test_attention_split_matches_reference(cuda, H, Hkv, HD, pos):
+    MAX = pos + 9
+    rng = np.random.default_rng(7 * H + pos)
+    q = rng.standard_normal(H * HD).astype(np.float32)
+    kc = rng.standard_normal(Hkv * MAX * HD).astype(np.float32)
+    vc = rng.standard_normal(Hkv * MAX * HD).astype(np.float32)
+    part = cuda.empty(ib.attention_split_part_bytes(H, HD) // 4 + 1, device="cuda")
+    counters = cuda.zeros(Hkv, dtype=cuda.int32, device="cuda")
+    dq, dk, dv = dev(cuda, q), dev(cuda, kc), dev(cuda, vc)
+    for p in (pos, pos + 1):
+        ref = attention_ref(q, kc, vc, H, Hkv, HD, MAX, p)
+        out = cuda.zeros(H * HD, device="cuda")
+        pos_dev = cuda.tensor([p], dtype=cuda.int32, device="cuda")
+        ib.attention_split(dq, dk, dv, out, H, Hkv, HD, MAX, pos_dev, 1.0 / math.sqrt(HD), part,
+                           counters)
+        assert np.all(np.abs(out.cpu().numpy() - ref) <= 2e-5 * (1 + np.abs(ref))), p
+        assert counters.cpu().tolist() == [0] * Hkv
+    assert ib.check_fault() == 0
+
+
+def test_attention_split_rejects_unsupported(cuda):
+    part = cuda.empty(1 << 16, device="cuda")
+    counters = cuda.zeros(8, dtype=cuda.int32, device="cuda")
+    pos_dev = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    x = cuda.zeros(1 << 16, device="cuda")
+    with pytest.raises(RuntimeError, match="group <= 8"):
+        ib.attention_split(x, x, x, x, 32, 2, 128, 16, pos_dev, 1.0, part, counters)
+    with pytest.raises(RuntimeError, match="head_dim"):
+        ib.attention_split(x, x, x, x, 8, 8, 256, 16, pos_dev, 1.0, part, counters)
+
+
 def test_gemv_int16(cuda):  # CudaTest.GemvInt16
     W = dev(cuda, np.array([1, 2, 6, 8], np.int16))
     sc = dev(cuda, np.array([1.0, 0.5], np.float32))
