@@ -28,6 +28,12 @@ __device__ __forceinline__ float wsum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+// A coherent (L2) load of a word another kernel writes, never merged with another load.
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ float wmax(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -327,7 +333,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     float* __restrict__ out, uint8_t* __restrict__ slab, int slab_kq, int n_heads, int n_kv_heads,
     int head_dim, int max_seq, float scale, const int* __restrict__ pos_dev) {
     pdl_launch_dependents();
-    pdl_wait();
     constexpr int LPP = 16, PPP = 32 / LPP;  // lanes per position, positions per pass
     constexpr int PW = ATT_TILE / ATT_WARPS;  // positions per warp per tile
     constexpr int PASSES = PW / PPP;
@@ -340,18 +345,67 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     __shared__ float linv[GMAX];
     __shared__ __align__(16) float ovals[GMAX * 128];
     __shared__ int is_last;
-    const int pos = *pos_dev;
     const int G = n_heads / n_kv_heads;
     const int hk = blockIdx.x, sp = blockIdx.y;
-    const int n_pos = pos + 1;
-    int per = (n_pos + ATT_SPLITS - 1) / ATT_SPLITS;
-    per = (per + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
-    const int live = (n_pos + per - 1) / per;
-    if (sp >= live || pos >= max_seq) return;
-    const int p0 = sp * per, p1 = min(n_pos, p0 + per);
     const int nv = head_dim >> 2;  // float4 per row
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pp = lane / LPP, li = lane % LPP;
+    const float4* k4 = reinterpret_cast<const float4*>(kc) + (size_t)hk * max_seq * nv;
+    const float4* v4 = reinterpret_cast<const float4*>(vc) + (size_t)hk * max_seq * nv;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 kr[PASSES][NVL], vr[PASSES][NVL];
+#pragma unroll
+    for (int p = 0; p < PASSES; ++p)
+#pragma unroll
+        for (int k = 0; k < NVL; ++k) kr[p][k] = vr[p][k] = z4;
+    // rows t0 + s, s < n, with lo <= t0 + s < hi of the tile at t0; the others keep
+    // their registers
+    auto load_tile = [&](int t0, int n, int lo, int hi) {
+#pragma unroll
+        for (int p = 0; p < PASSES; ++p) {
+            const int s = warp * PW + p * PPP + pp;
+#pragma unroll
+            for (int k = 0; k < NVL; ++k) {
+                const int c = li + LPP * k;
+                if (s < n && c < nv && t0 + s >= lo && t0 + s < hi) {
+                    kr[p][k] = __ldg(k4 + (size_t)(t0 + s) * nv + c);
+                    vr[p][k] = __ldg(v4 + (size_t)(t0 + s) * nv + c);
+                }
+            }
+        }
+    };
+    // this split's positions [p0, p1) for the token at `at`; live = splits in use
+    int live = 0, p0 = 0, p1 = 0;
+    auto span = [&](int at) {
+        const int n_pos = at + 1;
+        int per = (n_pos + ATT_SPLITS - 1) / ATT_SPLITS;
+        per = (per + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+        live = (n_pos + per - 1) / per;
+        p0 = sp * per;
+        p1 = min(n_pos, p0 + per);
+    };
+    // K and V rows below the step's position were written by earlier steps and do not
+    // change during this one (the previous kernel, the QKV projection, writes row `pos`
+    // only), so the first tile's other rows are loaded before the wait on that kernel:
+    // while it streams its weights, since it leaves room for these CTAs on every SM.
+    // The position word changes only between steps (a kernel launched without the PDL
+    // attribute ends each step); it is read again after the wait, and a different value
+    // reloads the whole tile.
+    const int pos_pre = ld_relaxed_gpu(pos_dev);
+    const bool pre = pos_pre >= 0 && pos_pre < max_seq;
+    if (pre) {
+        span(pos_pre);
+        if (sp < live) load_tile(p0, min(ATT_TILE, p1 - p0), 0, pos_pre);
+    }
+    pdl_wait();
+    const int pos = ld_relaxed_gpu(pos_dev);
+    if (pos < 0 || pos >= max_seq) return;
+    span(pos);
+    if (sp >= live) return;
+    if (pre && pos == pos_pre)
+        load_tile(p0, min(ATT_TILE, p1 - p0), pos, pos + 1);
+    else
+        load_tile(p0, min(ATT_TILE, p1 - p0), 0, max_seq);
     const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
     for (int i = tid; i < G * nv; i += ATT_WARPS * 32) qs[i / nv][i % nv] = q4[i];
     if (tid < G) {
@@ -359,9 +413,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         lrun[tid] = 0.f;
     }
     __syncthreads();
-    const float4* k4 = reinterpret_cast<const float4*>(kc) + (size_t)hk * max_seq * nv;
-    const float4* v4 = reinterpret_cast<const float4*>(vc) + (size_t)hk * max_seq * nv;
-    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 acc[GMAX][NVL];
 #pragma unroll
     for (int g = 0; g < GMAX; ++g)
@@ -369,18 +420,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         for (int k = 0; k < NVL; ++k) acc[g][k] = z4;
     for (int t0 = p0; t0 < p1; t0 += ATT_TILE) {
         const int n = min(ATT_TILE, p1 - t0);
-        float4 kr[PASSES][NVL], vr[PASSES][NVL];
-#pragma unroll
-        for (int p = 0; p < PASSES; ++p) {
-            const int s = warp * PW + p * PPP + pp;
-#pragma unroll
-            for (int k = 0; k < NVL; ++k) {
-                const int c = li + LPP * k;
-                const bool ok = s < n && c < nv;
-                kr[p][k] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + c) : z4;
-                vr[p][k] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + c) : z4;
-            }
-        }
+        // rows s >= n keep an earlier tile's values; every use below checks s < n
+        if (t0 != p0) load_tile(t0, n, 0, max_seq);
 #pragma unroll
         for (int p = 0; p < PASSES; ++p) {
             const int s = warp * PW + p * PPP + pp;

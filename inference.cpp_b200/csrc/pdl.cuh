@@ -3,7 +3,8 @@
 // A kernel launched with programmatic stream serialization may start while the
 // previous kernel on the stream is still running.  Such a kernel must execute
 // pdl_wait() before it touches anything the previous kernel writes or reads
-// (activations, caches, positions); work on constant data (weight prefetch) may
+// (activations, caches, positions); work on data that is constant while the
+// previous kernel runs (weight prefetch; KV-cache rows that earlier steps wrote) may
 // run before it.  pdl_launch_dependents() lets the next kernel start early; it
 // changes scheduling only, never visibility: the next kernel's pdl_wait() still
 // returns only after this grid has completed and its writes are visible.  Both
