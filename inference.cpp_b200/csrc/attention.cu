@@ -374,6 +374,20 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
             }
         }
     };
+    // every row of the tile at t0 (zeros past n): no register outlives its tile
+    auto load_full = [&](int t0, int n) {
+#pragma unroll
+        for (int p = 0; p < PASSES; ++p) {
+            const int s = warp * PW + p * PPP + pp;
+#pragma unroll
+            for (int k = 0; k < NVL; ++k) {
+                const int c = li + LPP * k;
+                const bool ok = s < n && c < nv;
+                kr[p][k] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + c) : z4;
+                vr[p][k] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + c) : z4;
+            }
+        }
+    };
     // this split's positions [p0, p1) for the token at `at`; live = splits in use
     int live = 0, p0 = 0, p1 = 0;
     auto span = [&](int at) {
@@ -386,13 +400,18 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     };
     // K and V rows below the step's position were written by earlier steps and do not
     // change during this one (the previous kernel, the QKV projection, writes row `pos`
-    // only), so the first tile's other rows are loaded before the wait on that kernel:
-    // while it streams its weights, since it leaves room for these CTAs on every SM.
-    // The position word changes only between steps (a kernel launched without the PDL
+    // only), so for groups of up to 4 the first tile's other rows are loaded before the
+    // wait on that kernel, while the CTAs that reach it early overlap its tail.  The
+    // position word changes only between steps (a kernel launched without the PDL
     // attribute ends each step); it is read again after the wait, and a different value
-    // reloads the whole tile.
-    const int pos_pre = ld_relaxed_gpu(pos_dev);
-    const bool pre = pos_pre >= 0 && pos_pre < max_seq;
+    // reloads the whole tile.  Measured on the decode step at position 2050: Llama-3-8B
+    // (group 4) 2.26 against 2.38 ms; Llama-3-70B (group 8, whose registers already
+    // spill) 12.11 against 11.92 ms, so the group-8 kernel loads every tile after the
+    // wait and after the query, in the loop below.
+    constexpr bool kPrefetch = GMAX <= 4;
+    int pos_pre = -1;
+    if (kPrefetch) pos_pre = ld_relaxed_gpu(pos_dev);
+    const bool pre = kPrefetch && pos_pre >= 0 && pos_pre < max_seq;
     if (pre) {
         span(pos_pre);
         if (sp < live) load_tile(p0, min(ATT_TILE, p1 - p0), 0, pos_pre);
@@ -404,8 +423,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     if (sp >= live) return;
     if (pre && pos == pos_pre)
         load_tile(p0, min(ATT_TILE, p1 - p0), pos, pos + 1);
-    else
-        load_tile(p0, min(ATT_TILE, p1 - p0), 0, max_seq);
+    else if (kPrefetch)
+        load_full(p0, min(ATT_TILE, p1 - p0));
     const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
     for (int i = tid; i < G * nv; i += ATT_WARPS * 32) qs[i / nv][i % nv] = q4[i];
     if (tid < G) {
@@ -420,8 +439,9 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         for (int k = 0; k < NVL; ++k) acc[g][k] = z4;
     for (int t0 = p0; t0 < p1; t0 += ATT_TILE) {
         const int n = min(ATT_TILE, p1 - t0);
-        // rows s >= n keep an earlier tile's values; every use below checks s < n
-        if (t0 != p0) load_tile(t0, n, 0, max_seq);
+        // without the prefetch every tile, the first included, loads here, after the
+        // query is in shared memory
+        if (!kPrefetch || t0 != p0) load_full(t0, n);
 #pragma unroll
         for (int p = 0; p < PASSES; ++p) {
             const int s = warp * PW + p * PPP + pp;

@@ -781,15 +781,16 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
         const int slot_b = ring_slot(TB, P::KB * Fmt<TB>::BB);
         const int wbytes = 16 * ((has_b && (!has_a || slot_b > slot_a)) ? slot_b : slot_a);
         const int stage = wbytes + P::SLICE;
-        // Ring depth.  4-bit kernels (27.9 KB K-quant stages) run 2 stages at 4 CTAs per
-        // SM: 223 KB in flight per SM, the consumers' latency hidden by warps.  Kernels
-        // with Q6_K rows (35.9 KB stages) run 3 stages at 2 CTAs per SM, the same bytes in
-        // flight as 2 stages at 3 CTAs, but half the register file stays free, so the
-        // next kernel's CTAs (attention after the QKV projection) become resident and
-        // reach their wait while this one streams.  Measured on the Llama-3-8B decode
-        // step at position 2050: 2.40 against 2.50 ms; 4 or 6 stages at one CTA per SM
-        // were slower (2.57, 2.59 ms), as were 3 stages for the 4-bit kernels (2.58 ms).
-        int S = (has_b && TB == IB_TYPE_Q6_K) ? 3 : 73728 / stage;
+        // Ring depth.  Short rows (K-quant rows of <= 4 stages: K <= 8192) run 2 stages
+        // at 3-4 CTAs per SM: 215-223 KB in flight per SM, and the row groups spread
+        // evenly over the CTAs.  Long Q6_K rows (the down projection: 7 stages per row
+        // group at K = 14336) run 3 stages at 2 CTAs per SM, so each CTA keeps a deeper
+        // queue through its row.  Measured on the Llama-3-8B decode step at position
+        // 2050: 2.26 ms, against 2.45 with 2 stages for the down projection, 2.32 with 3
+        // stages for the QKV projection and head too, 2.36 with 4 stages at one CTA per
+        // SM for the down projection, and 2.58 with 3 stages for the 4-bit kernels.
+        const int spg = nb / P::KB;  // ring stages per row group
+        int S = (has_b && TB == IB_TYPE_Q6_K && spg > 4) ? 3 : 73728 / stage;
         if (S < 2) S = 2;
         if (S > kMaxStages) S = kMaxStages;
         const size_t smem = (size_t)S * stage;
