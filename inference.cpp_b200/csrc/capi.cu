@@ -43,7 +43,7 @@ extern "C" int ib_init(int device) {
     cudaDeviceProp prop;
     IB_CUDA_CHECK(cudaGetDeviceProperties(&prop, device));
     if (prop.major != 10) {
-        set_error(std::string("CUDA: device ") + prop.name + " is not sm_100 (this build targets sm_100a)");
+        set_error(std::string("CUDA: device ") + prop.name + " is not sm_100 (the library is compiled for sm_100a)");
         return IB_ERR_UNSUPPORTED;
     }
     IB_CUDA_CHECK(cudaSetDevice(device));

@@ -2,8 +2,8 @@
  * TEST INFRASTRUCTURE ONLY -- the CPU oracle for the quantized-weight path.
  *
  * A plain-C restatement of the reference's CPU algorithms (0xiamsanj/inference.cpp),
- * used by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg as the
- * checker.  Nothing in the product links or calls this file.
+ * used by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg to check
+ * and time results.  Nothing in the product links or calls this file.
  *
  * Parity pin: tests/test_oracle_pin.py checks every function here against the
  * reference compiled from its own sources (oracle/_ref, built by oracle/Makefile)

@@ -3,9 +3,9 @@
 `Port` wraps oracle/liboracle.so, the plain-C restatement of the reference's
 algorithms (oracle.c).  `Ref` wraps oracle/_ref/libref_oracle.so, the
 reference's own CPU sources compiled here by oracle/Makefile (present only where
-the reference tree was available at build time; the GPU box receives the prebuilt
-file).  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use
-this module, and only as the checker.
+the reference tree was available at build time; a machine without that tree uses the
+prebuilt file).  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use
+this module, and only to check results.
 """
 from __future__ import annotations
 
