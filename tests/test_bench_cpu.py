@@ -1,0 +1,59 @@
+"""bench.py pieces that need no GPU: the reference arm's JSON line (the reference's own
+CPU matvec, or the C restatement where the reference was not built here) and the
+helpers that feed the roofline fields."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT, load_package
+
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+load_package()  # registers inference_cpp_b200 for the imports below
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                        "--steps", "1", "--warmup", "3"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT,
+                       env={k: v for k, v in os.environ.items()
+                            if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")})
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC
+    assert d["unit"] == "tok/s" and d["higher_is_better"] is True and d["value"] > 0
+    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] >= 3
+    assert d["config"]["workload"] == "llama-3-8b-q4k-decode"
+    cb = d["cpu_baseline"]
+    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_roofline_helpers():
+    peak, kind = bench.measured_peaks()
+    tpeak, tkind = bench.measured_tensor_peak()
+    if kind == "fallback":
+        assert peak == 6650.0
+    if tkind == "fallback":
+        assert tpeak == 1590.0
+    assert peak > 1000 and tpeak > 100
+    # the committed capture of the roofline shape gives its DRAM bytes; others give None
+    t = bench.traffic_from_profile(14336, 4096)
+    assert t is not None and 30e6 < t < 40e6
+    assert bench.traffic_from_profile(123, 456) is None
+
+
+@pytest.mark.parametrize("use_ref", [False, True])
+def test_cpu_reference_sample_is_bounded(use_ref):
+    from inference_cpp_b200 import gguf_writer as gw
+    tps, kind, per = bench.cpu_reference_sample(gw.CONFIGS["llama-3-8b"], 1, 0, use_ref=use_ref)
+    assert tps > 0 and len(per) == 1
+    if not use_ref:
+        assert kind == "port"
