@@ -720,19 +720,26 @@ static int decode_launches(Model* m) {
     return IB_OK;
 }
 
+// A captured graph, destroyed on every return path (the executable graph instantiated
+// from it keeps what it needs).
+struct CapturedGraph {
+    cudaGraph_t g = nullptr;
+    ~CapturedGraph() {
+        if (g) cudaGraphDestroy(g);
+    }
+};
+
 static int ensure_graph(Model* m) {
     if (m->graph_exec || !m->use_graph) return IB_OK;
-    cudaGraph_t g = nullptr;
+    CapturedGraph cg;
     IB_CUDA_CHECK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int r = decode_launches(m);
-    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
-    if (r != IB_OK) {
-        if (g) cudaGraphDestroy(g);
-        return r;
-    }
+    cudaError_t e = cudaStreamEndCapture(m->stream, &cg.g);
+    if (r != IB_OK) return r;
     IB_CUDA_CHECK(e);
-    IB_CUDA_CHECK(cudaGraphInstantiate(&m->graph_exec, g, 0));
-    cudaGraphDestroy(g);
+    const cudaError_t ie = cudaGraphInstantiate(&m->graph_exec, cg.g, 0);
+    if (ie != cudaSuccess) m->graph_exec = nullptr;
+    IB_CUDA_CHECK(ie);
     return IB_OK;
 }
 
@@ -900,23 +907,22 @@ extern "C" int ib_model_step_kernels(void* h, int* n) {
     IB_CUDA_CHECK(cudaSetDevice(m->device));
     int r = ensure_graph(m);
     if (r) return r;
-    cudaGraph_t g = nullptr;
+    CapturedGraph cg;
     IB_CUDA_CHECK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     r = decode_launches(m);
-    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
-    if (r) { if (g) cudaGraphDestroy(g); return r; }
+    cudaError_t e = cudaStreamEndCapture(m->stream, &cg.g);
+    if (r) return r;
     IB_CUDA_CHECK(e);
     size_t count = 0;
-    IB_CUDA_CHECK(cudaGraphGetNodes(g, nullptr, &count));
+    IB_CUDA_CHECK(cudaGraphGetNodes(cg.g, nullptr, &count));
     std::vector<cudaGraphNode_t> nodes(count);
-    IB_CUDA_CHECK(cudaGraphGetNodes(g, nodes.data(), &count));
+    IB_CUDA_CHECK(cudaGraphGetNodes(cg.g, nodes.data(), &count));
     int k = 0;
     for (auto nd : nodes) {
         cudaGraphNodeType t;
         IB_CUDA_CHECK(cudaGraphNodeGetType(nd, &t));
         if (t == cudaGraphNodeTypeKernel) ++k;
     }
-    cudaGraphDestroy(g);
     *n = k;
     return IB_OK;
 }
