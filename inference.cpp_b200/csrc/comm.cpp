@@ -97,18 +97,29 @@ int comm_peer_alloc(Comm* c, size_t bytes, void** local, void** peers) {
     *local = nullptr;
     for (int q = 0; q < W; ++q) peers[q] = nullptr;
     IB_CUDA_CHECK(cudaMalloc(local, bytes));
-    IB_CUDA_CHECK(cudaMemset(*local, 0, bytes));
+    // a failed step below releases what was allocated before it
+    auto fail = [&](cudaError_t e, const char* what, uint8_t* scratch) {
+        set_error(std::string("peer memory: ") + what + " failed: " + cudaGetErrorString(e));
+        if (scratch) cudaFree(scratch);
+        cudaFree(*local);
+        *local = nullptr;
+        return IB_ERR_CUDA;
+    };
+    cudaError_t ce = cudaMemset(*local, 0, bytes);
+    if (ce != cudaSuccess) return fail(ce, "cudaMemset", nullptr);
     if (W == 1) {
         peers[0] = *local;
         return IB_OK;
     }
     cudaIpcMemHandle_t mine;
-    IB_CUDA_CHECK(cudaIpcGetMemHandle(&mine, *local));
+    if ((ce = cudaIpcGetMemHandle(&mine, *local)) != cudaSuccess)
+        return fail(ce, "cudaIpcGetMemHandle", nullptr);
     const size_t hb = sizeof(cudaIpcMemHandle_t);
     uint8_t* dev = nullptr;
-    IB_CUDA_CHECK(cudaMalloc(&dev, hb * (W + 1)));
+    if ((ce = cudaMalloc(&dev, hb * (W + 1))) != cudaSuccess) return fail(ce, "cudaMalloc", nullptr);
     cudaStream_t st;
-    IB_CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    if ((ce = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess)
+        return fail(ce, "cudaStreamCreateWithFlags", dev);
     std::vector<cudaIpcMemHandle_t> all(W);
     int r = IB_OK;
     Nccl* nc = nullptr;
