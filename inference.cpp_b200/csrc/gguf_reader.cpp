@@ -11,6 +11,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cmath>
 #include <cstring>
 #include <stdexcept>
 
@@ -18,12 +19,15 @@ namespace ib {
 
 namespace {
 
+// Reads from [p, end).  Every length comes from the file, so each check compares it
+// with the bytes left instead of forming p + n, which a huge n would wrap.
 struct Cursor {
     const uint8_t* p;
     const uint8_t* end;
+    uint64_t left() const { return (uint64_t)(end - p); }
     template <typename T>
     T get() {
-        if (p + sizeof(T) > end) throw std::runtime_error("GGUF: truncated file");
+        if (left() < sizeof(T)) throw std::runtime_error("GGUF: truncated file");
         T v;
         std::memcpy(&v, p, sizeof(T));
         p += sizeof(T);
@@ -31,16 +35,22 @@ struct Cursor {
     }
     std::string str() {
         uint64_t n = get<uint64_t>();
-        if (p + n > end) throw std::runtime_error("GGUF: truncated string");
+        if (n > left()) throw std::runtime_error("GGUF: truncated string");
         std::string s(reinterpret_cast<const char*>(p), n);
         p += n;
         return s;
     }
-    void skip(uint64_t n) {
-        if (p + n > end) throw std::runtime_error("GGUF: truncated value");
-        p += n;
+    void skip(uint64_t n, uint64_t elem_size) {
+        if (elem_size == 0 || n > left() / elem_size)
+            throw std::runtime_error("GGUF: truncated value");
+        p += n * elem_size;
     }
 };
+
+// Float metadata as an integer, where it has one.
+int64_t float_to_int(double f) {
+    return std::isfinite(f) && std::fabs(f) < 9.0e18 ? (int64_t)f : 0;
+}
 
 size_t scalar_size(uint32_t t) {
     switch (t) {
@@ -93,7 +103,7 @@ void GGUFFile::open(const std::string& path) {
             } else {
                 size_t sz = scalar_size(at);
                 if (!sz) throw std::runtime_error("GGUF: bad array type");
-                c.skip(n * sz);
+                c.skip(n, sz);
             }
             mv.array_len = n;
         } else {
@@ -106,11 +116,16 @@ void GGUFFile::open(const std::string& path) {
                 case 3: mv.i = c.get<int16_t>(); break;
                 case 4: mv.i = c.get<uint32_t>(); break;
                 case 5: mv.i = c.get<int32_t>(); break;
-                case 6: mv.f = c.get<float>(); mv.i = (int64_t)mv.f; break;
+                case 6: mv.f = c.get<float>(); mv.i = float_to_int(mv.f); break;
                 case 7: mv.i = c.get<uint8_t>(); break;
                 case 10: mv.i = (int64_t)c.get<uint64_t>(); break;
                 case 11: mv.i = c.get<int64_t>(); break;
-                case 12: mv.f = (float)c.get<double>(); mv.i = (int64_t)mv.f; break;
+                case 12: {
+                    const double d = c.get<double>();
+                    mv.f = (float)d;
+                    mv.i = float_to_int(d);
+                    break;
+                }
             }
             if (t != 6 && t != 12) mv.f = (float)mv.i;
         }
@@ -128,6 +143,7 @@ void GGUFFile::open(const std::string& path) {
     uint64_t align = 32;
     auto it = meta_.find("general.alignment");
     if (it != meta_.end() && it->second.i > 0) align = (uint64_t)it->second.i;
+    if (align > (1u << 30)) throw std::runtime_error("GGUF: alignment out of range");
     data_offset_ = ((size_t)(c.p - base_) + align - 1) / align * align;
 }
 
@@ -138,9 +154,10 @@ const GGUFFile::TensorInfo* GGUFFile::find(const std::string& name) const {
 }
 
 const uint8_t* GGUFFile::data(const TensorInfo& t, size_t bytes) const {
-    size_t off = data_offset_ + t.offset;
-    if (off + bytes > size_) throw std::runtime_error("GGUF: tensor data out of range: " + t.name);
-    return base_ + off;
+    const uint64_t room = data_offset_ <= size_ ? size_ - data_offset_ : 0;
+    if (t.offset > room || bytes > room - t.offset)
+        throw std::runtime_error("GGUF: tensor data out of range: " + t.name);
+    return base_ + data_offset_ + t.offset;
 }
 
 int64_t GGUFFile::get_int(const std::string& key, int64_t def) const {

@@ -15,8 +15,10 @@
 #include <math.h>
 
 #include <chrono>
+#include <cstdint>
 #include <map>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -1028,22 +1030,40 @@ static int load_gguf(const char* path, int precision, int device, int max_seq, C
         c.vocab = (int)te->dims[1];
         const auto* g = f.find("blk.0.ffn_gate.weight");
         c.ffn = g && g->dims.size() == 2 ? (int)g->dims[1] : (int)f.get_int("llama.feed_forward_length", 0);
-        void* h = nullptr;
-        int st = model_create(&c, device, comm, &h);
-        if (st) return st;
+        // Every tensor's shape, type and byte range are checked before any device work,
+        // so a malformed file fails here with nothing to release.
+        struct Planned {
+            const GGUFFile::TensorInfo* t;
+            int64_t rows, cols;
+            const uint8_t* bytes;
+        };
+        std::vector<Planned> plan;
         for (const auto& t : f.tensors()) {
-            int64_t cols = t.dims.empty() ? 0 : t.dims[0];
-            int64_t rows = 1;
-            for (size_t d = 1; d < t.dims.size(); ++d) rows *= t.dims[d];
-            const int64_t nb = t.type == IB_TYPE_F32 ? rows * cols * 4
-                               : t.type == IB_TYPE_F16 ? rows * cols * 2
+            if (t.dims.empty() || t.dims.size() > 4)
+                throw std::runtime_error("GGUF: tensor " + t.name + " has " +
+                                         std::to_string(t.dims.size()) + " dimensions");
+            int64_t elems = 1;
+            for (int64_t d : t.dims) {
+                if (d <= 0 || d > INT32_MAX || elems > (int64_t(1) << 40) / d)
+                    throw std::runtime_error("GGUF: tensor " + t.name + " has a dimension out of range");
+                elems *= d;
+            }
+            const int64_t cols = t.dims[0], rows = elems / cols;
+            const int64_t nb = t.type == IB_TYPE_F32 ? elems * 4
+                               : t.type == IB_TYPE_F16 ? elems * 2
                                                        : packed_bytes(t.type, rows, cols);
             if (nb < 0) {
-                ib_model_free(h);
                 set_error("model: unsupported tensor type in " + t.name);
                 return IB_ERR_UNSUPPORTED;
             }
-            st = ib_model_set_tensor(h, t.name.c_str(), t.type, rows, cols, f.data(t, (size_t)nb), 0);
+            plan.push_back({&t, rows, cols, f.data(t, (size_t)nb)});
+        }
+        void* h = nullptr;
+        int st = model_create(&c, device, comm, &h);
+        if (st) return st;
+        for (const Planned& pl : plan) {
+            const auto& t = *pl.t;
+            st = ib_model_set_tensor(h, t.name.c_str(), t.type, pl.rows, pl.cols, pl.bytes, 0);
             if (st) {
                 if (st == IB_ERR_INVALID && ib::last_error().rfind("model: unknown tensor", 0) == 0) continue;
                 ib_model_free(h);
