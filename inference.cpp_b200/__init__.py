@@ -115,7 +115,8 @@ def lib() -> ctypes.CDLL:
 
 
 def last_error() -> str:
-    return (lib().ib_last_error() or b"").decode()
+    # messages can quote names read from a file, which need not be valid UTF-8
+    return (lib().ib_last_error() or b"").decode("utf-8", errors="replace")
 
 
 def check(status: int, what: str = "") -> None:

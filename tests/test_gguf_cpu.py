@@ -96,3 +96,33 @@ def test_well_formed_file_passes_the_parser():
     rc, h, msg = load(raw)
     assert rc != 0 and h is None
     assert "GGUF" not in msg and "configuration" in msg, msg
+
+
+def test_mutated_files_fail_cleanly():
+    """Seeded byte mutations and truncations of a valid file: every load returns (an
+    error, or a model where the mutation kept the file valid), and the message decodes
+    even when it quotes bytes from the file."""
+    import numpy as np
+    from inference_cpp_b200 import gguf_writer as gw
+    cfg = gw.LlamaConfig("fz", 1, 256, 4, 2, 512, 64, 32, 10000.0, 1e-5)
+    rng = np.random.default_rng(2026)
+    with tempfile.TemporaryDirectory() as d:
+        base = os.path.join(d, "base.gguf")
+        gw.write_llama_gguf(base, cfg, seed=1, synth_host=ib.synth_host)
+        raw = open(base, "rb").read()
+        path = os.path.join(d, "m.gguf")
+        for _ in range(300):
+            b = bytearray(raw)
+            if rng.integers(0, 3) == 0:
+                b = b[:int(rng.integers(0, len(b)))]
+            else:
+                for _ in range(int(rng.integers(1, 8))):
+                    b[int(rng.integers(0, 4096))] = int(rng.integers(0, 256))
+            with open(path, "wb") as f:
+                f.write(bytes(b))
+            h = ctypes.c_void_p()
+            rc = ib.lib().ib_model_load_gguf(path.encode(), 0, 0, 64, ctypes.byref(h))
+            if rc == 0:
+                ib.lib().ib_model_free(h)
+            else:
+                assert h.value is None and isinstance(ib.last_error(), str)
