@@ -57,3 +57,18 @@ def test_cpu_reference_sample_is_bounded(use_ref):
     assert tps > 0 and len(per) == 1
     if not use_ref:
         assert kind == "port"
+
+
+def test_clock_records_that_force_a_remeasurement():
+    ok = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    assert not bench.clocks_rejected(ok)
+    # the power cap alone is normal under load
+    assert not bench.clocks_rejected({"sm_mhz": 1300.0, "sm_max_mhz": 1965.0,
+                                      "reasons": ["sw_power_cap"]})
+    for r in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"):
+        assert bench.clocks_rejected(dict(ok, reasons=[r]))
+    # clocks well below their maximum with no reason: a lock left by someone else
+    assert bench.clocks_rejected({"sm_mhz": 1200.0, "sm_max_mhz": 1965.0, "reasons": []})
+    # no samples: nothing to reject on
+    assert not bench.clocks_rejected({"sm_mhz": None, "sm_max_mhz": None,
+                                      "reasons": ["nvidia-smi unavailable"]})
