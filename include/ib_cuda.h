@@ -106,11 +106,14 @@ int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float* dev_y, int
  * whose allocator is owned by another runtime, a memory-budgeted process).  The
  * activation-limb scratch is a static device array of 144 KiB, which caps cols at
  * IB_NOALLOC_MAX_COLS; larger cols return IB_ERR_INVALID with a message naming the
- * limit.  The first call on each device resolves that array's address (set-up); make
- * it before any stream capture.  The scratch needs no zeroing.  Calls overlapping in
- * time on one device share the scratch and race: order them on one stream.  The
- * weight pointer must meet the format's alignment (16 bytes for Q4_K, 8 for Q5_1,
- * 2 otherwise) and x 16 bytes; all six block formats are accepted. */
+ * limit.  The first call on each device resolves that array's address and prepares
+ * the kernels of all six formats (set-up); make it before any stream capture.  The
+ * resolved address belongs to the device's primary context: do not call this entry
+ * point again after cudaDeviceReset (or any other teardown of that context) in the
+ * same process.  The scratch needs no zeroing.  Calls overlapping in time on one
+ * device share the scratch and race: order them on one stream.  The weight pointer
+ * must meet the format's alignment (16 bytes for Q4_K, 8 for Q5_1, 2 otherwise) and
+ * x 16 bytes; all six block formats are accepted. */
 #define IB_NOALLOC_MAX_COLS 32768
 int ib_gemv_q_noalloc(int type, const void* dev_W, const float* dev_x, float* dev_y,
                       int64_t rows, int64_t cols, void* stream);

@@ -26,6 +26,8 @@
 // and t = 1 (limbs 2, 3), combined as (c0 * 128 + c1) * 2^-7 or * 2^-21.
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "gemv_math.cuh"
 #include "gemv_mma.cuh"
@@ -238,45 +240,98 @@ void xlimbs_carve(void* base, int K, XLimbs& xb) {
     xb.sum16 = (float*)p;
 }
 
+// Per-device launch set-up of each format's kernels: the shared-memory opt-in and the
+// occupancy of the TMA kernel, and the function attributes of the direct-load kernel
+// (which also makes the runtime load a lazily loaded module).  Done once per (device,
+// format) under a mutex, so concurrent first calls from several host threads are safe.
+constexpr int kSetupDevices = 64;
+static std::mutex g_setup_mu;
+static uint64_t g_setup_done[kSetupDevices];  // bit fmt_slot(TYPE) per device
+static int g_max_ctas[kSetupDevices][6];
+
+template <int TYPE>
+constexpr int fmt_slot() {
+    return TYPE == IB_TYPE_Q4_K ? 0 : TYPE == IB_TYPE_Q6_K ? 1 : TYPE == IB_TYPE_Q4_0 ? 2
+         : TYPE == IB_TYPE_Q5_0 ? 3 : TYPE == IB_TYPE_Q5_1 ? 4 : 5;
+}
+
+template <int TYPE>
+constexpr int ring_stages() {
+    return TYPE == IB_TYPE_Q6_K ? 2 : (TYPE == IB_TYPE_Q8_0 ? 3 : 4);
+}
+
+// With g_setup_mu held: the set-up of TYPE on device dev; *cap = resident TMA CTAs.
+template <int TYPE>
+static int setup_typed_locked(int dev, int* cap) {
+    using F = Fmt<TYPE>;
+    constexpr int NWC = 8, S = ring_stages<TYPE>(), slot = fmt_slot<TYPE>();
+    if (!(g_setup_done[dev] & (1ull << slot))) {
+        const size_t smem = (size_t)S * 16 * F::CHUNK;
+        auto kern = gemv_tma_kernel<TYPE, NWC, S>;
+        if (smem + 2048 > 48 * 1024)
+            IB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem));
+        int per_sm = 0, sms = 0;
+        IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (NWC + 1) * 32,
+                                                                    smem));
+        IB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        cudaFuncAttributes fa;
+        IB_CUDA_CHECK(cudaFuncGetAttributes(&fa, gemv_direct_kernel<TYPE, 8>));
+        g_max_ctas[dev][slot] = (per_sm > 0 ? per_sm : 1) * sms;
+        g_setup_done[dev] |= 1ull << slot;
+    }
+    *cap = g_max_ctas[dev][slot];
+    return IB_OK;
+}
+
+static int current_device(int* dev) {
+    IB_CUDA_CHECK(cudaGetDevice(dev));
+    IB_REQUIRE(*dev >= 0 && *dev < kSetupDevices, "gemv: device ordinal out of range");
+    return IB_OK;
+}
+
 template <int TYPE>
 static int launch_typed(const uint8_t* W, const XLimbs& xb, float* y, int64_t rows, int64_t cols,
                         cudaStream_t st) {
     using F = Fmt<TYPE>;
     constexpr int NWC = 8;
-    constexpr int S = TYPE == IB_TYPE_Q6_K ? 2 : (TYPE == IB_TYPE_Q8_0 ? 3 : 4);
+    constexpr int S = ring_stages<TYPE>();
     const int nb = (int)(cols / (F::K ? 256 : 32));
     const int n_rg = (int)((rows + 15) / 16);
     const size_t rbytes = (size_t)nb * F::BB;
     const bool tma_ok = nb % F::KB == 0 && rbytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
     if (tma_ok) {
         const size_t smem = (size_t)S * 16 * F::CHUNK;
-        auto kern = gemv_tma_kernel<TYPE, NWC, S>;
-        static int attr_dev_mask = 0;  // smem opt-in beyond 48 KB, once per device
-        static int max_ctas[64] = {0};
-        int dev = 0;
-        IB_CUDA_CHECK(cudaGetDevice(&dev));
-        if (!(attr_dev_mask & (1 << dev))) {
-            if (smem + 2048 > 48 * 1024)
-                IB_CUDA_CHECK(cudaFuncSetAttribute(
-                    kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            int per_sm = 0, sms = 0;
-            IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern,
-                                                                        (NWC + 1) * 32, smem));
-            IB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-            max_ctas[dev & 63] = (per_sm > 0 ? per_sm : 1) * sms;
-            attr_dev_mask |= 1 << dev;
+        int dev = 0, cap = 0, r;
+        if ((r = current_device(&dev))) return r;
+        {
+            std::lock_guard<std::mutex> lock(g_setup_mu);
+            if ((r = setup_typed_locked<TYPE>(dev, &cap))) return r;
         }
         // as many CTAs as fit, but dividing the row groups evenly
-        const int cap = max_ctas[dev & 63];
         const int per = (n_rg + cap - 1) / cap;
         const int grid = (n_rg + per - 1) / per;
-        kern<<<grid, (NWC + 1) * 32, smem, st>>>(W, xb, y, (int)rows, nb);
+        gemv_tma_kernel<TYPE, NWC, S><<<grid, (NWC + 1) * 32, smem, st>>>(W, xb, y, (int)rows, nb);
         IB_LAUNCH_CHECK("gemv_tma_kernel");
         return IB_OK;
     }
     gemv_direct_kernel<TYPE, 8><<<(unsigned)n_rg, 256, 0, st>>>(W, xb, y, (int)rows, nb);
     IB_LAUNCH_CHECK("gemv_direct_kernel");
     return IB_OK;
+}
+
+int gemv_mma_prepare_device() {
+    int dev = 0, cap = 0, r;
+    if ((r = current_device(&dev))) return r;
+    cudaFuncAttributes fa;
+    IB_CUDA_CHECK(cudaFuncGetAttributes(&fa, xq_kernel));
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    if ((r = setup_typed_locked<IB_TYPE_Q4_K>(dev, &cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q6_K>(dev, &cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q4_0>(dev, &cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q5_0>(dev, &cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q5_1>(dev, &cap))) return r;
+    return setup_typed_locked<IB_TYPE_Q8_0>(dev, &cap);
 }
 
 int gemv_mma_launch(int type, const void* W, const XLimbs& xb, float* y, int64_t rows,

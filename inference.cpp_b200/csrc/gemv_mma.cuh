@@ -23,6 +23,10 @@ bool gemv_mma_supported(int type);
 int gemv_mma_align(int type);
 int gemv_mma_launch(int type, const void* W, const XLimbs& xb, float* y, int64_t rows,
                     int64_t cols, cudaStream_t st);
+// Launch set-up of every format's GEMV kernels on the current device (function
+// attributes, shared-memory opt-in, occupancy, module loading), so later first calls of
+// a format do none of it.  Idempotent and thread-safe.
+int gemv_mma_prepare_device();
 // Reads and clears the GEMV kernels' fault word (0 = no bounded wait expired).
 int gemv_fault_take(int* code);
 

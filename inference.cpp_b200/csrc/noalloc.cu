@@ -2,11 +2,16 @@
 // scratch in a fixed file-scope device array, so a call allocates no device memory.
 //
 // The array's address is resolved once per device with cudaGetSymbolAddress, with
-// that device current, on the first call made on it; later calls reuse it.  The
-// scratch needs no initial value: every byte the GEMV kernel reads is first written
-// by the limb kernel of the same call, on the same stream.  Two calls in flight on
-// one device at once (different streams or host threads without ordering between
-// them) share the array and race.
+// that device current, on the first call made on it; later calls reuse it.  The same
+// one-time set-up prepares every kernel instance the entry point can launch, for all
+// six formats (function attributes, shared-memory opt-in, occupancy, module loading),
+// so a later first call of another format does no first-use work either.  The cached
+// address belongs to the device's primary context: after cudaDeviceReset, or anything
+// else that destroys that context, this entry point must not be called again in the
+// process.  The scratch needs no initial value: every byte the GEMV kernel reads is
+// first written by the limb kernel of the same call, on the same stream.  Two calls in
+// flight on one device at once (different streams or host threads without ordering
+// between them) share the array and race.
 #include <mutex>
 #include <string>
 
@@ -43,6 +48,8 @@ int scratch_address(void** out) {
                       cudaGetErrorString(e));
             return IB_ERR_CUDA;
         }
+        const int r = gemv_mma_prepare_device();
+        if (r != IB_OK) return r;
         g_scratch_addr[dev] = p;
     }
     *out = g_scratch_addr[dev];

@@ -308,13 +308,45 @@ static float dot_i16(const int16_t* a, const float* b, int64_t n, float s) {
     return s;
 }
 
+/* Threads of the row loops below (1 = sequential).  Rows are independent and each row's
+ * sum keeps the sequential order above, so the result does not depend on the count. */
+static int g_threads = 1;
+void orc_set_threads(int n) { g_threads = n > 0 ? n : 1; }
+
+/* dot() of four rows against one x, interleaved so the four sums proceed side by side;
+ * each sum sees exactly the operations dot() would apply to its row. */
+static void dot4(const float* a0, const float* a1, const float* a2, const float* a3,
+                 const float* b, int64_t n, float* out) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int64_t i = 0;
+    if (n >= 8) {
+        int64_t m = n & ~(int64_t)7;
+        if (n - m >= 4) m += 4;
+        for (; i < m; ++i) {
+            const float x = b[i];
+            s0 += a0[i] * x; s1 += a1[i] * x; s2 += a2[i] * x; s3 += a3[i] * x;
+        }
+    }
+    for (; i < n; ++i) {
+        s0 = fmaf(a0[i], b[i], s0); s1 = fmaf(a1[i], b[i], s1);
+        s2 = fmaf(a2[i], b[i], s2); s3 = fmaf(a3[i], b[i], s3);
+    }
+    out[0] = s0; out[1] = s1; out[2] = s2; out[3] = s3;
+}
+
 /* matvec: src/models/transformer.cpp:100-119 */
 void orc_matvec_f32(const float* W, const float* x, float* y, int64_t rows, int64_t cols) {
-    for (int64_t r = 0; r < rows; ++r) y[r] = dot(W + r * cols, x, cols, 0.0f);
+    const int64_t r4 = rows & ~(int64_t)3;
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1 && rows >= 256)
+    for (int64_t r = 0; r < r4; r += 4)
+        dot4(W + r * cols, W + (r + 1) * cols, W + (r + 2) * cols, W + (r + 3) * cols, x, cols,
+             y + r);
+    for (int64_t r = r4; r < rows; ++r) y[r] = dot(W + r * cols, x, cols, 0.0f);
 }
 
 void orc_matvec_i16(const int16_t* q, const float* scale, const float* x, float* y,
                     int64_t rows, int64_t cols) {
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1 && rows >= 256)
     for (int64_t r = 0; r < rows; ++r) y[r] = dot_i16(q + r * cols, x, cols, 0.0f) * scale[r];
 }
 
@@ -406,6 +438,52 @@ static void mv(const OWeight* w, const float* x, float* y, int64_t rows, int64_t
     else orc_matvec_f32(w->f, x, y, rows, cols);
 }
 
+/* mv() for T inputs X[T][cols] -> Y[T][rows]: each output is the same sequential sum
+ * as mv() gives it.  FP32 weights: the inputs are transposed to XT[cols][16] and one
+ * weight row is multiplied against 16 inputs at once, one vector lane per input, each
+ * lane doing dot()'s products and additions in dot()'s order (no contraction: this file
+ * is compiled with -ffp-contract=off); the scalar tail is fused as in dot(). */
+typedef float v8f __attribute__((vector_size(32)));
+
+static void mv_batch(const OWeight* w, const float* X, float* Y, int T, int64_t rows,
+                     int64_t cols) {
+    if (T == 1) { mv(w, X, Y, rows, cols); return; }
+    int64_t m = 0;  /* dot()'s unfused part */
+    if (cols >= 8) {
+        m = cols & ~(int64_t)7;
+        if (cols - m >= 4) m += 4;
+    }
+    for (int t0 = 0; t0 < T; t0 += 16) {
+        const int nt = T - t0 < 16 ? T - t0 : 16;
+        float* XT = (float*)aligned_alloc(32, (size_t)cols * 16 * 4);
+        for (int64_t j = 0; j < cols; ++j)
+            for (int t = 0; t < 16; ++t) XT[j * 16 + t] = t < nt ? X[(size_t)(t0 + t) * cols + j] : 0.0f;
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1 && rows >= 64)
+        for (int64_t r = 0; r < rows; ++r) {
+            float o[16];
+            if (w->int16) {
+                for (int t = 0; t < nt; ++t)
+                    o[t] = dot_i16(w->q + r * cols, X + (size_t)(t0 + t) * cols, cols, 0.0f) * w->s[r];
+            } else {
+                const float* wr = w->f + r * cols;
+                v8f a0 = {0}, a1 = {0};
+                for (int64_t j = 0; j < m; ++j) {
+                    const float wj = wr[j];
+                    const v8f wv = {wj, wj, wj, wj, wj, wj, wj, wj};
+                    const v8f x0 = *(const v8f*)(XT + j * 16), x1 = *(const v8f*)(XT + j * 16 + 8);
+                    a0 = a0 + wv * x0;
+                    a1 = a1 + wv * x1;
+                }
+                for (int t = 0; t < 8; ++t) { o[t] = a0[t]; o[t + 8] = a1[t]; }
+                for (int64_t j = m; j < cols; ++j)
+                    for (int t = 0; t < 16; ++t) o[t] = fmaf(wr[j], XT[j * 16 + t], o[t]);
+            }
+            for (int t = 0; t < nt; ++t) Y[(size_t)(t0 + t) * rows + r] = o[t];
+        }
+        free(XT);
+    }
+}
+
 static void emb_row(const OWeight* w, int tok, float* out, int64_t dim) {
     if (!w->int16) memcpy(out, w->f + (int64_t)tok * dim, (size_t)dim * 4);
     else for (int64_t i = 0; i < dim; ++i) out[i] = (float)w->q[(int64_t)tok * dim + i] * w->s[tok];
@@ -413,54 +491,74 @@ static void emb_row(const OWeight* w, int tok, float* out, int64_t dim) {
 
 static float sumsq(const float* x, int n) { return dot(x, x, n, 0.0f); }
 
-/* One token at absolute position pos; writes V logits. */
-static void forward_one(OModel* m, int tok, int pos, float* logits) {
+/* T tokens at absolute positions pos0..pos0+T-1, layer by layer.  Every token goes
+ * through exactly the arithmetic of a token-by-token forward: the block's k/v rows
+ * enter the cache before any of its attention runs, and token t attends to positions
+ * <= pos0 + t only.  logits (may be NULL: the head is then skipped) receives the V
+ * logits of the last token. */
+static void forward_block(OModel* m, const int* toks, int T, int pos0, float* logits) {
     const int D = m->D, H = m->H, Hkv = m->Hkv, HD = m->HD, F = m->FFN;
-    float* x = (float*)malloc((size_t)D * 4);
-    float* xn = (float*)malloc((size_t)D * 4);
-    float* q = (float*)malloc((size_t)H * HD * 4);
-    float* k = (float*)malloc((size_t)Hkv * HD * 4);
-    float* v = (float*)malloc((size_t)Hkv * HD * 4);
-    float* att = (float*)malloc((size_t)H * HD * 4);
-    float* sc = (float*)malloc((size_t)(pos + 1) * 4);
-    float* o = (float*)malloc((size_t)D * 4);
-    float* g = (float*)malloc((size_t)F * 4);
-    float* u = (float*)malloc((size_t)F * 4);
-    if (tok < 0 || tok >= m->V) tok = 0;
-    emb_row(&m->tok, tok, x, D);
+    const int last = pos0 + T - 1;
+    float* x = (float*)malloc((size_t)T * D * 4);
+    float* xn = (float*)malloc((size_t)T * D * 4);
+    float* q = (float*)malloc((size_t)T * H * HD * 4);
+    float* k = (float*)malloc((size_t)T * Hkv * HD * 4);
+    float* v = (float*)malloc((size_t)T * Hkv * HD * 4);
+    float* att = (float*)malloc((size_t)T * H * HD * 4);
+    float* scores = (float*)malloc((size_t)T * H * (last + 1) * 4);
+    float* o = (float*)malloc((size_t)T * D * 4);
+    float* g = (float*)malloc((size_t)T * F * 4);
+    float* u = (float*)malloc((size_t)T * F * 4);
+    for (int t = 0; t < T; ++t) {
+        int tok = toks[t];
+        if (tok < 0 || tok >= m->V) tok = 0;
+        emb_row(&m->tok, tok, x + (size_t)t * D, D);
+    }
     for (int l = 0; l < m->n_layers; ++l) {
         OWeight* L = &m->L[l * W_PER_LAYER];
-        float rms = sqrtf(sumsq(x, D) / D + m->eps);
-        for (int d = 0; d < D; ++d) xn[d] = x[d] / rms * L[W_AN].f[d];
-        mv(&L[W_Q], xn, q, H * HD, D);
-        mv(&L[W_K], xn, k, Hkv * HD, D);
-        mv(&L[W_V], xn, v, Hkv * HD, D);
-        for (int hh = 0; hh < H + Hkv; ++hh) {
-            float* vec = hh < H ? q + hh * HD : k + (hh - H) * HD;
-            for (int d = 0; d < HD; d += 2) {
-                float freq = 1.0f / powf(m->theta, (float)d / HD);
-                float ang = pos * freq;
-                float c = cosf(ang), s = sinf(ang);
-                float a = vec[d], b = vec[d + 1];
-                vec[d] = a * c - b * s;
-                vec[d + 1] = a * s + b * c;
-            }
+        for (int t = 0; t < T; ++t) {
+            const float* xt = x + (size_t)t * D;
+            float rms = sqrtf(sumsq(xt, D) / D + m->eps);
+            for (int d = 0; d < D; ++d) xn[(size_t)t * D + d] = xt[d] / rms * L[W_AN].f[d];
         }
+        mv_batch(&L[W_Q], xn, q, T, H * HD, D);
+        mv_batch(&L[W_K], xn, k, T, Hkv * HD, D);
+        mv_batch(&L[W_V], xn, v, T, Hkv * HD, D);
         float* kc = m->kc + (size_t)l * Hkv * m->max_seq * HD;
         float* vc = m->vc + (size_t)l * Hkv * m->max_seq * HD;
-        for (int hk = 0; hk < Hkv; ++hk)
-            for (int d = 0; d < HD; ++d) {
-                kc[((size_t)hk * m->max_seq + pos) * HD + d] = k[hk * HD + d];
-                vc[((size_t)hk * m->max_seq + pos) * HD + d] = v[hk * HD + d];
+        for (int t = 0; t < T; ++t) {
+            const int pos = pos0 + t;
+            float* qt = q + (size_t)t * H * HD;
+            float* kt = k + (size_t)t * Hkv * HD;
+            for (int hh = 0; hh < H + Hkv; ++hh) {
+                float* vec = hh < H ? qt + hh * HD : kt + (hh - H) * HD;
+                for (int d = 0; d < HD; d += 2) {
+                    float freq = 1.0f / powf(m->theta, (float)d / HD);
+                    float ang = pos * freq;
+                    float c = cosf(ang), s = sinf(ang);
+                    float a = vec[d], b = vec[d + 1];
+                    vec[d] = a * c - b * s;
+                    vec[d + 1] = a * s + b * c;
+                }
             }
+            for (int hk = 0; hk < Hkv; ++hk)
+                for (int d = 0; d < HD; ++d) {
+                    kc[((size_t)hk * m->max_seq + pos) * HD + d] = kt[hk * HD + d];
+                    vc[((size_t)hk * m->max_seq + pos) * HD + d] = v[(size_t)t * Hkv * HD + hk * HD + d];
+                }
+        }
         const int grp = H / Hkv;
-        for (int hq = 0; hq < H; ++hq) {
+#pragma omp parallel for schedule(dynamic) num_threads(g_threads) if (g_threads > 1 && T * H > 1)
+        for (int th = 0; th < T * H; ++th) {
+            const int t = th / H, hq = th % H, pos = pos0 + t;
+            const float* qh = q + (size_t)t * H * HD + (size_t)hq * HD;
+            float* sc = scores + (size_t)th * (last + 1);
             const float* kh = kc + (size_t)(hq / grp) * m->max_seq * HD;
             const float* vh = vc + (size_t)(hq / grp) * m->max_seq * HD;
             float mx = -INFINITY;
             for (int s = 0; s <= pos; ++s) {
                 float sco = 0.0f;
-                for (int d = 0; d < HD; ++d) sco = fmaf(q[hq * HD + d], kh[(size_t)s * HD + d], sco);
+                for (int d = 0; d < HD; ++d) sco = fmaf(qh[d], kh[(size_t)s * HD + d], sco);
                 sco /= sqrtf((float)HD);
                 sc[s] = sco;
                 mx = fmaxf(mx, sco);
@@ -471,24 +569,36 @@ static void forward_one(OModel* m, int tok, int pos, float* logits) {
             for (int d = 0; d < HD; ++d) {
                 float acc = 0;
                 for (int s = 0; s <= pos; ++s) acc = fmaf(sc[s], vh[(size_t)s * HD + d], acc);
-                att[hq * HD + d] = acc;
+                att[(size_t)t * H * HD + hq * HD + d] = acc;
             }
         }
-        mv(&L[W_O], att, o, D, H * HD);
-        for (int d = 0; d < D; ++d) x[d] += o[d];
-        rms = sqrtf(sumsq(x, D) / D + m->eps);
-        for (int d = 0; d < D; ++d) xn[d] = x[d] / rms * L[W_FN].f[d];
-        mv(&L[W_1], xn, g, F, D);
-        for (int i = 0; i < F; ++i) g[i] *= 1.0f / (1.0f + expf(-g[i]));
-        mv(&L[W_3], xn, u, F, D);
-        for (int i = 0; i < F; ++i) g[i] *= u[i];
-        mv(&L[W_2], g, o, D, F);
-        for (int d = 0; d < D; ++d) x[d] += o[d];
+        mv_batch(&L[W_O], att, o, T, D, H * HD);
+        for (size_t i = 0; i < (size_t)T * D; ++i) x[i] += o[i];
+        for (int t = 0; t < T; ++t) {
+            const float* xt = x + (size_t)t * D;
+            float rms = sqrtf(sumsq(xt, D) / D + m->eps);
+            for (int d = 0; d < D; ++d) xn[(size_t)t * D + d] = xt[d] / rms * L[W_FN].f[d];
+        }
+        mv_batch(&L[W_1], xn, g, T, F, D);
+        for (size_t i = 0; i < (size_t)T * F; ++i) g[i] *= 1.0f / (1.0f + expf(-g[i]));
+        mv_batch(&L[W_3], xn, u, T, F, D);
+        for (size_t i = 0; i < (size_t)T * F; ++i) g[i] *= u[i];
+        mv_batch(&L[W_2], g, o, T, D, F);
+        for (size_t i = 0; i < (size_t)T * D; ++i) x[i] += o[i];
     }
-    float rms = sqrtf(sumsq(x, D) / D + m->eps);
-    for (int d = 0; d < D; ++d) xn[d] = x[d] / rms * m->out_norm.f[d];
-    mv(m->tied ? &m->tok : &m->out, xn, logits, m->V, D);
-    free(x); free(xn); free(q); free(k); free(v); free(att); free(sc); free(o); free(g); free(u);
+    if (logits) {
+        const float* xt = x + (size_t)(T - 1) * D;
+        float rms = sqrtf(sumsq(xt, D) / D + m->eps);
+        for (int d = 0; d < D; ++d) xn[d] = xt[d] / rms * m->out_norm.f[d];
+        mv(m->tied ? &m->tok : &m->out, xn, logits, m->V, D);
+    }
+    free(x); free(xn); free(q); free(k); free(v); free(att); free(scores); free(o); free(g); free(u);
+}
+
+/* One token at absolute position pos; writes V logits (logits may be NULL: the output
+ * head is then skipped, as nothing reads it). */
+static void forward_one(OModel* m, int tok, int pos, float* logits) {
+    forward_block(m, &tok, 1, pos, logits);
 }
 
 /* sample_argmax: src/ops/ops.cpp:424-438 (first maximum wins) */
@@ -519,9 +629,13 @@ int orc_model_generate(void* h, const int32_t* prompt, int n_prompt, int max_tok
     int n = 0;
     for (int i = 0; i < n_prompt; ++i) out[n++] = prompt[i];
     int pos = 0;
-    for (int i = 0; i < n_prompt; ++i) {
-        if (pos >= m->max_seq) { free(lg); return -1; }
-        forward_one(m, prompt[i], pos++, lg);
+    if (n_prompt > m->max_seq) { free(lg); return -1; }
+    /* the prompt in blocks of up to 16 tokens; only the last position's logits pick a
+     * token */
+    for (int i = 0; i < n_prompt; i += 16) {
+        const int T = n_prompt - i < 16 ? n_prompt - i : 16;
+        forward_block(m, (const int*)prompt + i, T, pos, i + T == n_prompt ? lg : NULL);
+        pos += T;
     }
     for (int step = 0; step < max_tokens; ++step) {
         if (all_logits) memcpy(all_logits + (size_t)step * m->V, lg, (size_t)m->V * 4);

@@ -18,17 +18,19 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_oracle.so")
-REF_ROOT = os.environ.get("IB_REFERENCE_ROOT", "/root/reference")
+# the reference checkout whose CPU sources `build(ref=True)` compiles (environment only)
+REF_ROOT = os.environ.get("IB_REFERENCE_ROOT", "")
 
 _vp, _i, _i64, _f, _u32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint32
 
 
-def build(ref: bool = True) -> None:
+def build(ref: bool = True, ref_root: str | None = None) -> None:
     """make -C oracle port [ref] (ref only where the reference sources exist)."""
+    root = ref_root if ref_root is not None else REF_ROOT
     targets = ["port"]
-    if ref and os.path.isdir(os.path.join(REF_ROOT, "src")):
+    if ref and root and os.path.isdir(os.path.join(root, "src")):
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REF_ROOT={REF_ROOT}"] + targets, check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REF_ROOT={root}"] + targets, check=True)
 
 
 def _f32p(a):
@@ -56,7 +58,12 @@ class Port:
         L.orc_model_forward.argtypes = [_vp, _vp, _i, _i, _vp]
         L.orc_model_generate.argtypes = [_vp, _vp, _i, _i, _vp, _vp]
         L.orc_argmax.argtypes = [_vp, _i]
+        L.orc_set_threads.argtypes = [_i]
         self.L = L
+
+    def set_threads(self, n: int) -> None:
+        """Threads of the oracle's row and head loops (results do not depend on it)."""
+        self.L.orc_set_threads(int(n))
 
     def dequantize(self, type_: int, blocks: np.ndarray, n: int) -> np.ndarray:
         out = np.empty(n, dtype=np.float32)

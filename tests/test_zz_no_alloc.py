@@ -7,9 +7,14 @@ product of the dequantised weights within |y - y_ref| <= 2e-5 * sum_i |w_i x_i|
 different activations; the first call on a device does the scratch set-up.  The
 file is collected last and also passes alone in a fresh process.
 """
+import os
+import subprocess
+import sys
+import textwrap
+
 import pytest
 
-from conftest import load_package
+from conftest import ROOT, load_package
 
 ib = load_package()
 RTOL = 2e-5
@@ -62,6 +67,57 @@ def test_noalloc_allocates_nothing(cuda):
     free1, _ = ib.memory_info()
     assert free1 == free0
     assert torch.cuda.memory_allocated() == torch_alloc0
+
+
+# Run in a fresh process with lazy module loading, so that no kernel of the library has
+# been loaded or configured before the entry point's set-up call: every buffer is
+# allocated first, one set-up call (Q4_K) is made, and then the first call of every
+# format, at a shape on the TMA-staged kernel and at one on the direct-load kernel, must
+# leave the device's free memory and torch's allocator where the set-up call left them.
+_FIRST_CALLS = textwrap.dedent("""
+    import sys
+    sys.path.insert(0, {root!r})
+    import torch
+    from conftest import load_package
+    ib = load_package()
+    ib.init(0)
+    fmts = [ib.Q4_K, ib.Q6_K, ib.Q4_0, ib.Q5_0, ib.Q5_1, ib.Q8_0]
+    # (rows, cols): 4096 columns take the TMA kernel for every format; 256 columns
+    # (one K-quant block, eight 32-element blocks) take the direct-load kernel
+    shapes = [(4096, 4096), (40, 256)]
+    bufs = []
+    for t in fmts:
+        for rows, cols in shapes:
+            W = ib.synth_device(t, rows, cols, seed=rows + cols + t)
+            x = torch.randn(cols, device="cuda")
+            y = torch.empty(rows, device="cuda")
+            bufs.append((t, W, x, y, rows, cols))
+    torch.cuda.synchronize()
+    t0, W0, x0, y0, r0, c0 = bufs[0]
+    ib.gemv_q_noalloc(t0, W0, x0, y0, r0, c0)  # the one set-up call
+    torch.cuda.synchronize()
+    free0, _ = ib.memory_info()
+    alloc0 = torch.cuda.memory_allocated()
+    reserved0 = torch.cuda.memory_reserved()
+    for t, W, x, y, rows, cols in bufs[1:]:
+        ib.gemv_q_noalloc(t, W, x, y, rows, cols)
+    torch.cuda.synchronize()
+    free1, _ = ib.memory_info()
+    assert ib.check_fault() == 0
+    assert free1 == free0, (free0, free1)
+    assert torch.cuda.memory_allocated() == alloc0
+    assert torch.cuda.memory_reserved() == reserved0
+    print("first calls allocated nothing")
+""")
+
+
+def test_noalloc_first_call_of_every_format_allocates_nothing(cuda):
+    env = dict(os.environ, CUDA_MODULE_LOADING="LAZY")
+    code = _FIRST_CALLS.format(root=os.path.join(ROOT, "tests"))
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "first calls allocated nothing" in r.stdout
 
 
 def test_noalloc_rejects_cols_beyond_limit(cuda):
