@@ -40,6 +40,47 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "decode tok/s at Llama-3-8B-shape Q4_K; fused dequant-GEMV GB/s vs HBM peak"
+SHAPE_NAMES = {"llama-3-8b": "Llama-3-8B", "llama-3-70b": "Llama-3-70B",
+               "tinyllama-1.1b": "TinyLlama-1.1B", "stories15M": "stories15M",
+               "llama-3-8b-4l": "Llama-3-8B (4-layer)"}
+QUANT_NAMES = {"stories15M": "Q4_0"}
+
+
+def metric_for(cfg) -> str:
+    """The headline metric's wording for a workload (the default one is the 8B line)."""
+    if cfg.name == "llama-3-8b":
+        return METRIC
+    shape = SHAPE_NAMES.get(cfg.name, cfg.name)
+    quant = QUANT_NAMES.get(cfg.name, "Q4_K")
+    return f"decode tok/s at {shape}-shape {quant}; fused dequant-GEMV GB/s vs HBM peak"
+
+
+def weights_label(cfg) -> str:
+    names = {2: "Q4_0", 6: "Q5_0", 7: "Q5_1", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
+    lin = names.get(cfg.linear_type, str(cfg.linear_type))
+    extra = sorted({(names.get(t, str(t)), w) for t, w in
+                    ((cfg.attn_v_type, "attn_v"), (cfg.ffn_down_type, "ffn_down"),
+                     (cfg.output_type, "output")) if t != cfg.linear_type})
+    parts = [f"{lin} linears"]
+    by = {}
+    for n, w in extra:
+        by.setdefault(n, []).append(w)
+    for n, ws in by.items():
+        alt = " (alternate layers)" if cfg.q6k_alternate and n == names.get(cfg.attn_v_type) else ""
+        parts.append(f"{n} {'/'.join(ws)}{alt}")
+    return ", ".join(parts) + " (synthetic)"
+
+
+def workload_config(cfg, args, world, tp) -> dict:
+    """The config object both arms print (same keys and values for the same run)."""
+    seqs = 1 if tp else world
+    return {"workload": f"{cfg.name}-decode", "model": cfg.name, "prompt": args.prompt,
+            "global_batch": seqs, "seq_len": args.prompt + args.warmup + args.steps,
+            "parallelism": (f"tp{world}" if tp else f"replica{world}") if world > 1 else "single",
+            "weights": weights_label(cfg),
+            "l2": ("inputs larger than L2 (weights per step >> 126 MB)"
+                   if cfg.packed_weight_bytes() > 4 * 126e6 else
+                   "weights per step fit in the 126 MB L2; no flush between steps")}
 
 
 def load_pkg():
@@ -89,7 +130,7 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -259,57 +300,98 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_reference_sample(cfg, reps, warm, use_ref=True):
-    """Reference CPU matvec (FP32 host weights, single thread) on one layer's seven
-    projections plus 1/16 of the output head; returns (tok/s, kind, detail)."""
+class CpuBaselineUnavailable(Exception):
+    pass
+
+
+def cpu_forward_sample(ib, cfg, n_decode, layers=2, prompt_len=4, seed=20261201):
+    """The reference's own CPU forward (oracle/_ref: Model::forward through
+    ref_model_forward, FP32 host weights, one thread) on a reduced copy of the workload:
+    the same widths, vocabulary and quantisation, min(n_layers, `layers`) layers.  A
+    seeded GGUF of that model is written and loaded by the reference's loader; a
+    `prompt_len`-token prompt fills the KV cache, then `n_decode` single-token forwards
+    are timed.  The output head's matvec is timed alone as well, which separates it
+    from the per-layer cost; the full model's per-token time is
+        t_head + n_layers * (t_token - t_head) / layers_run.
+    The sample's positions are prompt_len.. (the GPU steps run past the prompt), so the
+    reference's attention over a long KV cache is not in it: the estimate favours the
+    CPU.  Returns a dict with the measured and extrapolated figures."""
+    import dataclasses
     import numpy as np
     sys.path.insert(0, ROOT)
     import __graft_entry__ as ge
+    from inference_cpp_b200 import gguf_writer as gw
     orc = ge.oracle()
-    kind = "reference" if (use_ref and orc.Ref.available()) else "port"
-    impl = orc.Ref() if kind == "reference" else orc.Port()
-    D, F, H, Hkv, HD, V = cfg.dim, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.vocab
-    shapes = [(H * HD, D), (Hkv * HD, D), (Hkv * HD, D), (D, H * HD), (F, D), (D, F), (F, D)]
-    rng = np.random.default_rng(0)
-    mats = [(rng.standard_normal(r * c, dtype=np.float32) * 0.02, r, c) for r, c in shapes]
-    head_rows = V // 16
-    head = rng.standard_normal(head_rows * D, dtype=np.float32) * 0.02
-    xs = {c: rng.standard_normal(c, dtype=np.float32) for _, c in shapes}
-
-    def one():
+    if not orc.Ref.available():
+        raise CpuBaselineUnavailable("oracle/_ref (the reference's CPU code) is not built")
+    if cfg.dim > 4096 or cfg.ffn > 16384:
+        raise CpuBaselineUnavailable(
+            "the reference's Model cannot run these widths: its stack arrays overflow at "
+            f"dim {cfg.dim} / ffn {cfg.ffn} (src/models/model.cpp:50,197)")
+    nl = min(cfg.n_layers, layers)
+    red = dataclasses.replace(cfg, name=cfg.name + "-cpu-sample", n_layers=nl,
+                              ctx=prompt_len + n_decode + 8)
+    ref = orc.Ref()
+    t_load = time.perf_counter()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "sample.gguf")
+        gw.write_llama_gguf(path, red, seed, ib.synth_host)
+        rm = ref.load(path, host_int16=False)
+    t_load = time.perf_counter() - t_load
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(1, cfg.vocab, size=prompt_len).astype(np.int32)
+    lg = rm.forward(prompt, 0)
+    tok = int(np.argmax(lg[-1]))
+    per = []
+    for i in range(n_decode):
         t0 = time.perf_counter()
-        for W, r, c in mats:
-            impl.matvec_f32(W, xs[c], r, c)
-        t1 = time.perf_counter()
-        impl.matvec_f32(head, xs[D], head_rows, D)
-        t2 = time.perf_counter()
-        return cfg.n_layers * (t1 - t0) + 16 * (t2 - t1)
+        lg = rm.forward(np.array([tok], dtype=np.int32), prompt_len + i)
+        per.append(time.perf_counter() - t0)
+        tok = int(np.argmax(lg[-1]))
+    t_head = rm.time_head(1)
+    t_tok = statistics.mean(per)
+    t_layer = max(t_tok - t_head, 0.0) / nl
+    full = t_head + cfg.n_layers * t_layer if nl < cfg.n_layers else t_tok
+    del rm
+    return {"sample_s": per, "sample_layers": nl, "t_head_s": t_head, "t_layer_s": t_layer,
+            "per_token_s": full, "tok_s": 1.0 / full, "load_s": t_load,
+            "positions": [prompt_len, prompt_len + n_decode - 1],
+            "sample": (f"reference Model::forward (oracle/_ref, FP32 host weights, 1 thread) on "
+                       f"a {nl}-layer copy of the workload (same widths, vocabulary and quant "
+                       f"mix): {n_decode} single-token forwards at positions {prompt_len}.."
+                       f"{prompt_len + n_decode - 1} after a {prompt_len}-token prompt; per "
+                       f"token {t_tok * 1e3:.0f} ms, output-head matvec alone "
+                       f"{t_head * 1e3:.0f} ms, so {t_layer * 1e3:.0f} ms per layer; "
+                       + (f"extrapolated to {cfg.n_layers} layers: head + {cfg.n_layers} x layer "
+                          f"= {full * 1e3:.0f} ms per token" if nl < cfg.n_layers else
+                          "the whole model, no extrapolation")
+                       + ". Attention over a long KV cache is not in the sample (it favours "
+                       "the CPU).")}
 
-    for _ in range(warm):
-        one()
-    per_tok = [one() for _ in range(reps)]
-    return 1.0 / statistics.mean(per_tok), kind, per_tok
 
-
-def run_reference(args, cfg, world, rank):
+def run_reference(args, cfg, world, rank, ib):
     if rank != 0:
         return 0
     t0 = time.perf_counter()
-    # bounded sample: at most 32 timed samples (about half a second each) so the arm ends
-    # within a few minutes whatever --steps is
-    tps, kind, per = cpu_reference_sample(cfg, min(args.steps, 32), min(args.warmup, 3))
-    cores = 1
-    line = {"metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps,
+    config = workload_config(cfg, args, world, args.tp and world > 1)
+    n = max(1, min(args.steps, 3))  # bounded: the run ends within a few minutes
+    try:
+        r = cpu_forward_sample(ib, cfg, n)
+    except CpuBaselineUnavailable as e:
+        print(json.dumps({"impl": "reference", "metric": metric_for(cfg), "unavailable": str(e),
+                          "config": config}), flush=True)
+        return 0
+    tps = r["tok_s"]
+    sample_ms = statistics.mean(r["sample_s"]) * 1e3
+    line = {"metric": metric_for(cfg), "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": 1, "ms_per_step": sample_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{cfg.name}-q4k-decode", "prompt": args.prompt,
-                       "parallelism": "cpu-1-thread"},
-            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": kind,
-                             "sample": f"{len(per)} samples, each one layer's 7 projections + "
-                                       "1/16 of the output head with the reference matvec (FP32 "
-                                       f"host weights), extrapolated to {cfg.n_layers} layers + "
-                                       "full head"},
+            "data": "synthetic", "impl": "reference", "config": config,
+            "step": "one sampled token through the reduced model (ms_per_step); value is the "
+                    "full model's tok/s extrapolated from it",
+            "extrapolated_ms_per_token": r["per_token_s"] * 1e3,
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": 1, "kind": "reference",
+                             "sample": r["sample"]},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "host_cores": os.cpu_count(), "wall_s": time.perf_counter() - t0}
     print(json.dumps(line), flush=True)
@@ -437,7 +519,7 @@ def main():
 
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
-        rc = run_reference(args, cfg, world, rank)
+        rc = run_reference(args, cfg, world, rank, ib)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
@@ -473,10 +555,16 @@ def main():
     prefill_ms = sorted(prefill_runs)[1]
 
     pos = args.prompt
+    torch.cuda.synchronize()
+    t_w = time.perf_counter()
     toks = m.decode_loop(first, pos, args.warmup)
+    torch.cuda.synchronize()
+    warm_ms = all_max(world, (time.perf_counter() - t_w) * 1e3 / args.warmup)
     pos += args.warmup
     tok = int(toks[-1])
-    torch.cuda.synchronize()
+    # replays of the timed steps before the timed region, inside the clock record: about
+    # 0.4 s, the same count on every rank (tensor-parallel steps hold collectives)
+    n_pre = max(1, int(400.0 / max(warm_ms * args.steps, 1e-3)) + 1)
     # The timed steps and the e2e steps, with SM clocks sampled throughout.  A record
     # that shows a slowdown (clocks_rejected) is measured once more over the same
     # positions and tokens, so the work is identical; every rank takes the same decision.
@@ -486,6 +574,12 @@ def main():
     for attempt in range(2):
         barrier(world)
         clocks = Clocks(local)
+        # the sampler covers n_pre replays of the same steps before the timed region (they
+        # rewrite the same KV rows with the same values), then the timed and e2e steps
+        for _ in range(n_pre):
+            m.decode_loop(tok0, pos0, args.steps)
+        torch.cuda.synchronize()
+        barrier(world)
         torch.cuda.synchronize()
         e0.record(ext)
         toks = m.decode_loop(tok0, pos0, args.steps)
@@ -527,27 +621,22 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            reps = 3
-            tps, kind, _ = cpu_reference_sample(cfg, reps, 1)
-            cpu = {"value": tps, "unit": "tok/s", "cores": 1, "kind": kind,
-                   "sample": f"{reps} samples of one layer's 7 projections + 1/16 of the output head "
-                             "(reference matvec, FP32 host weights, 1 thread), extrapolated to the "
-                             f"full {cfg.n_layers}-layer token"}
-        except Exception as e:  # the baseline is reported, never required
+            r = cpu_forward_sample(ib, cfg, 2)
+            cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": 1, "kind": "reference",
+                   "sample": r["sample"]}
+        except CpuBaselineUnavailable as e:
             cpu = {"value": None, "unit": "tok/s", "cores": 1, "kind": "unavailable", "sample": str(e)}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": 1, "kind": "unavailable", "sample": repr(e)}
     if rank == 0:
+        config = workload_config(cfg, args, world, tp)
+        config["decode_path"] = m.decode_path()
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "metric": metric_for(cfg), "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
             "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{cfg.name}-q4k-decode", "model": cfg.name,
-                       "prompt": args.prompt, "global_batch": seqs, "seq_len": pos,
-                       "parallelism": (f"tp{world}" if tp else f"replica{world}") if world > 1
-                       else "single",
-                       "weights": "Q4_K linears, Q6_K attn_v/ffn_down/output (synthetic)",
-                       "decode_path": "fused" if m.uses_fused() else "separate",
-                       "l2": "inputs larger than L2 (weights per step >> 126 MB)"},
+            "config": config,
             "e2e": {"value": seqs * e2e_steps / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -532,6 +532,10 @@ class Model:
         call("ib_model_uses_fused", self.h, ctypes.byref(f))
         return bool(f.value)
 
+    def decode_path(self) -> str:
+        """Which decode step runs: "fused" kernels or the "separate" per-op kernels."""
+        return "fused" if self.uses_fused() else "separate"
+
     def weight_bytes(self) -> int:
         n = ctypes.c_size_t()
         call("ib_model_weight_bytes", self.h, ctypes.byref(n))

@@ -170,6 +170,7 @@ class Ref:
         L.ref_model_weight_copy.argtypes = [_vp, ctypes.c_char_p, _i, _vp, _vp]
         L.ref_model_forward.argtypes = [_vp, _vp, _i, _i, _vp]
         L.ref_model_generate.argtypes = [_vp, _vp, _i, _i, _vp, _vp]
+        L.ref_model_time_head.argtypes = [_vp, _i, _vp]
         self.L = L
 
     def _chk(self, rc):
@@ -239,6 +240,12 @@ class RefModel:
         self.ref._chk(self.ref.L.ref_model_forward(self.h, ids.ctypes.data, ids.size, start,
                                                    out.ctypes.data))
         return out
+
+    def time_head(self, reps: int = 1) -> float:
+        """Seconds per call of the reference's output-head matvec alone."""
+        t = ctypes.c_double()
+        self.ref._chk(self.ref.L.ref_model_time_head(self.h, reps, ctypes.byref(t)))
+        return t.value
 
     def generate(self, prompt, max_tokens: int) -> np.ndarray:
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)

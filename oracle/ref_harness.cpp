@@ -8,6 +8,7 @@
 //   matvec (FP32 / INT16)          src/models/transformer.cpp:100-119
 //   load_model_weights (+ INT16)   src/models/transformer.cpp:135-310
 //   Model::forward / generate      src/models/model.cpp:244-399
+//   the output head's matvec       src/models/model.cpp:308-318 (timed alone)
 // The handle mirrors what src/main.cpp:117-190 builds: a GGUFParser, the loaded
 // ModelWeights moved into a Model, and a KVCache sized (layers, ctx, heads, hd).
 #include "core/tensor.hpp"
@@ -16,6 +17,7 @@
 #include "models/model.hpp"
 #include "models/transformer.hpp"
 
+#include <chrono>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -171,6 +173,24 @@ int ref_model_forward(void* h, const int32_t* ids, int T, int start_pos, float* 
         std::memcpy(input.data(), ids, static_cast<size_t>(T) * sizeof(int32_t));
         Tensor lg = m->model->forward(input, m->cache.get(), start_pos);
         std::memcpy(logits, lg.data(), lg.byte_size());
+    });
+}
+
+// Times the reference's output projection alone: matvec(output, x, logits) as
+// Model::forward applies it (src/models/model.cpp:308-318), reps times on a fixed
+// normalised input; *seconds = mean time per call.  Lets a caller separate the head
+// from the per-layer cost of a forward pass.
+int ref_model_time_head(void* h, int reps, double* seconds) {
+    return guarded([&] {
+        const ModelWeights& w = static_cast<RefModel*>(h)->model->weights();
+        const HostWeight& out_w = w.output_tied ? w.tok_embeddings : w.output;
+        std::vector<float> x(static_cast<size_t>(w.embed_dim), 0.01f);
+        std::vector<float> y(static_cast<size_t>(w.vocab_size));
+        if (reps < 1) reps = 1;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < reps; ++i) matvec(out_w, x.data(), y.data(), w.vocab_size, w.embed_dim);
+        const auto t1 = std::chrono::steady_clock::now();
+        *seconds = std::chrono::duration<double>(t1 - t0).count() / reps;
     });
 }
 
