@@ -1,5 +1,5 @@
 """bench.py pieces that need no GPU: the reference arm's JSON line (the reference's own
-CPU matvec, or the C restatement where the reference was not built here) and the
+CPU forward pass, Model::forward, on a reduced-layer copy of the workload) and the
 helpers that feed the roofline fields."""
 import json
 import os
@@ -29,9 +29,13 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC
     assert d["unit"] == "tok/s" and d["higher_is_better"] is True and d["value"] > 0
     assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] >= 3
-    assert d["config"]["workload"] == "llama-3-8b-q4k-decode"
+    assert d["config"]["workload"] == "llama-3-8b-decode"
+    # the sampled steps fit in the run: ms_per_step is one sampled token
+    assert d["ms_per_step"] * d["steps"] / 1e3 <= d["wall_s"]
+    assert d["extrapolated_ms_per_token"] >= d["ms_per_step"]
     cb = d["cpu_baseline"]
-    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert cb["kind"] == "reference" and cb["cores"] == 1 and cb["value"] == d["value"]
+    assert "2-layer copy" in cb["sample"] and "extrapolated to 32 layers" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
 
@@ -50,13 +54,24 @@ def test_roofline_helpers():
     assert bench.traffic_from_profile(123, 456) is None
 
 
-@pytest.mark.parametrize("use_ref", [False, True])
-def test_cpu_reference_sample_is_bounded(use_ref):
+def test_cpu_forward_sample_extrapolates_from_measured_layers(ib):
     from inference_cpp_b200 import gguf_writer as gw
-    tps, kind, per = bench.cpu_reference_sample(gw.CONFIGS["llama-3-8b"], 1, 0, use_ref=use_ref)
-    assert tps > 0 and len(per) == 1
-    if not use_ref:
-        assert kind == "port"
+    r = bench.cpu_forward_sample(ib, gw.CONFIGS["tinyllama-1.1b"], 1)
+    assert r["sample_layers"] == 2 and len(r["sample_s"]) == 1
+    assert r["t_head_s"] > 0 and r["t_layer_s"] > 0
+    assert abs(r["per_token_s"] - (r["t_head_s"] + 22 * r["t_layer_s"])) < 1e-9
+    # the whole model when it has no more layers than the sample
+    s = bench.cpu_forward_sample(ib, gw.CONFIGS["stories15M"], 1, layers=6)
+    assert s["sample_layers"] == 6 and s["per_token_s"] == s["sample_s"][0]
+    with pytest.raises(bench.CpuBaselineUnavailable, match="stack arrays"):
+        bench.cpu_forward_sample(ib, gw.CONFIGS["llama-3-70b"], 1)
+
+
+def test_metric_follows_the_workload():
+    from inference_cpp_b200 import gguf_writer as gw
+    assert bench.metric_for(gw.CONFIGS["llama-3-8b"]) == bench.METRIC
+    assert "Llama-3-70B-shape" in bench.metric_for(gw.CONFIGS["llama-3-70b"])
+    assert "stories15M-shape Q4_0" in bench.metric_for(gw.CONFIGS["stories15M"])
 
 
 def test_clock_records_that_force_a_remeasurement():
