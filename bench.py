@@ -499,8 +499,10 @@ def main():
     ap.add_argument("--nvtx-step", action="store_true",
                     help="after the measurement, run one ungraphed decode step in an NVTX "
                          "range named decode_step (for profiler launch lists)")
-    ap.add_argument("--decode-path", default="fused", choices=["fused", "separate"],
-                    help="fused decode kernels (default) or the separate per-op kernels")
+    ap.add_argument("--decode-path", default="fused",
+                    choices=["persistent", "fused", "separate"],
+                    help="the fused per-operation kernels (default), the persistent decode "
+                         "step (one kernel per token), or the separate per-op kernels")
     ap.add_argument("--sweep", action="store_true",
                     help="per-format GEMV / dequantisation GB/s over the op-sweep shapes "
                          "(one JSON line each) instead of the decode benchmark")
@@ -534,7 +536,8 @@ def main():
     tp = args.tp and world > 1
     comm = make_comm(ib, world, rank, local) if tp else None
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
-    m.set_fused(args.decode_path == "fused")
+    m.set_fused(args.decode_path != "separate")
+    m.set_persistent(args.decode_path == "persistent")
     rng = np.random.default_rng(42)
     prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
 

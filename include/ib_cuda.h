@@ -260,8 +260,20 @@ int ib_model_set_graph(void* model, int enabled);
  * SwiGLU and one down GEMV with the residual add, chained by programmatic dependent
  * launch.  Used only when every weight's format and shape has a fused kernel. */
 int ib_model_set_fused(void* model, int enabled);
-/* *fused = 1 when decode steps run on the fused kernels. */
+/* *fused = 1 when decode steps run on the fused kernels (either decode path below). */
 int ib_model_uses_fused(void* model, int* fused);
+/* Persistent decode step (default off): one kernel launch runs the whole step -- the
+ * fused kernels' work as a task list claimed in dependency order by a persistent grid,
+ * weights streaming across layer boundaries, attention splits and limb slabs published
+ * through per-slice readiness counters.  Used on one GPU when the fused kernels are in
+ * use and the shapes fit (head_dim 32, 64 or 128, at most 8 query heads per kv head);
+ * otherwise the fused per-operation kernels run.  No counterpart in the reference. */
+int ib_model_set_persistent(void* model, int enabled);
+#define IB_DECODE_SEPARATE 0
+#define IB_DECODE_FUSED 1
+#define IB_DECODE_PERSISTENT 2
+/* Which decode step runs: IB_DECODE_SEPARATE / _FUSED / _PERSISTENT. */
+int ib_model_decode_path(void* model, int* path);
 /* The stream the model launches on (a cudaStream_t), e.g. for event timing. */
 int ib_model_stream(void* model, void** stream);
 /* Number of kernels one decode step launches. */

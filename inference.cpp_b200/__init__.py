@@ -461,6 +461,8 @@ SIGNATURES.update({
     "ib_model_set_graph": [_vp, _i],
     "ib_model_set_fused": [_vp, _i],
     "ib_model_uses_fused": [_vp, _vp],
+    "ib_model_set_persistent": [_vp, _i],
+    "ib_model_decode_path": [_vp, _vp],
     "ib_model_weight_bytes": [_vp, _vp],
     "ib_model_decode_loop": [_vp, _c.c_int32, _i, _i, _vp],
     "ib_model_stream": [_vp, _vp],
@@ -532,9 +534,16 @@ class Model:
         call("ib_model_uses_fused", self.h, ctypes.byref(f))
         return bool(f.value)
 
+    def set_persistent(self, enabled: bool):
+        """The persistent decode step (one kernel per token) when the model supports it."""
+        call("ib_model_set_persistent", self.h, 1 if enabled else 0)
+
     def decode_path(self) -> str:
-        """Which decode step runs: "fused" kernels or the "separate" per-op kernels."""
-        return "fused" if self.uses_fused() else "separate"
+        """Which decode step runs: "persistent" (one kernel per token), "fused" per-op
+        kernels, or the "separate" kernels."""
+        p = ctypes.c_int()
+        call("ib_model_decode_path", self.h, ctypes.byref(p))
+        return {0: "separate", 1: "fused", 2: "persistent"}[p.value]
 
     def weight_bytes(self) -> int:
         n = ctypes.c_size_t()

@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "step.cuh"
 #include "gemv_mma.cuh"
 #include "ops.cuh"
 
@@ -143,6 +144,8 @@ extern "C" int ib_check_fault(int* code) {
     if ((st = decode_fault_take(&c2)) != IB_OK) return st;
     if (!*code) *code = c2;
     if ((st = gemm_fault_take(&c2)) != IB_OK) return st;
+    if (!*code) *code = c2;
+    if ((st = step_fault_take(&c2)) != IB_OK) return st;
     if (!*code) *code = c2;
     if (*code) {
         set_error("CUDA: a pipeline wait expired in a GEMV kernel (code " + std::to_string(*code) +

@@ -492,6 +492,7 @@ extern "C" int ib_model_finalize(void* h) {
         x.stride = c.dim;
     }
     m->fused_ok = fused_supported(m);
+    if ((st = build_step_plan(m))) return st;
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
     IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
     m->finalized = true;
@@ -613,6 +614,169 @@ bool fused_supported(const Model* m) {
     return true;
 }
 
+// The second format of each fused pair (Q6_K, Q8_0, Q5_1): its rows use ring slot B.
+static bool pair_member_b(int type) {
+    return type == IB_TYPE_Q6_K || type == IB_TYPE_Q8_0 || type == IB_TYPE_Q5_1;
+}
+
+// ---- persistent decode step: the task plan ------------------------------------------
+// Slab instances (inputs of the step's GEMVs, each with its readiness counters):
+//   0               embedding -> layer 0's QKV
+//   1 + 4l + 0      attention of layer l -> wo
+//   1 + 4l + 1      x after wo -> gate+up (ffn_norm)
+//   1 + 4l + 2      SwiGLU product -> down
+//   1 + 4l + 3      x after down -> layer l+1's QKV (attn_norm) or the head (output_norm)
+int build_step_plan(Model* m) {
+    m->persistent_ok = false;
+    const auto& c = m->cfg;
+    if (m->tp_size > 1 || !m->fused_ok || c.n_layers < 1 || m->tok.repr != REPR_PACKED) return IB_OK;
+    const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn;
+    const bool kq = m->slab_kq;
+    const int GS = kq ? 256 : 32, SE = kq ? 2048 : 1024, BE = kq ? 256 : 32;
+    const int G = H / Hkv;
+    if ((HD != 32 && HD != 64 && HD != 128) || G > 8 || G * HD > 1024 || (G * HD) % GS ||
+        D % GS || F % GS || (H * HD) % GS || D % block_elems(m->tok.type))
+        return IB_OK;
+    const int kmax = std::max(std::max(D, F), H * HD);
+    const int max_slices = (kmax + SE - 1) / SE, max_groups = kmax / GS;
+    const int n_inst = 1 + 4 * c.n_layers;
+    const int type_a = m->layers[0].wq.type;
+    bool pad[2] = {false, false};
+    std::vector<StepPhase> ph;
+    int t = 0;
+    auto add = [&](StepPhase p) {
+        p.first = t;
+        t += p.n;
+        ph.push_back(p);
+    };
+    auto gemv = [&](const FusedGemv& g, int pro, int epi, int in_inst) {
+        StepPhase p{};
+        p.kind = TK_GEMV;
+        p.g = g;
+        p.g.work = nullptr;
+        p.pro = pro;
+        p.epi = epi;
+        p.nb = g.K / BE;
+        p.spg = (g.K + SE - 1) / SE;
+        p.in_inst = in_inst;
+        p.out_inst = -1;
+        p.n = g.paired ? g.rows[0] / 8 : (g.rows[0] + g.rows[1] + g.rows[2] + 15) / 16;
+        for (int sgm = 0; sgm < g.n_seg; ++sgm) {
+            const int64_t rb = packed_bytes(g.type[sgm], 1, g.K);
+            if (((uintptr_t)g.W[sgm] & 15) || rb % 16) pad[pair_member_b(g.type[sgm]) ? 1 : 0] = true;
+        }
+        return p;
+    };
+    {
+        StepPhase e{};
+        e.kind = TK_EMBED;
+        e.n = D / GS;
+        e.x = m->x;
+        e.norm = m->layers[0].attn_norm;
+        e.ssq = m->ssq;
+        e.out_slab = m->slab_x;
+        e.out_inst = 0;
+        add(e);
+    }
+    int in_x = 0;  // instance of the next QKV's input
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer& L = m->layers[l];
+        const int base = 1 + 4 * l;
+        StepPhase q = gemv(fg_qkv(m, L), PRO_NORM, EPI_QKV, in_x);
+        q.layer = l;
+        add(q);
+        StepPhase a{};
+        a.kind = TK_ATTN;
+        a.n = Hkv * kStepAttMaxSplits;
+        a.layer = l;
+        a.q = m->q;
+        a.kc = L.kc;
+        a.vc = L.vc;
+        a.out_slab = m->slab_att;
+        a.out_inst = base;
+        add(a);
+        StepPhase wo = gemv(fg_wo(m, L), PRO_PLAIN, EPI_RESID, base);
+        wo.out_inst = base + 1;
+        wo.out_src = m->x;
+        wo.out_norm = L.ffn_norm;
+        wo.out_ssq = m->ssq;
+        wo.out_slab = m->slab_x;
+        wo.out_per_group = GS / 16;
+        add(wo);
+        StepPhase fi = gemv(fg_ffn_in(m, L), PRO_NORM, EPI_SWIGLU, base + 1);
+        fi.out_inst = base + 2;
+        fi.out_src = m->gate;
+        fi.out_slab = m->slab_h;
+        fi.out_per_group = GS / 8;
+        add(fi);
+        StepPhase dn = gemv(fg_ffn_out(m, L), PRO_PLAIN, EPI_RESID, base + 2);
+        dn.out_inst = base + 3;
+        dn.out_src = m->x;
+        dn.out_norm = l + 1 < c.n_layers ? m->layers[l + 1].attn_norm : m->out_norm;
+        dn.out_ssq = m->ssq;
+        dn.out_slab = m->slab_x;
+        dn.out_per_group = GS / 16;
+        add(dn);
+        in_x = base + 3;
+    }
+    add(gemv(fg_head(m), PRO_NORM, EPI_ARGMAX, in_x));
+    StepParams& P = m->step;
+    P = StepParams{};
+    P.HD = HD;
+    int grid = 0;
+    int r = step_geometry(type_a, pad[0], pad[1], G, HD, P, &grid);
+    if (r == IB_ERR_UNSUPPORTED) return IB_OK;  // the fused kernels stay in use
+    if (r) return r;
+    P.n_phases = (int)ph.size();
+    P.n_tasks = t;
+    P.max_slices = max_slices;
+    P.max_groups = max_groups;
+    P.max_kv = Hkv;
+    P.ready_off = 2;
+    P.grp_off = P.ready_off + n_inst * max_slices;
+    P.att_ready_off = P.grp_off + n_inst * max_groups;
+    P.att_done_off = P.att_ready_off + c.n_layers * Hkv;
+    m->step_ctr_bytes = step_counter_bytes(n_inst, max_slices, max_groups, c.n_layers, Hkv);
+    StepPhase* dph = nullptr;
+    IB_CUDA_CHECK(cudaMalloc(&dph, ph.size() * sizeof(StepPhase)));
+    m->allocations.push_back(dph);
+    IB_CUDA_CHECK(cudaMemcpyAsync(dph, ph.data(), ph.size() * sizeof(StepPhase),
+                                  cudaMemcpyHostToDevice, m->stream));
+    P.phases = dph;
+    IB_CUDA_CHECK(cudaMalloc(&P.ctr, m->step_ctr_bytes));
+    m->allocations.push_back(P.ctr);
+    IB_CUDA_CHECK(cudaMemsetAsync(P.ctr, 0, m->step_ctr_bytes, m->stream));
+    IB_CUDA_CHECK(cudaMalloc(&P.att_acc, (size_t)H * kStepAttMaxSplits * HD * 4 + 16));
+    m->allocations.push_back(P.att_acc);
+    IB_CUDA_CHECK(cudaMalloc(&P.att_ml, (size_t)H * kStepAttMaxSplits * 8 + 16));
+    m->allocations.push_back(P.att_ml);
+    P.dev_i32 = m->dev_i32;
+    P.tokens = m->dev_tokens;
+    P.best = m->best;
+    P.max_seq = c.max_seq;
+    P.emb = (const uint8_t*)m->tok.w;
+    P.emb_type = m->tok.type;
+    P.vocab = c.vocab;
+    P.dim = D;
+    P.H = H;
+    P.Hkv = Hkv;
+    P.scale = 1.0f / sqrtf((float)HD);
+    P.att_target = (G + 2) * HD / 16;
+    m->step_grid = grid;
+    m->step_type = type_a;
+    m->persistent_ok = true;
+    return IB_OK;
+}
+
+static int step_launches(Model* m) {
+    IB_CUDA_CHECK(cudaMemsetAsync(m->step.ctr, 0, m->step_ctr_bytes, m->stream));
+    return step_launch(m->step, m->step_type, m->step_grid, m->stream);
+}
+
+static bool persistent_active(const Model* m) {
+    return m->use_persistent && m->persistent_ok && m->use_fused && m->fused_ok;
+}
+
 static int embed_launch(Model* m) {
     const auto& c = m->cfg;
     const int* tok = m->dev_i32;
@@ -685,6 +849,7 @@ static int decode_launches_fused(Model* m) {
 // One decode step for the token in dev_i32[0] at position dev_i32[1]; the greedy
 // next token lands in dev_i32[2].  Every launch reads the position on the device.
 static int decode_launches(Model* m) {
+    if (persistent_active(m)) return step_launches(m);
     if (m->use_fused && m->fused_ok) return decode_launches_fused(m);
     const auto& c = m->cfg;
     const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
@@ -937,6 +1102,25 @@ extern "C" int ib_model_set_fused(void* h, int enabled) {
         cudaGraphExecDestroy(m->graph_exec);
         m->graph_exec = nullptr;
     }
+    return IB_OK;
+}
+
+extern "C" int ib_model_set_persistent(void* h, int enabled) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    m->use_persistent = enabled != 0;
+    if (m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    return IB_OK;
+}
+
+extern "C" int ib_model_decode_path(void* h, int* path) {
+    IB_REQUIRE(h && path, "null pointer argument");
+    Model* m = (Model*)h;
+    *path = persistent_active(m) ? IB_DECODE_PERSISTENT
+            : (m->use_fused && m->fused_ok) ? IB_DECODE_FUSED : IB_DECODE_SEPARATE;
     return IB_OK;
 }
 

@@ -7,6 +7,7 @@
 
 #include "../../include/ib_cuda.h"
 #include "decode.cuh"
+#include "step.cuh"
 
 namespace ib {
 
@@ -57,6 +58,12 @@ struct Model {
     bool use_graph = true;
     bool use_fused = true;  // fused decode kernels when every weight supports them
     bool fused_ok = false;
+    // persistent decode step (step.cu): one kernel per token, single GPU
+    bool use_persistent = false;
+    bool persistent_ok = false;
+    StepParams step{};
+    int step_grid = 0, step_type = 0;
+    size_t step_ctr_bytes = 0;
     Linear tok, out;
     float* out_norm = nullptr;
     std::vector<Layer> layers;
@@ -90,6 +97,8 @@ struct Model {
 int decode_step(Model* m, int token, int pos, float* host_logits, int* next);
 // True when every decode GEMV of the model has a fused kernel (decode.cu).
 bool fused_supported(const Model* m);
+// Plans the persistent decode step when the model supports it (sets persistent_ok).
+int build_step_plan(Model* m);
 int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_logits, int* next);
 
 }  // namespace ib

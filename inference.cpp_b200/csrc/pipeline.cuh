@@ -49,6 +49,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of the phase with the given parity (mbarrier.test_wait never
+// suspends the thread, unlike try_wait): for loops that poll several conditions.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity; false (and g_fault set) on expiry.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* fault, int code) {
     for (uint32_t i = 0; i < kWaitPolls; ++i) {

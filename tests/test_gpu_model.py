@@ -88,6 +88,7 @@ def test_fused_decode_matches_oracle(cuda, port, cfg):
     tensors = synth(cfg, 77)
     om = port.model(cfg, tensors)
     a = ib.Model.from_tensors(cfg, tensors)
+    a.set_persistent(False)  # the per-operation fused kernels (test_gpu_step.py: persistent)
     b = ib.Model.from_tensors(cfg, tensors)
     b.set_fused(False)
     assert not b.uses_fused()
