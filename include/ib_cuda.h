@@ -280,6 +280,8 @@ int ib_model_stream(void* model, void** stream);
 int ib_model_step_kernels(void* model, int* n_kernels);
 /* Bytes of weights held on the device. */
 int ib_model_weight_bytes(void* model, size_t* bytes);
+/* The model's configuration (the whole model's shapes under tensor parallelism). */
+int ib_model_get_config(void* model, ib_model_config* cfg);
 
 /* ---- tensor parallelism (no counterpart in the reference, which runs on one GPU) ----
  * One process per GPU.  Rank 0 creates an id (ib_comm_unique_id), every rank receives

@@ -4,7 +4,9 @@
 // written against that header compile unchanged; failures throw
 // std::runtime_error with the library's message, as the reference's check()
 // does (src/ops/cuda_backend.cpp:76-85).  The quantized entry points after the
-// reference's set are additions for weights kept in GGUF block form.
+// reference's set are additions for weights kept in GGUF block form.  The model
+// runner on packed weights is in ib_cuda_model.hpp (kept apart so that this header
+// can stand in for ops/cuda_backend.hpp next to the reference's models/cuda_model.hpp).
 #pragma once
 
 #include <cstddef>
@@ -77,41 +79,3 @@ void embedding_q(int type, const Buffer& table, const Buffer& ids, const Buffer&
                  int64_t vocab, int64_t dim);
 
 }  // namespace inference::cuda
-
-namespace inference {
-
-// Generation timing breakdown, as include/models/cuda_model.hpp:12-17.
-struct GenerationStats {
-    double init_ms = 0;
-    double prefill_ms = 0;
-    double decode_ms = 0;
-    int generated = 0;
-};
-
-// A model on the GPU loaded from a GGUF file with its weights kept in block form
-// (precision "native"), or converted to INT16 / FP32 on the GPU ("int16", "fp32",
-// the reference's --gpu-precision values).  Replaces the GpuState cache of
-// src/models/model_cuda.cpp:25-259 for callers that hold the GGUF path.
-class CudaModel {
-public:
-    CudaModel(const std::string& gguf_path, const std::string& precision = "native",
-              int device = 0, int max_seq = 0);
-    ~CudaModel();
-    CudaModel(const CudaModel&) = delete;
-    CudaModel& operator=(const CudaModel&) = delete;
-
-    // Greedy generation (temperature 0): prompt followed by up to max_tokens ids,
-    // stopping at eos_token_id (>= 0) or the end of the context (generate_cuda,
-    // src/models/model_cuda.cpp:442-495).
-    std::vector<int> generate(const std::vector<int>& prompt, int max_tokens,
-                              int eos_token_id = -1, GenerationStats* stats = nullptr);
-    size_t weight_bytes() const;
-    void* handle() const { return h_; }
-
-private:
-    void* h_ = nullptr;
-};
-
-bool cuda_model_available();
-
-}  // namespace inference

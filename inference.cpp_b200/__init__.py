@@ -462,6 +462,7 @@ SIGNATURES.update({
     "ib_model_set_fused": [_vp, _i],
     "ib_model_uses_fused": [_vp, _vp],
     "ib_model_set_persistent": [_vp, _i],
+    "ib_model_get_config": [_vp, _vp],
     "ib_model_decode_path": [_vp, _vp],
     "ib_model_weight_bytes": [_vp, _vp],
     "ib_model_decode_loop": [_vp, _c.c_int32, _i, _i, _vp],

@@ -6,6 +6,7 @@
 
 #include "../../include/ib_cuda.h"
 #include "../../include/ib_cuda_backend.hpp"
+#include "../../include/ib_cuda_model.hpp"
 
 namespace inference::cuda {
 
@@ -180,6 +181,10 @@ CudaModel::CudaModel(const std::string& path, const std::string& precision, int 
                      int max_seq) {
     if (ib_model_load_gguf(path.c_str(), precision_code(precision), device, max_seq, &h_) != IB_OK)
         throw std::runtime_error(ib_last_error());
+    ib_model_config cfg{};
+    if (ib_model_get_config(h_, &cfg) != IB_OK) throw std::runtime_error(ib_last_error());
+    vocab_ = cfg.vocab;
+    max_seq_ = cfg.max_seq;
 }
 
 CudaModel::~CudaModel() {
@@ -187,7 +192,7 @@ CudaModel::~CudaModel() {
 }
 
 std::vector<int> CudaModel::generate(const std::vector<int>& prompt, int max_tokens,
-                                     int eos_token_id, GenerationStats* stats) {
+                                     int eos_token_id, CudaModelStats* stats) {
     std::vector<int32_t> in(prompt.begin(), prompt.end());
     std::vector<int32_t> out(prompt.size() + (size_t)(max_tokens > 0 ? max_tokens : 0));
     int n = 0;
@@ -204,12 +209,28 @@ std::vector<int> CudaModel::generate(const std::vector<int>& prompt, int max_tok
     return std::vector<int>(out.begin(), out.begin() + n);
 }
 
+int CudaModel::prefill(const std::vector<int>& ids, float* logits) {
+    std::vector<int32_t> in(ids.begin(), ids.end());
+    int32_t next = 0;
+    if (ib_model_prefill(h_, in.data(), (int)in.size(), 0, logits, &next) != IB_OK)
+        throw std::runtime_error(ib_last_error());
+    return next;
+}
+
+int CudaModel::decode(int token, int pos, float* logits) {
+    int32_t next = 0;
+    if (ib_model_decode(h_, token, pos, logits, &next) != IB_OK)
+        throw std::runtime_error(ib_last_error());
+    return next;
+}
+
+int CudaModel::vocab() const { return vocab_; }
+int CudaModel::max_seq() const { return max_seq_; }
+
 size_t CudaModel::weight_bytes() const {
     size_t n = 0;
     if (ib_model_weight_bytes(h_, &n) != IB_OK) throw std::runtime_error(ib_last_error());
     return n;
 }
-
-bool cuda_model_available() { return cuda::available(); }
 
 }  // namespace inference

@@ -1280,6 +1280,12 @@ extern "C" int ib_model_load_gguf_tp(const char* path, int precision, int device
     return load_gguf(path, precision, device, max_seq, (Comm*)comm, out);
 }
 
+extern "C" int ib_model_get_config(void* h, ib_model_config* cfg) {
+    IB_REQUIRE(h && cfg, "null pointer argument");
+    *cfg = ((Model*)h)->full;
+    return IB_OK;
+}
+
 extern "C" int ib_model_weight_bytes(void* h, size_t* bytes) {
     IB_REQUIRE(h && bytes, "null pointer argument");
     Model* m = (Model*)h;

@@ -296,41 +296,61 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
         const bool got = mbar_wait(abar, a_ph, &g_step_fault, 31);
         a_ph ^= 1u;
         if (!got) return false;
-        // this warp's positions of the tile, one at a time: scores of every head, then an
-        // online-softmax update of the warp's running state
-        for (int i = 0; i < PPW; ++i) {
-            const int s = warp * PPW + i;
-            if (s >= nt) break;
-            float kr[J], vr[J];
+        // this warp's positions of the tile, two at a time: the scores of every head for
+        // both (their reductions interleaved), then one online-softmax update of the
+        // warp's running state per head
+        for (int i = 0; i < PPW; i += 2) {
+            const int s0 = warp * PPW + i, s1 = s0 + 1;
+            if (s0 >= nt) break;
+            const bool has1 = i + 1 < PPW && s1 < nt;
+            float k0[J], k1[J];
 #pragma unroll
             for (int j = 0; j < J; ++j) {
-                kr[j] = sK[s * HD + lane + 32 * j];
-                vr[j] = sV[s * HD + lane + 32 * j];
+                k0[j] = sK[s0 * HD + lane + 32 * j];
+                k1[j] = has1 ? sK[s1 * HD + lane + 32 * j] : 0.f;
             }
-            float sc[GM];
+            float d0[GM], d1[GM];
 #pragma unroll
             for (int g = 0; g < GM; ++g) {
-                float d = 0.f;
+                float a = 0.f, b = 0.f;
                 if (g < G) {
 #pragma unroll
-                    for (int j = 0; j < J; ++j) d = fmaf(sq[g * HD + lane + 32 * j], kr[j], d);
+                    for (int j = 0; j < J; ++j) {
+                        const float qv = sq[g * HD + lane + 32 * j];
+                        a = fmaf(qv, k0[j], a);
+                        b = fmaf(qv, k1[j], b);
+                    }
                 }
-                sc[g] = d;
+                d0[g] = a;
+                d1[g] = b;
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-                for (int g = 0; g < GM; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+                for (int g = 0; g < GM; ++g)
+                    if (g < G) {
+                        d0[g] += __shfl_xor_sync(0xffffffffu, d0[g], o);
+                        d1[g] += __shfl_xor_sync(0xffffffffu, d1[g], o);
+                    }
+            float v0[J], v1[J];
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                v0[j] = sV[s0 * HD + lane + 32 * j];
+                v1[j] = has1 ? sV[s1 * HD + lane + 32 * j] : 0.f;
+            }
 #pragma unroll
             for (int g = 0; g < GM; ++g) {
                 if (g < G) {
-                    const float x = sc[g] * P.scale;
-                    const float mn = fmaxf(m[g], x);
+                    const float x0 = d0[g] * P.scale;
+                    const float x1 = has1 ? d1[g] * P.scale : -INFINITY;
+                    const float mn = fmaxf(m[g], fmaxf(x0, x1));
                     const float al = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
-                    const float p = expf(x - mn);
-                    l[g] = fmaf(l[g], al, p);
+                    const float p0 = expf(x0 - mn);
+                    const float p1 = has1 ? expf(x1 - mn) : 0.f;
+                    l[g] = fmaf(l[g], al, p0 + p1);
 #pragma unroll
-                    for (int j = 0; j < J; ++j) acc[g][j] = fmaf(acc[g][j], al, p * vr[j]);
+                    for (int j = 0; j < J; ++j)
+                        acc[g][j] = fmaf(acc[g][j], al, fmaf(p0, v0[j], p1 * v1[j]));
                     m[g] = mn;
                 }
             }
@@ -403,21 +423,45 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
         if (lane == 0) linv[g] = 1.0f / L;
     }
     if (!cbar(cb, cb_ph, lane)) return false;
-    for (int idx = tid; idx < n_out; idx += kNWC * 32) {
-        const int g = idx / HD, e = idx - g * HD;
-        const float* src = P.att_acc + (size_t)(h * G + g) * kStepAttMaxSplits * HD + e;
+    // two threads per four consecutive outputs, each over half of the splits (8 loads in
+    // flight), combined with one shuffle; the loop runs on whole warps
+    for (int i0 = warp * 32; i0 < n_out / 2; i0 += kNWC * 32) {
+        const int i = i0 + lane;
+        const bool act = i < n_out / 2;
+        const int quad = act ? i >> 1 : 0, half = i & 1;
+        const int g = (quad * 4) / HD, e = quad * 4 - g * HD;
+        const float4* src = reinterpret_cast<const float4*>(
+            P.att_acc + (size_t)(h * G + g) * kStepAttMaxSplits * HD + e);
         const float* w = wsp + g * kStepAttMaxSplits;
-        float a = 0.f;
-        int ci = 0;
-        for (; ci + 8 <= live; ci += 8) {
-            float b[8];
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c0 = half; act && c0 < live; c0 += 16) {
+            float4 b[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) b[u] = __ldcg(src + (size_t)(ci + u) * HD);
+            for (int u = 0; u < 8; ++u) {
+                const int ci = c0 + 2 * u;
+                b[u] = ci < live ? __ldcg(src + (size_t)ci * (HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) a = fmaf(w[ci + u], b[u], a);
+            for (int u = 0; u < 8; ++u) {
+                const int ci = c0 + 2 * u;
+                const float wt = ci < live ? w[ci] : 0.f;
+                a.x = fmaf(wt, b[u].x, a.x);
+                a.y = fmaf(wt, b[u].y, a.y);
+                a.z = fmaf(wt, b[u].z, a.z);
+                a.w = fmaf(wt, b[u].w, a.w);
+            }
         }
-        for (; ci < live; ++ci) a = fmaf(w[ci], __ldcg(src + (size_t)ci * HD), a);
-        ov[idx] = a * linv[g];
+        a.x += __shfl_xor_sync(0xffffffffu, a.x, 1);
+        a.y += __shfl_xor_sync(0xffffffffu, a.y, 1);
+        a.z += __shfl_xor_sync(0xffffffffu, a.z, 1);
+        a.w += __shfl_xor_sync(0xffffffffu, a.w, 1);
+        if (act && half == 0) {
+            const float inv = linv[g];
+            ov[quad * 4 + 0] = a.x * inv;
+            ov[quad * 4 + 1] = a.y * inv;
+            ov[quad * 4 + 2] = a.z * inv;
+            ov[quad * 4 + 3] = a.w * inv;
+        }
     }
     if (!cbar(cb, cb_ph, lane)) return false;
     constexpr int GS = SlabG<KQ>::GS, PER = GS / 32;
