@@ -56,6 +56,12 @@ constexpr int kProducer = kNWC;      // warp index of the producer
 constexpr int kEpilogue = kNWC + 1;  // warp index of the epilogue warp
 constexpr int kStepThreads = (kNWC + 2) * 32;
 constexpr int kNQ = 4;               // partial-sum buffers between math and epilogue warps
+// CTAs per SM the kernel is built for (registers: 65536 / (CTAs * 320 threads)); the ring
+// gets as many stages as fit beside them.
+#ifndef IB_STEP_CTAS_PER_SM
+#define IB_STEP_CTAS_PER_SM 3
+#endif
+constexpr int kStepCtasPerSm = IB_STEP_CTAS_PER_SM;
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     int v;
@@ -245,15 +251,18 @@ __device__ void embed_task(const StepParams& P, const StepPhase& ph, int gi, flo
 }
 
 // Attention task (kv head h, split sp) on the eight math warps; scratch = the task's
-// ring slot.  J = head_dim / 32 (each lane holds dims lane + 32j); up to 8 query heads
-// per kv head.  Returns false on an expired wait.
+// ring slot.  J = head_dim / 32 (each lane holds dims lane + 32j).  Warp w serves query
+// head w % G of the kv head's group over part w / G of each tile's positions (8 / G
+// parts), with its own running online-softmax state; the warps' states are merged
+// once per split.  Returns false on an expired wait.
 template <bool KQ, int J>
 __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint8_t* slot,
                           uint64_t* cb, uint32_t& cb_ph, uint64_t* abar, uint32_t& a_ph,
                           int* s_flag, int pos, int warp, int lane) {
-    constexpr int GM = 8, HD = 32 * J;
+    constexpr int HD = 32 * J;
     const int tid = warp * 32 + lane;
-    const int Hkv = P.Hkv, G = P.H / Hkv, TILE = P.att_tile, PPW = TILE / kNWC;
+    const int Hkv = P.Hkv, G = P.H / Hkv, TILE = P.att_tile;
+    const int parts = kNWC / G, gw = warp % G, part = warp / G, ppp = TILE / parts;
     const int first = gph->first, layer = gph->layer;
     const int h = (t - first) % Hkv, sp = (t - first) / Hkv;
     const int n_pos = pos + 1;
@@ -268,21 +277,13 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
     const float* vh = gph->vc + (size_t)h * P.max_seq * HD;
     const float* qh = gph->q + (size_t)h * n_out;
     // the QKV row groups of this kv head's heads have finished
-    int ok = 1;
-    if (tid == 0) {
-        ok = wait_count(P.ctr + P.att_ready_off + layer * P.max_kv + h, P.att_target, 41);
-        *s_flag = ok;
-    }
+    if (tid == 0)
+        *s_flag = wait_count(P.ctr + P.att_ready_off + layer * P.max_kv + h, P.att_target, 41);
     if (!cbar(cb, cb_ph, lane)) return false;
     if (!*s_flag) return false;
-    float m[GM], l[GM], acc[GM][J];
+    float m = -INFINITY, l = 0.f, acc[J], qr[J];
 #pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int j = 0; j < J; ++j) acc[g][j] = 0.f;
-    }
+    for (int j = 0; j < J; ++j) acc[j] = 0.f;
     for (int t0 = p0; t0 < p1; t0 += TILE) {
         const int nt = min(TILE, p1 - t0);
         if (tid == 0) {
@@ -296,92 +297,59 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
         const bool got = mbar_wait(abar, a_ph, &g_step_fault, 31);
         a_ph ^= 1u;
         if (!got) return false;
-        // this warp's positions of the tile, two at a time: the scores of every head for
-        // both (their reductions interleaved), then one online-softmax update of the
-        // warp's running state per head
-        for (int i = 0; i < PPW; i += 2) {
-            const int s0 = warp * PPW + i, s1 = s0 + 1;
-            if (s0 >= nt) break;
-            const bool has1 = i + 1 < PPW && s1 < nt;
-            float k0[J], k1[J];
+        if (t0 == p0) {
+#pragma unroll
+            for (int j = 0; j < J; ++j) qr[j] = sq[gw * HD + lane + 32 * j] * P.scale;
+        }
+        // this warp's positions of the tile, two at a time (their reductions interleaved),
+        // one online-softmax update per pair
+        const int s_end = min(nt, (part + 1) * ppp);
+        for (int s0 = part * ppp; s0 < s_end; s0 += 2) {
+            const int s1 = s0 + 1;
+            const bool has1 = s1 < s_end;
+            float a = 0.f, b = 0.f, v0[J], v1[J];
 #pragma unroll
             for (int j = 0; j < J; ++j) {
-                k0[j] = sK[s0 * HD + lane + 32 * j];
-                k1[j] = has1 ? sK[s1 * HD + lane + 32 * j] : 0.f;
-            }
-            float d0[GM], d1[GM];
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-                float a = 0.f, b = 0.f;
-                if (g < G) {
-#pragma unroll
-                    for (int j = 0; j < J; ++j) {
-                        const float qv = sq[g * HD + lane + 32 * j];
-                        a = fmaf(qv, k0[j], a);
-                        b = fmaf(qv, k1[j], b);
-                    }
-                }
-                d0[g] = a;
-                d1[g] = b;
+                const int e = lane + 32 * j;
+                a = fmaf(qr[j], sK[s0 * HD + e], a);
+                b = has1 ? fmaf(qr[j], sK[s1 * HD + e], b) : b;
+                v0[j] = sV[s0 * HD + e];
+                v1[j] = has1 ? sV[s1 * HD + e] : 0.f;
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int g = 0; g < GM; ++g)
-                    if (g < G) {
-                        d0[g] += __shfl_xor_sync(0xffffffffu, d0[g], o);
-                        d1[g] += __shfl_xor_sync(0xffffffffu, d1[g], o);
-                    }
-            float v0[J], v1[J];
-#pragma unroll
-            for (int j = 0; j < J; ++j) {
-                v0[j] = sV[s0 * HD + lane + 32 * j];
-                v1[j] = has1 ? sV[s1 * HD + lane + 32 * j] : 0.f;
+            for (int o = 16; o > 0; o >>= 1) {
+                a += __shfl_xor_sync(0xffffffffu, a, o);
+                b += __shfl_xor_sync(0xffffffffu, b, o);
             }
+            if (!has1) b = -INFINITY;
+            const float mn = fmaxf(m, fmaxf(a, b));
+            const float al = m == -INFINITY ? 0.f : expf(m - mn);
+            const float e0 = expf(a - mn), e1 = has1 ? expf(b - mn) : 0.f;
+            l = fmaf(l, al, e0 + e1);
 #pragma unroll
-            for (int g = 0; g < GM; ++g) {
-                if (g < G) {
-                    const float x0 = d0[g] * P.scale;
-                    const float x1 = has1 ? d1[g] * P.scale : -INFINITY;
-                    const float mn = fmaxf(m[g], fmaxf(x0, x1));
-                    const float al = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
-                    const float p0 = expf(x0 - mn);
-                    const float p1 = has1 ? expf(x1 - mn) : 0.f;
-                    l[g] = fmaf(l[g], al, p0 + p1);
-#pragma unroll
-                    for (int j = 0; j < J; ++j)
-                        acc[g][j] = fmaf(acc[g][j], al, fmaf(p0, v0[j], p1 * v1[j]));
-                    m[g] = mn;
-                }
-            }
+            for (int j = 0; j < J; ++j) acc[j] = fmaf(acc[j], al, fmaf(e0, v0[j], e1 * v1[j]));
+            m = mn;
         }
         if (!cbar(cb, cb_ph, lane)) return false;  // the tile buffer is free again
     }
-    // merge the warps' states: per warp (m, l) and its accumulators, then one partial
+    // merge the warps' states: per warp (m, l) and its accumulator, then one partial
     // (max M, sum L, unnormalised accumulator) per query head of this split
-    float* sacc = reinterpret_cast<float*>(slot);      // [kNWC][G][HD]
-    float2* sml = reinterpret_cast<float2*>(sacc + kNWC * n_out);  // [kNWC][G]
+    float* sacc = reinterpret_cast<float*>(slot);                 // [kNWC][HD]
+    float2* sml = reinterpret_cast<float2*>(sacc + kNWC * HD);  // [kNWC]
 #pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        if (g < G) {
-#pragma unroll
-            for (int j = 0; j < J; ++j) sacc[(warp * G + g) * HD + lane + 32 * j] = acc[g][j];
-            if (lane == 0) sml[warp * G + g] = make_float2(m[g], l[g]);
-        }
-    }
+    for (int j = 0; j < J; ++j) sacc[warp * HD + lane + 32 * j] = acc[j];
+    if (lane == 0) sml[warp] = make_float2(m, l);
     if (!cbar(cb, cb_ph, lane)) return false;
     for (int idx = tid; idx < n_out; idx += kNWC * 32) {
         const int g = idx / HD, e = idx - g * HD;
         float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kNWC; ++w) M = fmaxf(M, sml[w * G + g].x);
+        for (int w = g; w < kNWC; w += G) M = fmaxf(M, sml[w].x);
         float L = 0.f, a = 0.f;
-#pragma unroll
-        for (int w = 0; w < kNWC; ++w) {
-            const float2 v = sml[w * G + g];
+        for (int w = g; w < kNWC; w += G) {
+            const float2 v = sml[w];
             const float wt = v.x == -INFINITY ? 0.f : expf(v.x - M);
             L = fmaf(wt, v.y, L);
-            a = fmaf(wt, sacc[(w * G + g) * HD + e], a);
+            a = fmaf(wt, sacc[w * HD + e], a);
         }
         P.att_acc[((size_t)(h * G + g) * kStepAttMaxSplits + sp) * HD + e] = a;
         if (e == 0) P.att_ml[(size_t)(h * G + g) * kStepAttMaxSplits + sp] = make_float2(M, L);
@@ -395,7 +363,7 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
     // the last split combines: weights per split, then the outputs, then the limb groups
     float* wsp = reinterpret_cast<float*>(slot);  // [G][kStepAttMaxSplits]
     float* linv = wsp + G * kStepAttMaxSplits;    // [G]
-    float* ov = linv + GM;                        // [G * HD]
+    float* ov = linv + 8;                         // [G * HD]
     for (int g = warp; g < G; g += kNWC) {
         const float2* ml = P.att_ml + (size_t)(h * G + g) * kStepAttMaxSplits;
         float m4[4], l4[4];
@@ -423,27 +391,27 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
         if (lane == 0) linv[g] = 1.0f / L;
     }
     if (!cbar(cb, cb_ph, lane)) return false;
-    // two threads per four consecutive outputs, each over half of the splits (8 loads in
-    // flight), combined with one shuffle; the loop runs on whole warps
-    for (int i0 = warp * 32; i0 < n_out / 2; i0 += kNWC * 32) {
+    // four threads per four consecutive outputs, each over a quarter of the splits (8
+    // loads in flight), combined with two shuffles; the loop runs on whole warps
+    for (int i0 = warp * 32; i0 < n_out; i0 += kNWC * 32) {
         const int i = i0 + lane;
-        const bool act = i < n_out / 2;
-        const int quad = act ? i >> 1 : 0, half = i & 1;
+        const bool act = i < n_out;
+        const int quad = act ? i >> 2 : 0, qtr = i & 3;
         const int g = (quad * 4) / HD, e = quad * 4 - g * HD;
         const float4* src = reinterpret_cast<const float4*>(
             P.att_acc + (size_t)(h * G + g) * kStepAttMaxSplits * HD + e);
         const float* w = wsp + g * kStepAttMaxSplits;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c0 = half; act && c0 < live; c0 += 16) {
+        for (int c0 = qtr; act && c0 < live; c0 += 32) {
             float4 b[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const int ci = c0 + 2 * u;
+                const int ci = c0 + 4 * u;
                 b[u] = ci < live ? __ldcg(src + (size_t)ci * (HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const int ci = c0 + 2 * u;
+                const int ci = c0 + 4 * u;
                 const float wt = ci < live ? w[ci] : 0.f;
                 a.x = fmaf(wt, b[u].x, a.x);
                 a.y = fmaf(wt, b[u].y, a.y);
@@ -451,11 +419,14 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
                 a.w = fmaf(wt, b[u].w, a.w);
             }
         }
-        a.x += __shfl_xor_sync(0xffffffffu, a.x, 1);
-        a.y += __shfl_xor_sync(0xffffffffu, a.y, 1);
-        a.z += __shfl_xor_sync(0xffffffffu, a.z, 1);
-        a.w += __shfl_xor_sync(0xffffffffu, a.w, 1);
-        if (act && half == 0) {
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            a.x += __shfl_xor_sync(0xffffffffu, a.x, o);
+            a.y += __shfl_xor_sync(0xffffffffu, a.y, o);
+            a.z += __shfl_xor_sync(0xffffffffu, a.z, o);
+            a.w += __shfl_xor_sync(0xffffffffu, a.w, o);
+        }
+        if (act && qtr == 0) {
             const float inv = linv[g];
             ov[quad * 4 + 0] = a.x * inv;
             ov[quad * 4 + 1] = a.y * inv;
@@ -496,7 +467,7 @@ __device__ __forceinline__ void task_epilogue(const StepPhase& ph, int rg, int l
 }
 
 template <int TA, int TB, int J>
-__global__ void __launch_bounds__(kStepThreads, 2) decode_step_kernel(const StepParams P) {
+__global__ void __launch_bounds__(kStepThreads, kStepCtasPerSm) decode_step_kernel(const StepParams P) {
     using PR = Pair<TA, TB>;
     constexpr bool KQ = PR::KQ;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -874,7 +845,7 @@ size_t step_counter_bytes(int n_inst, int max_slices, int max_groups, int n_laye
 // the combine's weights and outputs).
 static size_t attention_smem(int G, int HD, int tile) {
     const size_t a = (size_t)2 * tile * HD * 4 + (size_t)G * HD * 4;
-    const size_t b = (size_t)kNWC * G * HD * 4 + (size_t)kNWC * G * 8;
+    const size_t b = (size_t)kNWC * HD * 4 + (size_t)kNWC * 8;
     const size_t c = (size_t)G * kStepAttMaxSplits * 4 + 8 * 4 + (size_t)G * HD * 4;
     return a > b ? (a > c ? a : c) : (b > c ? b : c);
 }
@@ -897,14 +868,15 @@ static int geometry_inst(StepParams& p, int* grid) {
     IB_CUDA_CHECK(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     cudaFuncAttributes fa;
     IB_CUDA_CHECK(cudaFuncGetAttributes(&fa, kern));
-    // two CTAs per SM with as many stages as fit (at most kStepMaxStages), else one
+    // kStepCtasPerSm CTAs per SM with as many stages as fit (at most kStepMaxStages),
+    // else two stages at whatever fits
     int S = kStepMaxStages;
     for (; S >= 2; --S) {
         const size_t smem = (size_t)S * p.stage_bytes;
         if (smem + fa.sharedSizeBytes > (size_t)max_optin) continue;
         IB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStepThreads, smem));
-        if (per_sm >= 2) break;
+        if (per_sm >= kStepCtasPerSm) break;
     }
     if (S < 2) {
         S = 2;
@@ -960,8 +932,8 @@ static int pair_index(int type) {
 }
 
 int step_geometry(int type_a, bool pad_a, bool pad_b, int G, int HD, StepParams& p, int* grid) {
-    if (G < 1 || G > 8 || G * HD > 1024) {
-        set_error("decode step: at most 8 query heads per kv head and 1024 outputs per kv head");
+    if (G < 1 || G > 8 || 8 % G || G * HD > 1024) {
+        set_error("decode step: 1, 2, 4 or 8 query heads per kv head");
         return IB_ERR_UNSUPPORTED;
     }
     switch (pair_index(type_a)) {

@@ -28,7 +28,7 @@ enum { TK_EMBED = 0, TK_GEMV = 1, TK_ATTN = 2 };
 
 constexpr int kStepMaxStages = 4;
 constexpr int kStepAttMaxSplits = 128;  // attention split slots per kv head
-constexpr int kStepAttMinSplit = 64;    // positions per split at least
+constexpr int kStepAttMinSplit = 32;    // positions per split at least
 
 // One phase: a run of consecutive tasks of one kind.
 struct StepPhase {
