@@ -44,6 +44,7 @@ SHAPE_NAMES = {"llama-3-8b": "Llama-3-8B", "llama-3-70b": "Llama-3-70B",
                "tinyllama-1.1b": "TinyLlama-1.1B", "stories15M": "stories15M",
                "llama-3-8b-4l": "Llama-3-8B (4-layer)"}
 QUANT_NAMES = {"stories15M": "Q4_0"}
+QNAME = {2: "Q4_0", 6: "Q5_0", 7: "Q5_1", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
 
 
 def metric_for(cfg) -> str:
@@ -194,28 +195,30 @@ def build_model(ib, cfg, prompt_len, steps, warmup, device, seed=20261201, comm=
 
 
 def time_gemv(ib, cfg, seed=20261201):
-    """The decode GEMV kernel on the ffn_gate shape (Q4_K), over min(n_layers, 32) distinct
-    weight matrices (larger than L2 together), its limb slab computed once: CUDA-graph
+    """The decode GEMV kernel on the ffn_gate shape in the workload's linear format, over
+    min(n_layers, 32) distinct weight matrices (larger than L2 together for the 1B-and-up
+    shapes), its limb slab computed once: CUDA-graph
     replays of the kernel alone, timed with events on the replay stream.  Returns the
     per-launch time as a chain with programmatic dependent launch (how the decode step
     runs it: each launch streams its weights while the previous one finishes) and as
     standalone launches."""
     import torch
     from inference_cpp_b200 import gguf_writer as gw
+    t = cfg.linear_type
     rows, cols = cfg.ffn, cfg.dim
     n = min(cfg.n_layers, 32)
-    Ws = [ib.synth_device(ib.Q4_K, rows, cols, gw.tensor_seed(seed + 1, f"w{i}"), 0.02) for i in range(n)]
+    Ws = [ib.synth_device(t, rows, cols, gw.tensor_seed(seed + 1, f"w{i}"), 0.02) for i in range(n)]
     x = torch.randn(cols, device="cuda")
     y = torch.empty(rows, device="cuda")
-    slab = ib.limb_slab(ib.Q4_K, x, cols)
+    slab = ib.limb_slab(t, x, cols)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         for i in range(2 * n):
-            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
+            ib.gemv_q_slab(t, Ws[i % n], slab, rows, cols, y=y)
         torch.cuda.nvtx.range_push("gemv_roofline")  # a profiler's capture of this kernel
         for i in range(n):
-            ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y)
+            ib.gemv_q_slab(t, Ws[i % n], slab, rows, cols, y=y)
         torch.cuda.nvtx.range_pop()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
@@ -225,7 +228,7 @@ def time_gemv(ib, cfg, seed=20261201):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for i in range(reps):
-                ib.gemv_q_slab(ib.Q4_K, Ws[i % n], slab, rows, cols, y=y, chained=chained)
+                ib.gemv_q_slab(t, Ws[i % n], slab, rows, cols, y=y, chained=chained)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(s):  # the replay and its events on one stream
             g.replay()
@@ -236,7 +239,7 @@ def time_gemv(ib, cfg, seed=20261201):
         torch.cuda.synchronize()
         out[chained] = e0.elapsed_time(e1) / reps
         del g
-    nbytes = ib.packed_nbytes(ib.Q4_K, rows, cols) + 4 * cols + 4 * rows
+    nbytes = ib.packed_nbytes(t, rows, cols) + 4 * cols + 4 * rows
     del Ws
     torch.cuda.empty_cache()
     return nbytes, out[True], out[False], reps
@@ -244,27 +247,28 @@ def time_gemv(ib, cfg, seed=20261201):
 
 def time_gemm(ib, cfg, T, seed=20261201):
     """The prefill GEMM (tcgen05) on the ffn_gate shape: Y[T, ffn] = X[T, dim] . W^T with
-    Q4_K weights, timed with events on its stream over 3 launches after one warm-up; one
+    the workload's linear format, timed with events on its stream over 3 launches after one warm-up; one
     more launch sits in an NVTX range named gemm_roofline (for a profiler)."""
     import torch
     from inference_cpp_b200 import gguf_writer as gw
+    t = cfg.linear_type
     rows, cols = cfg.ffn, cfg.dim
-    W = ib.synth_device(ib.Q4_K, rows, cols, gw.tensor_seed(seed + 2, "gemm"), 0.02)
+    W = ib.synth_device(t, rows, cols, gw.tensor_seed(seed + 2, "gemm"), 0.02)
     X = torch.randn(T * cols, device="cuda")
     Y = torch.empty(T * rows, device="cuda")
     s = torch.cuda.current_stream()
-    ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+    ib.gemm_q(t, W, X, T, rows, cols, Y=Y)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 3
     e0.record(s)
     for _ in range(reps):
-        ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+        ib.gemm_q(t, W, X, T, rows, cols, Y=Y)
     e1.record(s)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     torch.cuda.nvtx.range_push("gemm_roofline")
-    ib.gemm_q(ib.Q4_K, W, X, T, rows, cols, Y=Y)
+    ib.gemm_q(t, W, X, T, rows, cols, Y=Y)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     del W, X, Y
@@ -643,8 +647,8 @@ def main():
             "e2e": {"value": seqs * e2e_steps / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic_from_profile(cfg.ffn, cfg.dim),
-                         "kernel": f"gemv_q Q4_K {cfg.ffn}x{cfg.dim}",
+                         "frac": achieved / peak, "traffic": traffic_from_profile(cfg.ffn, cfg.dim) if cfg.linear_type == 12 else None,
+                         "kernel": f"gemv_q {QNAME[cfg.linear_type]} {cfg.ffn}x{cfg.dim}",
                          "bytes_per_launch": nbytes, "avg_launch_us": gemv_ms * 1e3,
                          "timing": "back-to-back launches chained by programmatic dependent "
                                    "launch, as in the decode step",
@@ -658,7 +662,7 @@ def main():
                         "runs_ms": [round(r, 3) for r in prefill_runs],
                         "timing": "median of 3 after a full-length warm-up",
                         "tok_s": args.prompt / (prefill_ms * 1e-3),
-                        "gemm": {"kernel": f"gemm_tc Q4_K {cfg.ffn}x{cfg.dim}, T={args.prompt}",
+                        "gemm": {"kernel": f"gemm_tc {QNAME[cfg.linear_type]} {cfg.ffn}x{cfg.dim}, T={args.prompt}",
                                  "ms": gemm_ms, "tflops": gemm_flops / (gemm_ms * 1e-3) / 1e12,
                                  "peak": tpeak, "peak_kind": tpeak_kind,
                                  "frac": gemm_flops / (gemm_ms * 1e-3) / 1e12 / tpeak,
