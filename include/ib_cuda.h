@@ -139,9 +139,16 @@ int ib_gemv_q_slab_chained(int type, const void* dev_W, const void* dev_slab, fl
  * src/ops/cuda_kernels.cu:279-346). */
 int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float* dev_Y, int64_t T,
               int64_t rows, int64_t cols, void* stream);
-/* Which kernel ib_gemm_q runs (process-wide): 0 = tcgen05 tensor cores with FP32
- * accumulation in tensor memory, operands as FP16 hi/lo pairs (default; used when
- * cols % 64 == 0, else 1); 1 = CUDA-core FP32 tiles.  No counterpart in the reference. */
+/* Which kernel ib_gemm_q runs (process-wide).  Both tensor-core kernels use tcgen05 with
+ * FP32 accumulation in tensor memory and operands as FP16 hi/lo pairs:
+ *   0  automatic (default): for T >= 128 the packed weights are decoded once into FP16
+ *      planes and a TMA-fed kernel (128 x 256 tiles) multiplies them; shorter prompts
+ *      decode each weight tile inside the kernel (128 x 128 tiles); shapes neither takes
+ *      (cols % 64 != 0) run on CUDA cores
+ *   1  CUDA-core FP32 tiles
+ *   2  the in-kernel-decode tensor-core kernel where it applies
+ *   3  the planes kernel where it applies
+ * No counterpart in the reference. */
 int ib_gemm_set_path(int path);
 
 /* Embedding gather with dequantisation: out[t, :] = dequant(table[ids[t], :]).

@@ -278,12 +278,13 @@ def gemm_q(type_: int, W, X, T: int, rows: int, cols: int, Y=None, stream=None):
     return Y
 
 
-GEMM_TENSOR_CORES, GEMM_CUDA_CORES = 0, 1
+GEMM_TENSOR_CORES, GEMM_CUDA_CORES, GEMM_TC_STAGED, GEMM_TC_PLANES = 0, 1, 2, 3
 
 
 def gemm_set_path(path: int) -> None:
-    """Kernel behind gemm_q (process-wide): GEMM_TENSOR_CORES (tcgen05, default) or
-    GEMM_CUDA_CORES."""
+    """Kernel behind gemm_q (process-wide): GEMM_TENSOR_CORES (tcgen05, automatic choice;
+    default), GEMM_CUDA_CORES, or one tcgen05 kernel: GEMM_TC_STAGED (weights decoded per
+    tile in the kernel) or GEMM_TC_PLANES (weights decoded once into FP16 planes, TMA)."""
     call("ib_gemm_set_path", path)
 
 

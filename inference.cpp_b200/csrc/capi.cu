@@ -145,6 +145,8 @@ extern "C" int ib_check_fault(int* code) {
     if (!*code) *code = c2;
     if ((st = gemm_fault_take(&c2)) != IB_OK) return st;
     if (!*code) *code = c2;
+    if ((st = gemm_planes_fault_take(&c2)) != IB_OK) return st;
+    if (!*code) *code = c2;
     if ((st = step_fault_take(&c2)) != IB_OK) return st;
     if (!*code) *code = c2;
     if (*code) {

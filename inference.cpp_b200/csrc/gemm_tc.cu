@@ -432,6 +432,13 @@ __global__ void split_x_kernel(const float* __restrict__ X, __half* __restrict__
     }
 }
 
+int gemm_split_x(const float* X, void* Xh, void* Xl, size_t n, cudaStream_t st) {
+    const int g = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    split_x_kernel<<<g, 256, 0, st>>>(X, (__half*)Xh, (__half*)Xl, n);
+    IB_LAUNCH_CHECK("split_x_kernel");
+    return IB_OK;
+}
+
 template <int TYPE>
 static int launch_tc(const void* W, const float* X, float* Y, int T, int rows, int cols,
                      cudaStream_t st) {
@@ -441,9 +448,7 @@ static int launch_tc(const void* W, const float* X, float* Y, int T, int rows, i
     if (r) return r;
     __half* Xh = (__half*)ws;
     __half* Xl = Xh + n;
-    const int g = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-    split_x_kernel<<<g, 256, 0, st>>>(X, Xh, Xl, n);
-    IB_LAUNCH_CHECK("split_x_kernel");
+    if ((r = gemm_split_x(X, Xh, Xl, n, st))) return r;
     auto kern = gemm_tc_kernel<TYPE>;
     static bool attr_set[64] = {};
     int dev = 0;

@@ -622,7 +622,9 @@ extern "C" int ib_gemm_i16(const int16_t* W, const float* row_scale, const float
 static int g_gemm_path = 0;
 
 extern "C" int ib_gemm_set_path(int path) {
-    IB_REQUIRE(path == 0 || path == 1, "gemm path must be 0 (tensor cores) or 1 (CUDA cores)");
+    IB_REQUIRE(path >= 0 && path <= 3,
+               "gemm path must be 0 (tensor cores, automatic), 1 (CUDA cores), 2 (tensor cores, "
+               "staged blocks) or 3 (tensor cores, dequantised planes)");
     g_gemm_path = path;
     return IB_OK;
 }
@@ -637,7 +639,16 @@ extern "C" int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float*
         return IB_ERR_UNSUPPORTED;
     }
     IB_REQUIRE(cols % block_elems(type) == 0, "cols must be a multiple of the block size");
-    if (gemm_tc_supported(type, T, rows, cols) && g_gemm_path == 0)
-        return gemm_q_tc(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, as_stream(stream));
-    return gemm_q_simt(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, as_stream(stream));
+    cudaStream_t st = as_stream(stream);
+    const bool planes = gemm_planes_supported(type, T, rows, cols);
+    const bool staged = gemm_tc_supported(type, T, rows, cols);
+    // automatic: prompts of kPlanesMinT tokens and more decode the weights once into FP16
+    // planes (their decode is then shared by every token tile); shorter ones decode each
+    // tile in the kernel
+    constexpr int64_t kPlanesMinT = 128;
+    if (planes && (g_gemm_path == 3 || (g_gemm_path == 0 && (T >= kPlanesMinT || !staged))))
+        return gemm_q_planes(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, st);
+    if (staged && (g_gemm_path == 0 || g_gemm_path == 2))
+        return gemm_q_tc(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, st);
+    return gemm_q_simt(type, dev_W, dev_X, dev_Y, (int)T, (int)rows, (int)cols, st);
 }

@@ -6,7 +6,7 @@
 
 namespace ib {
 
-enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_GEMM = 2, WS_SLOTS = 3 };
+enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_GEMM = 2, WS_GEMM_W = 3, WS_SLOTS = 4 };
 int workspace_get(int slot, size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
 // Decode attention in one launch (split flash-decode, last-CTA combine); also writes
@@ -43,6 +43,13 @@ int argmax_launch(const float* x, int n, int32_t* out, cudaStream_t st);
 int elementwise_launch(int op, float* a, const float* b, int n, cudaStream_t st);
 // Prefill GEMM on the tensor cores (gemm_tc.cu): packed weights, cols % 64 == 0.
 bool gemm_tc_supported(int type, int64_t T, int64_t rows, int64_t cols);
+// X (FP32, n values) -> FP16 hi/lo planes (gemm_tc.cu).
+int gemm_split_x(const float* X, void* Xh, void* Xl, size_t n, cudaStream_t st);
+// The tcgen05 GEMM on dequantised FP16 planes fed by TMA (gemm_tma.cu).
+bool gemm_planes_supported(int type, int64_t T, int64_t rows, int64_t cols);
+int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
+                  cudaStream_t st);
+int gemm_planes_fault_take(int* code);
 int gemm_q_tc(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
               cudaStream_t st);
 int gemm_fault_take(int* code);

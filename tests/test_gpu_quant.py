@@ -130,14 +130,15 @@ def test_gemm_q_vs_oracle(cuda, port, type_):
 
 
 @pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
-@pytest.mark.parametrize("path", [ib.GEMM_TENSOR_CORES, ib.GEMM_CUDA_CORES], ids=["tcgen05", "simt"])
+@pytest.mark.parametrize("path", [ib.GEMM_TENSOR_CORES, ib.GEMM_CUDA_CORES, ib.GEMM_TC_STAGED,
+                                  ib.GEMM_TC_PLANES], ids=["auto", "simt", "tc-staged", "tc-planes"])
 def test_gemm_q_paths_vs_oracle(cuda, port, type_, path):
     """Both prefill GEMM kernels against the oracle's FP32 dequantisation: tiles with
     ragged edges in rows and tokens, K running through every pipeline stage many times."""
     rng = np.random.default_rng(700 + type_)
     try:
         ib.gemm_set_path(path)
-        for T, rows, cols in [(257, 300, 2048), (128, 128, 4096), (17, 513, 1536)]:
+        for T, rows, cols in [(257, 300, 2048), (128, 128, 4096), (17, 513, 1536), (600, 130, 768)]:
             blk = ib.synth_host(type_, rows, cols, seed=7000 + T + rows + type_)
             X = rng.standard_normal((T, cols)).astype(np.float32)
             W = port.dequantize(type_, blk, rows * cols).reshape(rows, cols)
