@@ -62,7 +62,8 @@ def test_new_entry_points_validate_without_gpu():
     """Entry points added beside the reference's interface reject bad arguments before
     any device or NCCL call."""
     L = ib.lib()
-    assert L.ib_gemm_set_path(2) == 1                      # only 0 and 1
+    assert L.ib_gemm_set_path(4) == 1                      # only 0 to 3
+    assert L.ib_gemm_set_path(-1) == 1
     assert L.ib_gemm_set_path(0) == 0
     cfg = ib.ModelConfig(1, 256, 4, 2, 512, 300, 64, 10000.0, 1e-5, 0)
     h = ctypes.c_void_p()
