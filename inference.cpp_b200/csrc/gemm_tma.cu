@@ -6,9 +6,10 @@
 // planes W = Wh + Wl (hi = fp16(w), lo = fp16(w - hi); the bit-exact element
 // expressions of quant.cuh), next to X's planes (split_x_kernel), and a pure tensor-core
 // GEMM consumes them:
-//   producer warp   one thread issues, per 64-column step, four 2-D TMA tile loads
-//                   (cp.async.bulk.tensor, 128-byte swizzle, no multicast): Wh, Wl
-//                   (128 rows) and Xh, Xl (256 tokens), completing on the stage's
+//   producer warp   one thread issues, per 32-column step, four 2-D TMA tile loads
+//                   (cp.async.bulk.tensor, 64-byte swizzle, no multicast) into a
+//                   four-stage ring: Wh, Wl (128 rows) and Xh, Xl (256 tokens),
+//                   completing on the stage's
 //                   mbarrier; rows and tokens past the edges are filled with zeros
 //   MMA warp        one thread issues per 16-column slice tcgen05.mma kind::f16
 //                   M 128 x N 256 for Wh.Xh + Wh.Xl + Wl.Xh into an FP32 accumulator of
@@ -38,10 +39,10 @@ static __device__ int g_gemm_tma_fault;
 
 constexpr int TM_M = 128;   // weight rows per tile (MMA M)
 constexpr int TM_N = 256;   // tokens per tile (MMA N)
-constexpr int TM_BK = 64;   // columns per stage: one 128-byte swizzle row of fp16
-constexpr int TM_STAGES = 2;
-constexpr int TM_A = TM_M * TM_BK * 2;  // 16 KB
-constexpr int TM_B = TM_N * TM_BK * 2;  // 32 KB
+constexpr int TM_BK = 32;   // columns per stage: one 64-byte swizzle row of fp16
+constexpr int TM_STAGES = 4;
+constexpr int TM_A = TM_M * TM_BK * 2;  // 8 KB
+constexpr int TM_B = TM_N * TM_BK * 2;  // 16 KB
 constexpr int TM_STAGE = 2 * TM_A + 2 * TM_B;
 constexpr int TM_THREADS = 6 * 32;      // producer, MMA, four epilogue warps
 constexpr size_t TM_SMEM = (size_t)TM_STAGES * TM_STAGE + 1024;
@@ -84,10 +85,11 @@ __device__ __forceinline__ void tm_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// K-major tile, 128-byte swizzle, 8-row groups 1024 bytes apart, sm_100 descriptor.
+// K-major tile, 64-byte swizzle (layout type 4), 8-row groups 512 bytes apart, sm_100
+// descriptor (version 1).
 __device__ __forceinline__ uint64_t tm_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
 
 // kind::f16: D FP32, A and B FP16, both K-major, M x N.
@@ -126,7 +128,7 @@ __device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 // 2-D tiled TMA load (no multicast) of the box at (x = column, y = row) into shared
-// memory, completing on bar.  x is a multiple of 64 fp16 (128 bytes).
+// memory, completing on bar.  x is a multiple of 32 fp16 (64 bytes).
 __device__ __forceinline__ void tma_load2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                            uint64_t* bar) {
     asm volatile(
@@ -264,7 +266,7 @@ static int tensor_map_2d(CUtensorMap* map, const void* base, int64_t inner, int6
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
