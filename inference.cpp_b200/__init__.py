@@ -29,6 +29,8 @@ TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q5_0: "Q5_0", Q5_1: "Q5_1",
 TYPE_BY_NAME = {v: k for k, v in TYPE_NAMES.items()}
 BLOCK_ELEMS = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256, F32: 1, F16: 1}
 BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q6_K: 210, F32: 4, F16: 2}
+# byte alignment the GEMV entry points require of a weight base
+GEMV_ALIGN = {Q4_0: 2, Q5_0: 2, Q5_1: 8, Q8_0: 2, Q4_K: 16, Q6_K: 2}
 
 IB_OK = 0
 

@@ -155,8 +155,10 @@ int tp_key_max_launch(const TpExchange& x, unsigned long long* best, cudaStream_
 // ---- TMA-staged persistent kernel: kNWC consumer warps + 1 producer warp ---------
 // Stage layout: 16 weight rows at slot_a / slot_b bytes apart (padded so the
 // consumers' loads of 8 rows spread over the shared-memory banks), then the limb
-// slice at byte wbytes.
-template <int TA, int TB, int PRO, int EPI>
+// slice at byte wbytes.  GEN: rows whose length is not a whole number of stages, or
+// that do not start on 16-byte boundaries (the instantiation without it keeps the
+// producer's and consumers' per-stage work to the aligned case).
+template <int TA, int TB, int PRO, int EPI, bool GEN>
 __global__ void __launch_bounds__((kNWC + 1) * 32)
     fused_tma_kernel(const FusedGemv p, int S, int slot_a, int slot_b, int wbytes) {
     using P = Pair<TA, TB>;
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     __shared__ float red[2][kNWC][16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = p.K / P::BE;
-    const int spg = nb / P::KB;
+    const int spg = GEN ? (nb + P::KB - 1) / P::KB : nb / P::KB;  // GEN: the last may be short
     const int stage_bytes = wbytes + P::SLICE;
     const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
     if (threadIdx.x == 0) {
@@ -188,7 +190,10 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Row groups come
         // from the work counter (or the static stride); stage_rg[s] tells the consumers
         // which row group a stage holds, -1 ends their loop.  Stage slot s and its phase
-        // advance incrementally (no divisions in the loop).
+        // advance incrementally (no divisions in the loop).  A row that does not start on
+        // a 16-byte boundary is copied from the boundary below it (the offset is the same
+        // in every stage: a full stage is a multiple of 16 bytes) and its copy length
+        // rounded up to 16 bytes; the row slots have room for the extra 16 bytes.
         auto limbs = [&](int slot_s, int st) {
             if (lane == 16)
                 bulk_g2s(smem + (size_t)slot_s * stage_bytes + wbytes,
@@ -211,24 +216,37 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
             const int n = group_rows(p, rg);
             const int slot = isb ? slot_b : slot_a;
             const uint8_t* src = p.W[0];
+            uint32_t off = 0;
             if (lane < n) {
                 int seg, lr;
                 tile_row(p, rg, lane, seg, lr);
                 src = p.W[seg] + (size_t)lr * nb * bb;
+                if (GEN) {
+                    off = (uint32_t)((uintptr_t)src & 15u);
+                    src -= off;
+                }
             }
             for (int st = 0; st < spg; ++st, ++it) {
                 if (it >= S && !mbar_wait(&empty[s], ph ^ 1, &g_decode_fault, 11)) {
                     ok = false;
                     break;
                 }
+                uint32_t len = (uint32_t)chunk, tot = (uint32_t)(n * chunk);
+                if (GEN) {
+                    const int nbl = nb - st * P::KB < P::KB ? nb - st * P::KB : P::KB;
+                    len = lane < n ? (off + (uint32_t)(nbl * bb) + 15u) & ~15u : 0u;
+                    tot = len;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                }
                 if (lane == 0) {
                     stage_rg[s] = rg;
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)(n * chunk + P::SLICE));
+                    mbar_arrive_expect_tx(&full[s], tot + (uint32_t)P::SLICE);
                 }
                 __syncwarp();
                 if (lane < n)
                     bulk_g2s(smem + (size_t)s * stage_bytes + (size_t)lane * slot,
-                             src + (size_t)st * chunk, (uint32_t)chunk, &full[s]);
+                             src + (size_t)st * chunk, len, &full[s]);
                 if (waited) {
                     limbs(s, st);
                 } else if (it == S - 1) {
@@ -273,6 +291,15 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         const bool isb = group_is_b<TA, TB>(p, rg);
         const int n = group_rows(p, rg);
         const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
+        const size_t rbytes = (size_t)nb * (isb ? Fmt<TB>::BB : Fmt<TA>::BB);
+        int oa = 0, ob = 0;
+        if (GEN) {
+            int seg, lr;
+            tile_row(p, rg, ra, seg, lr);
+            oa = (int)((uintptr_t)(p.W[seg] + (size_t)lr * rbytes) & 15u);
+            tile_row(p, rg, rb, seg, lr);
+            ob = (int)((uintptr_t)(p.W[seg] + (size_t)lr * rbytes) & 15u);
+        }
         for (int st = 0; st < spg; ++st) {
             if (st > 0 && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) {
                 ok = false;
@@ -280,12 +307,22 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
             }
             const uint8_t* base = smem + (size_t)s * stage_bytes;
             const uint8_t* slab = base + wbytes;
-            if (isb)
-                stage_math<TB, P::KB, P::SE, P::GS>(base, slab, slot_b, ra, rb, c, ll, warp, acc_a,
-                                                    acc_b);
-            else
-                stage_math<TA, P::KB, P::SE, P::GS>(base, slab, slot_a, ra, rb, c, ll, warp, acc_a,
-                                                    acc_b);
+            const int nbl = nb - st * P::KB;
+            if (!GEN || nbl >= P::KB) {
+                if (isb)
+                    stage_math<TB, P::KB, P::SE, P::GS, true>(base, slab, slot_b, ra, rb, oa, ob,
+                                                              P::KB, c, ll, warp, acc_a, acc_b);
+                else
+                    stage_math<TA, P::KB, P::SE, P::GS, true>(base, slab, slot_a, ra, rb, oa, ob,
+                                                              P::KB, c, ll, warp, acc_a, acc_b);
+            } else {
+                if (isb)
+                    stage_math<TB, P::KB, P::SE, P::GS, false>(base, slab, slot_b, ra, rb, oa, ob,
+                                                               nbl, c, ll, warp, acc_a, acc_b);
+                else
+                    stage_math<TA, P::KB, P::SE, P::GS, false>(base, slab, slot_a, ra, rb, oa, ob,
+                                                               nbl, c, ll, warp, acc_a, acc_b);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (++s == S) {
@@ -310,64 +347,13 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     }
 }
 
-// ---- direct-load kernel (rows not sliceable into 16-byte TMA copies) ---------------
-template <int TA, int TB, int PRO, int EPI>
-__global__ void __launch_bounds__(kNWC * 32) fused_direct_kernel(const FusedGemv p) {
-    using P = Pair<TA, TB>;
-    __shared__ float red[2][kNWC][16];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = p.K / P::BE;
-    const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
-    pdl_launch_dependents();
-    pdl_wait();
-    const float rms = PRO == PRO_NORM ? rms_of<P::GS>(p, lane) : 1.0f;
-    const LaneCtx c = lane_ctx();
-    float acc_a = 0.f, acc_b = 0.f;
-    int k = 0;
-    for (int rg = blockIdx.x; rg < n_rg; rg += gridDim.x, ++k) {
-        int sa_, la, sb_, lb;
-        tile_row(p, rg, c.g, sa_, la);
-        tile_row(p, rg, c.g + 8, sb_, lb);
-        const bool isb = group_is_b<TA, TB>(p, rg);
-        const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
-        const size_t rb = (size_t)nb * bb;
-        const uint8_t* Wa = p.W[sa_] + (size_t)la * rb;
-        const uint8_t* Wb = p.W[sb_] + (size_t)lb * rb;
-        for (int kb = warp * P::UNIT; kb < nb; kb += kNWC * P::UNIT) {
-            const int slice = kb / P::KB, kbl = kb - slice * P::KB;
-            const int nbl = nb - slice * P::KB < P::KB ? nb - slice * P::KB : P::KB;
-            const uint8_t* sl = p.slab + (size_t)slice * P::SLICE;
-            XLimbs xs;
-            xs.limbs = (int8_t*)sl;
-            xs.scale = (float*)(sl + P::SE * 4);
-            xs.sum32 = xs.scale + P::SE / P::GS;
-            xs.sum16 = xs.sum32 + P::SE / 32;
-            if (isb)
-                block_math<TB, false, false>(Wa + (size_t)kb * bb, Wb + (size_t)kb * bb, kbl, nbl,
-                                             xs, c, acc_a, acc_b);
-            else
-                block_math<TA, false, false>(Wa + (size_t)kb * bb, Wb + (size_t)kb * bb, kbl, nbl,
-                                             xs, c, acc_a, acc_b);
-        }
-        finish_group<EPI>(p, red[k & 1], rg, warp, lane, c, rms, acc_a, acc_b);
-    }
-    if (tp_exchanges<EPI>(p)) {  // as in fused_tma_kernel; every thread gets here
-        if (EPI == EPI_ARGMAX) __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0 && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
-            tp_finish<EPI>(p);
-            p.work[0] = 0;
-            p.work[1] = 0;
-        }
-    }
-}
-
 // ---- host side ----------------------------------------------------------------------
-// Row stride in a stage: >= the chunk, a multiple of 16, and congruent to 32 (Q4_K's
-// 8-byte loads) or 16 (the 2/4-byte loads of the other formats) modulo 128.
-static int ring_slot(int type, int chunk) {
+// Row stride in a stage: >= the chunk (+16 bytes when rows do not start on 16-byte
+// boundaries), a multiple of 16, and congruent to 32 (Q4_K's 8-byte loads) or 16 (the
+// 2/4-byte loads of the other formats) modulo 128.
+static int ring_slot(int type, int chunk, bool pad) {
     const int want = type == IB_TYPE_Q4_K ? 32 : 16;
-    int s = (chunk + 15) / 16 * 16;
+    int s = (chunk + (pad ? 16 : 0) + 15) / 16 * 16;
     while (s % 128 != want) s += 16;
     return s;
 }
@@ -462,9 +448,12 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
     bool has_a = false, has_b = false;
     for (int s = 0; s < p.n_seg; ++s) (p.type[s] == TA ? has_a : has_b) = true;
     int r;
-    if (nb % P::KB == 0) {
-        const int slot_a = ring_slot(TA, P::KB * Fmt<TA>::BB);
-        const int slot_b = ring_slot(TB, P::KB * Fmt<TB>::BB);
+    {
+        const bool pad_a = has_a && (size_t)nb * Fmt<TA>::BB % 16 != 0;
+        const bool pad_b = has_b && (size_t)nb * Fmt<TB>::BB % 16 != 0;
+        const bool gen = pad_a || pad_b || nb % P::KB != 0;
+        const int slot_a = ring_slot(TA, P::KB * Fmt<TA>::BB, pad_a);
+        const int slot_b = ring_slot(TB, P::KB * Fmt<TB>::BB, pad_b);
         const int wbytes = 16 * ((has_b && (!has_a || slot_b > slot_a)) ? slot_b : slot_a);
         const int stage = wbytes + P::SLICE;
         // Ring depth.  Short rows (K-quant rows of <= 4 stages: K <= 8192) run 2 stages
@@ -475,12 +464,13 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
         // 2050: 2.26 ms, against 2.45 with 2 stages for the down projection, 2.32 with 3
         // stages for the QKV projection and head too, 2.36 with 4 stages at one CTA per
         // SM for the down projection, and 2.58 with 3 stages for the 4-bit kernels.
-        const int spg = nb / P::KB;  // ring stages per row group
+        const int spg = (nb + P::KB - 1) / P::KB;  // ring stages per row group
         int S = (has_b && TB == IB_TYPE_Q6_K && spg > 4) ? 3 : 73728 / stage;
         if (S < 2) S = 2;
         if (S > kMaxStages) S = kMaxStages;
         const size_t smem = (size_t)S * stage;
-        auto kern = fused_tma_kernel<TA, TB, PRO, EPI>;
+        auto kern = gen ? fused_tma_kernel<TA, TB, PRO, EPI, true>
+                        : fused_tma_kernel<TA, TB, PRO, EPI, false>;
         int cap = 0;
         if ((r = max_ctas((const void*)kern, (kNWC + 1) * 32, smem, &cap))) return r;
         // dynamic schedule: every resident slot claims row groups; static: an even split
@@ -488,13 +478,7 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
         const int grid = p.work ? (n_rg < cap ? n_rg : cap) : (n_rg + per - 1) / per;
         IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3((kNWC + 1) * 32), smem, st, pdl, p, S,
                                  slot_a, slot_b, wbytes));
-        return IB_OK;
     }
-    auto kern = fused_direct_kernel<TA, TB, PRO, EPI>;
-    int cap = 0;
-    if ((r = max_ctas((const void*)kern, kNWC * 32, 0, &cap))) return r;
-    const int grid = n_rg < cap ? n_rg : cap;
-    IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(kNWC * 32), 0, st, pdl, p));
     return IB_OK;
 }
 

@@ -303,33 +303,48 @@ __device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*re
     return true;
 }
 
-// One stage (KB blocks of the 16 tile rows; limb slice at `slab`) for this warp's
-// share of the blocks.
-template <int TYPE, int KB, int SE, int GS>
+// One stage of the 16 tile rows (limb slice at `slab`) for this warp's share of the
+// blocks: rows ra / rb start at byte offsets oa / ob of their row slots.  FULL: the
+// stage holds KB blocks (loops unrolled); otherwise nbl < KB, the last stage of a row
+// whose length is not a whole number of stages.
+template <int TYPE, int KB, int SE, int GS, bool FULL>
 __device__ __forceinline__ void stage_math(const uint8_t* base, const uint8_t* slab, int slot,
-                                           int ra, int rb, const LaneCtx& c, const LeanLane& ll,
-                                           int warp, float& acc_a, float& acc_b) {
+                                           int ra, int rb, int oa, int ob, int nbl,
+                                           const LaneCtx& c, const LeanLane& ll, int warp,
+                                           float& acc_a, float& acc_b) {
     using F = Fmt<TYPE>;
     if constexpr (TYPE == IB_TYPE_Q4_K) {
         const uint32_t b = smem_u32(base), x = smem_u32(slab);
-        const uint32_t wa = b + (uint32_t)(ra * slot), wb = b + (uint32_t)(rb * slot);
+        const uint32_t wa = b + (uint32_t)(ra * slot + oa), wb = b + (uint32_t)(rb * slot + ob);
         const uint32_t scale = x + SE * 4, sum32 = scale + (SE / GS) * 4;
-#pragma unroll
-        for (int kbl = warp; kbl < KB; kbl += kNWC)
+        auto one = [&](int kbl) {
             q4k_tile_lean(wa + kbl * F::BB, wb + kbl * F::BB, x + kbl * 1024, sum32 + kbl * 32,
                           ldsf<0>(scale + kbl * 4), c, ll, acc_a, acc_b);
+        };
+        if constexpr (FULL) {
+#pragma unroll
+            for (int kbl = warp; kbl < KB; kbl += kNWC) one(kbl);
+        } else {
+            for (int kbl = warp; kbl < nbl; kbl += kNWC) one(kbl);
+        }
     } else {
         XLimbs xs;
         xs.limbs = (int8_t*)slab;
         xs.scale = (float*)(slab + SE * 4);
         xs.sum32 = xs.scale + SE / GS;
         xs.sum16 = xs.sum32 + SE / 32;
-        const uint8_t* sa = base + (size_t)ra * slot;
-        const uint8_t* sb = base + (size_t)rb * slot;
+        const uint8_t* sa = base + (size_t)ra * slot + oa;
+        const uint8_t* sb = base + (size_t)rb * slot + ob;
+        if constexpr (FULL) {
 #pragma unroll
-        for (int kbl = warp * F::UNIT; kbl < KB; kbl += kNWC * F::UNIT)
-            block_math<TYPE, true, true>(sa + kbl * F::BB, sb + kbl * F::BB, kbl, KB, xs, c,
-                                         acc_a, acc_b);
+            for (int kbl = warp * F::UNIT; kbl < KB; kbl += kNWC * F::UNIT)
+                block_math<TYPE, true, true>(sa + kbl * F::BB, sb + kbl * F::BB, kbl, KB, xs, c,
+                                             acc_a, acc_b);
+        } else {
+            for (int kbl = warp * F::UNIT; kbl < nbl; kbl += kNWC * F::UNIT)
+                block_math<TYPE, true, true>(sa + kbl * F::BB, sb + kbl * F::BB, kbl, nbl, xs, c,
+                                             acc_a, acc_b);
+        }
     }
 }
 

@@ -5,8 +5,10 @@
 // a ring of S shared-memory stages, one 16-row x KB-block slice per stage,
 // guarded by mbarriers (full: transaction bytes; empty: one arrival per consumer
 // warp).  The bytes in flight are set by the ring, not by registers or occupancy.
-// Shapes whose row slices are not 16-byte aligned use the same math with direct
-// global loads.
+// Rows that do not start on a 16-byte boundary are copied from the boundary below
+// (row slots 16 bytes longer, per-row offsets); the last stage of a row may hold
+// fewer blocks.  Only a weight base that is not 16-byte aligned takes direct global
+// loads.
 //
 // Math: a SIMT FP32 dot product costs ~3 issue slots per 4-bit weight (unpack,
 // int->float, FMA).  Here the quants are widened to int8 with one LOP3 per four
@@ -107,19 +109,24 @@ __device__ __forceinline__ void finish_rows(float (*red)[16], int warp, const La
 // CTA c owns row groups (16 rows) c, c + G, c + 2G, ... (G = gridDim.x, chosen so the
 // groups divide evenly over the CTAs).  The producer streams every group's stages
 // through one ring without pausing between groups; consumers reduce each group's
-// partials behind a named barrier (double-buffered, so one barrier per group).
-template <int TYPE, int NWC, int S>
+// partials behind a named barrier (double-buffered, so one barrier per group).  `slot`
+// is the row stride in a stage: CHUNK, or CHUNK + 16 when rows do not start on 16-byte
+// boundaries (a row is then copied from the boundary below it, at the same offset in
+// every stage, since CHUNK is a multiple of 16).  GEN: such rows, or rows whose length
+// is not a whole number of stages; the instantiation without it keeps the aligned case
+// free of the per-row offsets and lengths.
+template <int TYPE, int NWC, int S, bool GEN>
 __global__ void __launch_bounds__((NWC + 1) * 32) gemv_tma_kernel(const uint8_t* __restrict__ W,
                                                                  XLimbs xb, float* __restrict__ y,
-                                                                 int rows, int nb) {
+                                                                 int rows, int nb, int slot) {
     using F = Fmt<TYPE>;
-    extern __shared__ __align__(128) uint8_t smem[];  // [S][16][CHUNK]
+    extern __shared__ __align__(128) uint8_t smem[];  // [S][16][slot]
     __shared__ __align__(8) uint64_t full[S], empty[S];
     __shared__ float red[2][NWC][16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_rg = (rows + 15) / 16;
     const int my_rg = blockIdx.x < n_rg ? (n_rg - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int spg = nb / F::KB;  // stages per row group
+    const int spg = GEN ? (nb + F::KB - 1) / F::KB : nb / F::KB;  // stages per row group
     const int total = my_rg * spg;
     const size_t rbytes = (size_t)nb * F::BB;
     if (threadIdx.x == 0) {
@@ -138,12 +145,21 @@ __global__ void __launch_bounds__((NWC + 1) * 32) gemv_tma_kernel(const uint8_t*
             const int rg = blockIdx.x + (it / spg) * gridDim.x, st = it % spg;
             const int row_base = rg * 16, n = min(16, rows - row_base);
             if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, &g_gemv_fault, 1)) break;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(n * F::CHUNK));
+            const uint8_t* src = W + (size_t)(row_base + min(lane, n - 1)) * rbytes;
+            uint32_t off = 0, len = F::CHUNK, tot = (uint32_t)(n * F::CHUNK);
+            if (GEN) {
+                const int nbl = min(F::KB, nb - st * F::KB);
+                off = (uint32_t)((uintptr_t)src & 15u);
+                len = lane < n ? (off + (uint32_t)(nbl * F::BB) + 15u) & ~15u : 0u;
+                tot = len;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            }
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], tot);
             __syncwarp();
             if (lane < n)
-                bulk_g2s(smem + ((size_t)s * 16 + lane) * F::CHUNK,
-                         W + (size_t)(row_base + lane) * rbytes + (size_t)st * F::CHUNK, F::CHUNK,
-                         &full[s]);
+                bulk_g2s(smem + ((size_t)s * 16 + lane) * (GEN ? slot : F::CHUNK),
+                         src - off + (size_t)st * F::CHUNK, len, &full[s]);
             issued = it + 1;
         }
         // make sure no copy is still landing when the CTA retires (normally a no-op)
@@ -161,12 +177,24 @@ __global__ void __launch_bounds__((NWC + 1) * 32) gemv_tma_kernel(const uint8_t*
         if (ok && !mbar_wait(&full[s], (it / S) & 1, &g_gemv_fault, 3)) ok = false;
         if (ok) {
             const int ra = min(c.g, n - 1), rb = min(c.g + 8, n - 1);
-            const uint8_t* sa = smem + ((size_t)s * 16 + ra) * F::CHUNK;
-            const uint8_t* sb = smem + ((size_t)s * 16 + rb) * F::CHUNK;
+            int oa = 0, ob = 0;
+            if (GEN) {
+                oa = (int)((uintptr_t)(W + (size_t)(row_base + ra) * rbytes) & 15u);
+                ob = (int)((uintptr_t)(W + (size_t)(row_base + rb) * rbytes) & 15u);
+            }
+            const uint8_t* sa = smem + ((size_t)s * 16 + ra) * (GEN ? slot : F::CHUNK) + oa;
+            const uint8_t* sb = smem + ((size_t)s * 16 + rb) * (GEN ? slot : F::CHUNK) + ob;
+            const int nbl = nb - st * F::KB;
+            if (!GEN || nbl >= F::KB) {
 #pragma unroll
-            for (int kbl = warp * F::UNIT; kbl < F::KB; kbl += NWC * F::UNIT)
-                block_math<TYPE, true>(sa + kbl * F::BB, sb + kbl * F::BB, st * F::KB + kbl, nb,
-                                       xb, c, acc_a, acc_b);
+                for (int kbl = warp * F::UNIT; kbl < F::KB; kbl += NWC * F::UNIT)
+                    block_math<TYPE, true>(sa + kbl * F::BB, sb + kbl * F::BB, st * F::KB + kbl,
+                                           nb, xb, c, acc_a, acc_b);
+            } else {
+                for (int kbl = warp * F::UNIT; kbl < nbl; kbl += NWC * F::UNIT)
+                    block_math<TYPE, true>(sa + kbl * F::BB, sb + kbl * F::BB, st * F::KB + kbl,
+                                           nb, xb, c, acc_a, acc_b);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -247,7 +275,7 @@ void xlimbs_carve(void* base, int K, XLimbs& xb) {
 constexpr int kSetupDevices = 64;
 static std::mutex g_setup_mu;
 static uint64_t g_setup_done[kSetupDevices];  // bit fmt_slot(TYPE) per device
-static int g_max_ctas[kSetupDevices][6];
+static int g_max_ctas[kSetupDevices][6][2];  // [.][.][general instantiation]
 
 template <int TYPE>
 constexpr int fmt_slot() {
@@ -260,27 +288,36 @@ constexpr int ring_stages() {
     return TYPE == IB_TYPE_Q6_K ? 2 : (TYPE == IB_TYPE_Q8_0 ? 3 : 4);
 }
 
-// With g_setup_mu held: the set-up of TYPE on device dev; *cap = resident TMA CTAs.
+template <int TYPE>
+constexpr size_t ring_bytes(bool pad) {
+    return (size_t)ring_stages<TYPE>() * 16 * (Fmt<TYPE>::CHUNK + (pad ? 16 : 0));
+}
+
+// With g_setup_mu held: the set-up of TYPE on device dev; cap[gen] = resident CTAs of
+// the aligned / general TMA kernel.
 template <int TYPE>
 static int setup_typed_locked(int dev, int* cap) {
-    using F = Fmt<TYPE>;
     constexpr int NWC = 8, S = ring_stages<TYPE>(), slot = fmt_slot<TYPE>();
     if (!(g_setup_done[dev] & (1ull << slot))) {
-        const size_t smem = (size_t)S * 16 * F::CHUNK;
-        auto kern = gemv_tma_kernel<TYPE, NWC, S>;
-        if (smem + 2048 > 48 * 1024)
-            IB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)smem));
-        int per_sm = 0, sms = 0;
-        IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (NWC + 1) * 32,
-                                                                    smem));
+        int sms = 0;
         IB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        for (int gen = 0; gen < 2; ++gen) {
+            auto kern = gen ? gemv_tma_kernel<TYPE, NWC, S, true> : gemv_tma_kernel<TYPE, NWC, S, false>;
+            const size_t smem = ring_bytes<TYPE>(gen != 0);  // the general case: padded rows
+            if (smem + 2048 > 48 * 1024)
+                IB_CUDA_CHECK(cudaFuncSetAttribute(
+                    kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            int per_sm = 0;
+            IB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern,
+                                                                        (NWC + 1) * 32, smem));
+            g_max_ctas[dev][slot][gen] = (per_sm > 0 ? per_sm : 1) * sms;
+        }
         cudaFuncAttributes fa;
         IB_CUDA_CHECK(cudaFuncGetAttributes(&fa, gemv_direct_kernel<TYPE, 8>));
-        g_max_ctas[dev][slot] = (per_sm > 0 ? per_sm : 1) * sms;
         g_setup_done[dev] |= 1ull << slot;
     }
-    *cap = g_max_ctas[dev][slot];
+    cap[0] = g_max_ctas[dev][slot][0];
+    cap[1] = g_max_ctas[dev][slot][1];
     return IB_OK;
 }
 
@@ -298,20 +335,22 @@ static int launch_typed(const uint8_t* W, const XLimbs& xb, float* y, int64_t ro
     constexpr int S = ring_stages<TYPE>();
     const int nb = (int)(cols / (F::K ? 256 : 32));
     const int n_rg = (int)((rows + 15) / 16);
-    const size_t rbytes = (size_t)nb * F::BB;
-    const bool tma_ok = nb % F::KB == 0 && rbytes % 16 == 0 && ((uintptr_t)W & 15) == 0;
-    if (tma_ok) {
-        const size_t smem = (size_t)S * 16 * F::CHUNK;
-        int dev = 0, cap = 0, r;
+    const bool pad = (size_t)nb * F::BB % 16 != 0;
+    const bool gen = pad || nb % F::KB != 0;
+    if (((uintptr_t)W & 15) == 0) {
+        const size_t smem = ring_bytes<TYPE>(pad);
+        int dev = 0, cap[2] = {0, 0}, r;
         if ((r = current_device(&dev))) return r;
         {
             std::lock_guard<std::mutex> lock(g_setup_mu);
-            if ((r = setup_typed_locked<TYPE>(dev, &cap))) return r;
+            if ((r = setup_typed_locked<TYPE>(dev, cap))) return r;
         }
         // as many CTAs as fit, but dividing the row groups evenly
-        const int per = (n_rg + cap - 1) / cap;
+        const int per = (n_rg + cap[gen] - 1) / cap[gen];
         const int grid = (n_rg + per - 1) / per;
-        gemv_tma_kernel<TYPE, NWC, S><<<grid, (NWC + 1) * 32, smem, st>>>(W, xb, y, (int)rows, nb);
+        auto kern = gen ? gemv_tma_kernel<TYPE, NWC, S, true> : gemv_tma_kernel<TYPE, NWC, S, false>;
+        kern<<<grid, (NWC + 1) * 32, smem, st>>>(W, xb, y, (int)rows, nb,
+                                                 F::CHUNK + (pad ? 16 : 0));
         IB_LAUNCH_CHECK("gemv_tma_kernel");
         return IB_OK;
     }
@@ -321,17 +360,17 @@ static int launch_typed(const uint8_t* W, const XLimbs& xb, float* y, int64_t ro
 }
 
 int gemv_mma_prepare_device() {
-    int dev = 0, cap = 0, r;
+    int dev = 0, cap[2] = {0, 0}, r;
     if ((r = current_device(&dev))) return r;
     cudaFuncAttributes fa;
     IB_CUDA_CHECK(cudaFuncGetAttributes(&fa, xq_kernel));
     std::lock_guard<std::mutex> lock(g_setup_mu);
-    if ((r = setup_typed_locked<IB_TYPE_Q4_K>(dev, &cap))) return r;
-    if ((r = setup_typed_locked<IB_TYPE_Q6_K>(dev, &cap))) return r;
-    if ((r = setup_typed_locked<IB_TYPE_Q4_0>(dev, &cap))) return r;
-    if ((r = setup_typed_locked<IB_TYPE_Q5_0>(dev, &cap))) return r;
-    if ((r = setup_typed_locked<IB_TYPE_Q5_1>(dev, &cap))) return r;
-    return setup_typed_locked<IB_TYPE_Q8_0>(dev, &cap);
+    if ((r = setup_typed_locked<IB_TYPE_Q4_K>(dev, cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q6_K>(dev, cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q4_0>(dev, cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q5_0>(dev, cap))) return r;
+    if ((r = setup_typed_locked<IB_TYPE_Q5_1>(dev, cap))) return r;
+    return setup_typed_locked<IB_TYPE_Q8_0>(dev, cap);
 }
 
 int gemv_mma_launch(int type, const void* W, const XLimbs& xb, float* y, int64_t rows,

@@ -175,35 +175,6 @@ __device__ __forceinline__ int qkv_kv_head(const FusedGemv& g, int rg) {
     return (R - g.rows[0] - g.rows[1]) / HD;
 }
 
-// One stage of a task: this warp's blocks of the stage's nbl blocks, rows ra / rb at
-// byte offsets oa / ob in their row slots.
-template <int TYPE, int SE, int GS>
-__device__ __forceinline__ void step_stage_math(const uint8_t* base, const uint8_t* slab, int slot,
-                                                int ra, int rb, int oa, int ob, int nbl,
-                                                const LaneCtx& c, const LeanLane& ll, int warp,
-                                                float& acc_a, float& acc_b) {
-    using F = Fmt<TYPE>;
-    if constexpr (TYPE == IB_TYPE_Q4_K) {
-        const uint32_t b = smem_u32(base), x = smem_u32(slab);
-        const uint32_t wa = b + (uint32_t)(ra * slot + oa), wb = b + (uint32_t)(rb * slot + ob);
-        const uint32_t scale = x + SE * 4, sum32 = scale + (SE / GS) * 4;
-        for (int kbl = warp; kbl < nbl; kbl += kNWC)
-            q4k_tile_lean(wa + kbl * F::BB, wb + kbl * F::BB, x + kbl * 1024, sum32 + kbl * 32,
-                          ldsf<0>(scale + kbl * 4), c, ll, acc_a, acc_b);
-    } else {
-        XLimbs xs;
-        xs.limbs = (int8_t*)slab;
-        xs.scale = (float*)(slab + SE * 4);
-        xs.sum32 = xs.scale + SE / GS;
-        xs.sum16 = xs.sum32 + SE / 32;
-        const uint8_t* sa = base + (size_t)ra * slot + oa;
-        const uint8_t* sb = base + (size_t)rb * slot + ob;
-        for (int kbl = warp * F::UNIT; kbl < nbl; kbl += kNWC * F::UNIT)
-            block_math<TYPE, true, true>(sa + kbl * F::BB, sb + kbl * F::BB, kbl, nbl, xs, c,
-                                         acc_a, acc_b);
-    }
-}
-
 // What the producer records about a task in the slot of its first stage.
 struct SlotRec {
     int task, phase, kind, rg, n, isb, spg, nb, stride;
@@ -760,11 +731,13 @@ __global__ void __launch_bounds__(kStepThreads, kStepCtasPerSm) decode_step_kern
                     const uint8_t* base = smem + (size_t)cs * P.stage_bytes;
                     const int nbl = min(PR::KB, nb - st * PR::KB);
                     if (isb)
-                        step_stage_math<TB, PR::SE, PR::GS>(base, base + P.wbytes, stride, ra, rb, oa,
-                                                            ob, nbl, c, ll, warp, acc_a, acc_b);
+                        stage_math<TB, PR::KB, PR::SE, PR::GS, false>(
+                            base, base + P.wbytes, stride, ra, rb, oa, ob, nbl, c, ll, warp, acc_a,
+                            acc_b);
                     else
-                        step_stage_math<TA, PR::SE, PR::GS>(base, base + P.wbytes, stride, ra, rb, oa,
-                                                            ob, nbl, c, ll, warp, acc_a, acc_b);
+                        stage_math<TA, PR::KB, PR::SE, PR::GS, false>(
+                            base, base + P.wbytes, stride, ra, rb, oa, ob, nbl, c, ll, warp, acc_a,
+                            acc_b);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[cs]);
                     if (++cs == S) {

@@ -27,7 +27,11 @@ def to_dev(cuda, a):
 
 def shapes_for(type_):
     be = ib.BLOCK_ELEMS[type_]
-    base = [(1, be), (7, be), (33, 2 * be), (64, 512), (1000, 1024), (4096, 4096)]
+    # rows of 1-3 and 22 / 28 K-quant blocks end in a short ring stage; Q6_K rows of 22
+    # / 28 blocks (4620 / 5880 bytes) and 32-element rows of 9 blocks do not start on
+    # 16-byte boundaries
+    base = [(1, be), (7, be), (33, 2 * be), (64, 512), (1000, 1024), (4096, 4096),
+            (40, 5632), (24, 7168)]
     if be == 32:
         base += [(288, 288), (768, 288), (5, 32 * 9)]
     return base

@@ -72,8 +72,10 @@ def test_noalloc_allocates_nothing(cuda):
 # Run in a fresh process with lazy module loading, so that no kernel of the library has
 # been loaded or configured before the entry point's set-up call: every buffer is
 # allocated first, one set-up call (Q4_K) is made, and then the first call of every
-# format, at a shape on the TMA-staged kernel and at one on the direct-load kernel, must
-# leave the device's free memory and torch's allocator where the set-up call left them.
+# format, at a shape of whole ring stages, at one of a single short stage, and (for the
+# formats with 2-byte alignment) with a weight base off a 16-byte boundary, which takes
+# the direct-load kernel, must leave the device's free memory and torch's allocator
+# where the set-up call left them.
 _FIRST_CALLS = textwrap.dedent("""
     import sys
     sys.path.insert(0, {root!r})
@@ -82,13 +84,19 @@ _FIRST_CALLS = textwrap.dedent("""
     ib = load_package()
     ib.init(0)
     fmts = [ib.Q4_K, ib.Q6_K, ib.Q4_0, ib.Q5_0, ib.Q5_1, ib.Q8_0]
-    # (rows, cols): 4096 columns take the TMA kernel for every format; 256 columns
-    # (one K-quant block, eight 32-element blocks) take the direct-load kernel
-    shapes = [(4096, 4096), (40, 256)]
+    # (rows, cols, byte offset of the weights): 4096 columns fill whole stages of the TMA
+    # kernel; 256 columns (one K-quant block, eight 32-element blocks) one short stage
+    shapes = [(4096, 4096, 0), (40, 256, 0), (40, 256, 2)]
     bufs = []
     for t in fmts:
-        for rows, cols in shapes:
+        for rows, cols, off in shapes:
+            if off % ib.GEMV_ALIGN[t]:
+                continue
             W = ib.synth_device(t, rows, cols, seed=rows + cols + t)
+            if off:
+                Wo = torch.empty(W.numel() + off, dtype=torch.uint8, device="cuda")
+                Wo[off:].copy_(W)
+                W = Wo[off:]
             x = torch.randn(cols, device="cuda")
             y = torch.empty(rows, device="cuda")
             bufs.append((t, W, x, y, rows, cols))
