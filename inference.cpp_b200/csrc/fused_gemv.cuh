@@ -237,37 +237,9 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
     }
 }
 
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"r"(kNWC * 32) : "memory");
-}
-
-// Sums the consumer warps' partials of the row group, applies the RMSNorm divisor
-// and runs the epilogue.
-template <int EPI>
-__device__ __forceinline__ void finish_group(const FusedGemv& p, float (*r)[16], int rg,
-                                             int warp, int lane, const LaneCtx& c, float rms,
-                                             float& acc_a, float& acc_b) {
-    acc_a = quad_sum(acc_a);
-    acc_b = quad_sum(acc_b);
-    if (c.t == 0) {
-        r[warp][c.g] = acc_a;
-        r[warp][c.g + 8] = acc_b;
-    }
-    consumers_sync();
-    if (warp == 0) {
-        float v = 0.f;
-        if (lane < 16) {
-#pragma unroll
-            for (int w = 0; w < kNWC; ++w) v += r[w][lane];
-        }
-        epilogue<EPI>(p, rg, lane, v / rms);
-    }
-    acc_a = 0.f;
-    acc_b = 0.f;
-}
-
-// finish_group with bounded mbarrier handshakes instead of a named barrier (the TMA
-// kernel's consumer warps leave their loop independently after a failed wait):
+// Sums the consumer warps' partials of the row group, applies the RMSNorm divisor and
+// runs the epilogue, with bounded mbarrier handshakes (the TMA kernel's consumer warps
+// leave their loop independently after a failed wait):
 // every warp posts its partials to red[b] and arrives on rfull[b]; warp 0 waits, reduces,
 // runs the epilogue and frees the buffer on rfree[b]; a warp reusing red[b] (two row
 // groups later) first waits for that free.  Use u = rgl >> 1 of buffer b = rgl & 1.
