@@ -20,11 +20,14 @@ roofline: the dominant kernel, the Q4_K fused dequant-GEMV of ffn_gate/ffn_up
 cpu_baseline / --impl reference: the reference's own CPU matvec (oracle/_ref, or
         the C restatement where it was not built) on a bounded sample: one layer's
         seven projections plus 1/16 of the output head, extrapolated per token.
-With torchrun (N > 1) every rank decodes its own replica by default (no collective
-on the data path; value is the sum over ranks, timed as the max over ranks).  With
---tp the N ranks hold one tensor-parallel model instead (Megatron split, NCCL
-allreduce after attn_output and ffn_down, cross-rank argmax of the head): value is
-that single sequence's tok/s (strong scaling).
+With torchrun (N > 1) the N ranks hold one tensor-parallel model (Megatron split:
+q/k/v and gate/up rows, attn_output and ffn_down input columns, the head's vocabulary
+rows; one exchange of the row-split projections' rows per sublayer over NVLink peer
+memory in the fused decode step, NCCL allreduce in prefill; a cross-rank argmax of the
+head): value is that single sequence's tok/s (strong scaling), and the line's
+`exchange` field gives one exchange round's device time, measured in isolation, and
+its share of the step.  --replicas instead has every rank decode its own copy (no
+collective on the data path; value is the sum over ranks, timed as the max over ranks).
 """
 from __future__ import annotations
 
@@ -377,7 +380,7 @@ def run_reference(args, cfg, world, rank, ib):
     if rank != 0:
         return 0
     t0 = time.perf_counter()
-    config = workload_config(cfg, args, world, args.tp and world > 1)
+    config = workload_config(cfg, args, world, world > 1 and not args.replicas)
     n = max(1, min(args.steps, 3))  # bounded: the run ends within a few minutes
     try:
         r = cpu_forward_sample(ib, cfg, n)
@@ -511,8 +514,10 @@ def main():
                     help="per-format GEMV / dequantisation GB/s over the op-sweep shapes "
                          "(one JSON line each) instead of the decode benchmark")
     ap.add_argument("--tp", action="store_true",
-                    help="with N > 1: one tensor-parallel model over the N GPUs instead of "
-                         "N replicas")
+                    help="with N > 1: one tensor-parallel model over the N GPUs (the default)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N > 1: N independent replicas instead of one tensor-parallel "
+                         "model")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -537,7 +542,7 @@ def main():
     ib.init(local)
     if args.sweep:
         return run_sweep(ib, args) if rank == 0 else 0
-    tp = args.tp and world > 1
+    tp = world > 1 and not args.replicas
     comm = make_comm(ib, world, rank, local) if tp else None
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
     m.set_fused(args.decode_path != "separate")
@@ -616,6 +621,19 @@ def main():
     clk["remeasured"] = remeasured
 
     kernels_per_step = m.step_kernels()
+    exchange = None
+    if tp and m.decode_path() == "fused":
+        # one exchange round (every rank's rows to every rank, then the rank-ordered sum
+        # and the next GEMV's slab) in isolation; the step holds one per row-split
+        # projection (attn_output, ffn_down) of every layer
+        barrier(world)
+        ex_us = all_max(world, m.tp_exchange_us(4 * cfg.n_layers))
+        rounds = 2 * cfg.n_layers
+        exchange = {"us_per_round": ex_us, "rounds_per_step": rounds,
+                    "share": rounds * ex_us / (dev_ms / args.steps * 1e3),
+                    "method": "device time of one round timed in isolation (a push kernel "
+                              "plus the receiving slab kernel), max over ranks; in the step "
+                              "the push is the row-split GEMV's epilogue"}
     nbytes, gemv_ms, gemv_solo_ms, gemv_reps = time_gemv(ib, cfg)
     gemm_flops, gemm_ms = time_gemm(ib, cfg, args.prompt)
     tpeak, tpeak_kind = measured_tensor_peak()
@@ -669,6 +687,7 @@ def main():
                                  "note": "useful flops 2*T*rows*cols; the kernel issues 3 fp16 "
                                          "MMAs per product (hi/lo operand pairs)"}},
             "cpu_baseline": cpu,
+            "exchange": exchange,
             "clocks": clk,
             "gpu_launches": kernels_per_step * args.steps,
         }

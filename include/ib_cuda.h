@@ -295,10 +295,37 @@ int ib_model_get_config(void* model, ib_model_config* cfg);
  * it out of band and calls ib_comm_init.  NCCL (libnccl.so.2) is opened at run time;
  * without it these calls return IB_ERR_COMM and the rest of the library works. */
 int ib_comm_unique_id(uint8_t* id128);
+/* The communicator runs in NCCL's non-blocking mode: initialisation and every later
+ * NCCL call settle within timeout_ms (ib_comm_init: IB_COMM_DEFAULT_TIMEOUT_MS), or the
+ * call returns IB_ERR_TIMEOUT (IB_ERR_COMM on an NCCL error) and the communicator is
+ * aborted -- ncclCommAbort, which also ends NCCL kernels still waiting for a rank that
+ * never arrived -- so a rank that never joins (or dies) leaves the others with an error,
+ * not a hang.  Every later call on an aborted communicator fails at once. */
+#define IB_COMM_DEFAULT_TIMEOUT_MS 300000
 int ib_comm_init(int rank, int world, const uint8_t* id128, int device, void** comm);
+int ib_comm_init_timeout(int rank, int world, const uint8_t* id128, int device,
+                         int64_t timeout_ms, void** comm);
 /* In-place sum over the ranks (FP32), on `stream`. */
 int ib_comm_allreduce_f32(void* comm, float* dev_buf, int64_t n, void* stream);
+/* *failed = 1 once the communicator has been aborted (after a failed or expired call,
+ * or ib_comm_abort). */
+int ib_comm_failed(void* comm, int* failed);
+/* Aborts the communicator (ncclCommAbort); ib_comm_free still releases the handle. */
+int ib_comm_abort(void* comm);
 int ib_comm_free(void* comm);
+/* The tensor-parallel model's peer-memory set-up (inside ib_model_finalize) is a
+ * two-round protocol in which every rank fails together: round 1 gathers each rank's
+ * status and IPC handle, round 2 the status of mapping the others' buffers; a rank that
+ * failed earlier in its set-up still joins both rounds.  This runs that protocol with a
+ * stand-in IPC layer (no device memory: a rank's handle is its rank number) over the
+ * caller's all-gather, for host-side tests of the failure paths: local_status != 0
+ * marks this rank as failed before the set-up, and on rank fail_rank the step
+ * fail_step (1 = export the handle, 2 = map a peer) fails.  Returns what the set-up
+ * returns on this rank (IB_OK or IB_ERR_COMM, the message names the failing rank);
+ * *opened / *closed count the stand-in mappings made and released. */
+typedef int (*ib_gather_fn)(void* ctx, const uint8_t* mine, uint8_t* all, size_t bytes);
+int ib_peer_setup_check(int rank, int world, int local_status, int fail_rank, int fail_step,
+                        ib_gather_fn gather, void* gather_ctx, int* opened, int* closed);
 /* Host-side shard of a packed [rows, cols] tensor: axis 0 = the rank's contiguous
  * rows/world rows, axis 1 = the rank's contiguous (cols/block)/world blocks of every
  * row (the split of an input dimension on block boundaries). */
@@ -320,6 +347,14 @@ int ib_model_create_tp(const ib_model_config* cfg, int device, void* comm, void*
 int ib_tp_wait_selftest(int peer_sends, int* fault, float* x_out);
 int ib_model_load_gguf_tp(const char* path, int precision, int device, int max_seq, void* comm,
                           void** model);
+/* Device time of one exchange round of the fused tensor-parallel decode step, measured
+ * in isolation: every rank's rows of the model's dimension sent to every rank over peer
+ * memory, then received, summed in rank order and turned into the next GEMV's limb slab
+ * (zero rows, so the model's state is unchanged).  The step holds one round after each
+ * row-split projection (attn_output, ffn_down).  Collective: every rank calls it with the
+ * same `rounds`; IB_ERR_TIMEOUT when a peer's rows did not arrive within the exchange's
+ * bounded wait. */
+int ib_model_tp_exchange_time(void* model, int rounds, float* us_per_round);
 
 /* ---- seeded synthetic weights (test and benchmark data, not a timed path) ---
  * Fills a [rows, cols] tensor of `type` with blocks encoding N(0, std) values

@@ -29,10 +29,12 @@ TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q5_0: "Q5_0", Q5_1: "Q5_1",
 TYPE_BY_NAME = {v: k for k, v in TYPE_NAMES.items()}
 BLOCK_ELEMS = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256, F32: 1, F16: 1}
 BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q6_K: 210, F32: 4, F16: 2}
+COMM_DEFAULT_TIMEOUT_MS = 300000  # IB_COMM_DEFAULT_TIMEOUT_MS
 # byte alignment the GEMV entry points require of a weight base
 GEMV_ALIGN = {Q4_0: 2, Q5_0: 2, Q5_1: 8, Q8_0: 2, Q4_K: 16, Q6_K: 2}
 
 IB_OK = 0
+IB_ERR_INVALID, IB_ERR_CUDA, IB_ERR_UNSUPPORTED, IB_ERR_OOM, IB_ERR_TIMEOUT, IB_ERR_COMM = range(1, 7)
 
 _c = ctypes
 _vp, _i, _i64, _f, _sz, _u64 = _c.c_void_p, _c.c_int, _c.c_int64, _c.c_float, _c.c_size_t, _c.c_uint64
@@ -64,6 +66,11 @@ SIGNATURES = {
     "ib_gemv_q_slab_chained": [_i, _vp, _vp, _vp, _i64, _i64, _vp],
     "ib_comm_unique_id": [_vp],
     "ib_comm_init": [_i, _i, _vp, _i, _vp],
+    "ib_comm_init_timeout": [_i, _i, _vp, _i, _i64, _vp],
+    "ib_comm_failed": [_vp, _vp],
+    "ib_comm_abort": [_vp],
+    "ib_peer_setup_check": [_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp],
+    "ib_model_tp_exchange_time": [_vp, _i, _vp],
     "ib_comm_allreduce_f32": [_vp, _vp, _i64, _vp],
     "ib_comm_free": [_vp],
     "ib_tp_shard": [_i, _vp, _i64, _i64, _i, _i, _i, _vp],
@@ -248,13 +255,25 @@ def tp_shard(type_: int, data, rows: int, cols: int, axis: int, rank: int, world
 
 
 class Comm:
-    """NCCL communicator for tensor parallelism (one process per GPU)."""
+    """NCCL communicator for tensor parallelism (one process per GPU), in NCCL's
+    non-blocking mode: initialisation and every later call settle within timeout_ms or
+    raise (IB_ERR_TIMEOUT), and the communicator is then aborted."""
 
-    def __init__(self, rank: int, world: int, uid: bytes, device: int = 0):
+    def __init__(self, rank: int, world: int, uid: bytes, device: int = 0,
+                 timeout_ms: int = COMM_DEFAULT_TIMEOUT_MS):
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
         h = ctypes.c_void_p()
-        call("ib_comm_init", rank, world, buf, device, ctypes.byref(h))
+        call("ib_comm_init_timeout", rank, world, buf, device, timeout_ms, ctypes.byref(h))
         self.h, self.rank, self.world = h, rank, world
+
+    @property
+    def failed(self) -> bool:
+        f = ctypes.c_int()
+        call("ib_comm_failed", self.h, ctypes.byref(f))
+        return bool(f.value)
+
+    def abort(self):
+        call("ib_comm_abort", self.h)
 
     @staticmethod
     def unique_id() -> bytes:
@@ -270,6 +289,33 @@ class Comm:
         if self.h:
             call("ib_comm_free", self.h)
             self.h = None
+
+
+GATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                             ctypes.c_size_t)
+
+
+def peer_setup_check(rank: int, world: int, gather, local_status: int = 0, fail_rank: int = -1,
+                     fail_step: int = 0):
+    """The tensor-parallel peer-memory set-up protocol with a stand-in IPC layer over
+    `gather(bytes) -> list of world bytes objects` (ib_peer_setup_check).  Returns
+    (status code, error text or "", mappings made, mappings released)."""
+    def cb(_ctx, mine, out, n):
+        try:
+            parts = gather(ctypes.string_at(mine, n))
+            blob = b"".join(parts)
+            if len(blob) != n * world:
+                return 1
+            ctypes.memmove(out, blob, len(blob))
+            return 0
+        except Exception:  # a rank that left: the protocol reports the failure
+            return 1
+    fn = GATHER_FN(cb)
+    opened, closed = ctypes.c_int(), ctypes.c_int()
+    rc = lib().ib_peer_setup_check(rank, world, local_status, fail_rank, fail_step,
+                                   ctypes.cast(fn, ctypes.c_void_p), None, ctypes.byref(opened),
+                                   ctypes.byref(closed))
+    return rc, (last_error() if rc else ""), opened.value, closed.value
 
 
 def gemm_q(type_: int, W, X, T: int, rows: int, cols: int, Y=None, stream=None):
@@ -548,6 +594,13 @@ class Model:
         p = ctypes.c_int()
         call("ib_model_decode_path", self.h, ctypes.byref(p))
         return {0: "separate", 1: "fused", 2: "persistent"}[p.value]
+
+    def tp_exchange_us(self, rounds: int = 64) -> float:
+        """Device time of one exchange round of the fused tensor-parallel step, in
+        isolation (collective: every rank calls it with the same rounds)."""
+        us = ctypes.c_float()
+        call("ib_model_tp_exchange_time", self.h, rounds, ctypes.byref(us))
+        return us.value
 
     def weight_bytes(self) -> int:
         n = ctypes.c_size_t()

@@ -518,6 +518,28 @@ __global__ void tp_selftest_push_kernel(uint64_t* region, int world, int stride,
         st_tagged(region + (size_t)src * stride + i, 1u, __float_as_uint(0.25f * (float)(src + 1)));
 }
 
+// One exchange round's sending side, as the row-split GEMV's epilogue and its last CTA
+// do it (every rank's rows, zeros here, into slot [rank] of every rank's region, tagged
+// with the exchange number; then the exchange counter advances).  One CTA.
+__global__ void tp_probe_push_kernel(const TpExchange x, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t e = __ldcg(x.seq);
+    const size_t at = ((size_t)(e & 1u) * x.world + x.rank) * x.stride;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < x.world) st_tagged((uint64_t*)x.region[q] + at + i, e + 1, 0u);
+    __syncthreads();
+    if (threadIdx.x == 0) *x.seq = e + 1;
+}
+
+int tp_probe_launch(const TpExchange& x, float* xv, int n, bool kquant, uint8_t* slab,
+                    cudaStream_t st) {
+    IB_CUDA_CHECK(launch_pdl(tp_probe_push_kernel, dim3(1), dim3(256), 0, st, true, x, n));
+    return xq_slab_launch(xv, nullptr, n, kquant, slab, nullptr, st, true, &x);
+}
+
 }  // namespace ib
 
 // One exchange on this GPU between rank 0 and a stand-in rank 1 whose rows arrive only

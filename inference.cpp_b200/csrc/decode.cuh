@@ -109,6 +109,11 @@ struct FusedGemv {
 // fused kernel (the caller then uses the separate kernels).
 int fused_gemv_launch(const FusedGemv& p, int pro, int epi, cudaStream_t st, bool pdl);
 bool fused_gemv_supported(const FusedGemv& p, int epi);
+// One tensor-parallel exchange round in isolation (the sending side of a row-split
+// GEMV's epilogue with zero rows, then the receiving slab kernel that adds every rank's
+// rows to xv[0..n) and builds its slab): collective, every rank launches the same rounds.
+int tp_probe_launch(const TpExchange& x, float* xv, int n, bool kquant, uint8_t* slab,
+                    cudaStream_t st);
 // Reads and clears the fused kernels' fault word (0 = no bounded wait expired).
 int decode_fault_take(int* code);
 // Decodes the ARGMAX key into a row index (resets nothing).

@@ -355,11 +355,9 @@ static int alloc_f(Model* m, float** p, size_t n) {
     return IB_OK;
 }
 
-extern "C" int ib_model_finalize(void* h) {
-    IB_REQUIRE(h, "null model");
-    Model* m = (Model*)h;
+// The model's device buffers (everything but the tensor-parallel peer memory).
+static int finalize_buffers(Model* m) {
     IB_CUDA_CHECK(cudaSetDevice(m->device));
-    if (m->finalized) return IB_OK;
     const auto& c = m->cfg;
     auto missing = [&](const std::string& what) {
         set_error("model: tensor not set: " + what);
@@ -470,27 +468,44 @@ extern "C" int ib_model_finalize(void* h) {
         m->logits_local = m->logits;
     }
     if (m->tp_size > 1) {
-        // the fused step's row-split GEMVs exchange their rows over peer memory
-        const int W = m->tp_size;
-        if (W > kMaxRanks) {
-            set_error("model: at most 8 tensor-parallel ranks");
-            return IB_ERR_UNSUPPORTED;
-        }
-        void* local = nullptr;
-        if ((st = comm_peer_alloc(m->comm, tp_region_bytes(W, c.dim), &local, m->tp_peers)))
-            return st;
-        m->tp_local = (uint8_t*)local;
         uint32_t* seq = nullptr;
         IB_CUDA_CHECK(cudaMalloc(&seq, 16));
-        IB_CUDA_CHECK(cudaMemset(seq, 0, 16));
         m->allocations.push_back(seq);
-        TpExchange& x = m->tpx;
-        for (int q = 0; q < W; ++q) x.region[q] = (uint8_t*)m->tp_peers[q];
-        x.seq = seq;
-        x.rank = m->tp_rank;
-        x.world = W;
-        x.stride = c.dim;
+        IB_CUDA_CHECK(cudaMemset(seq, 0, 16));
+        m->tpx.seq = seq;
     }
+    return IB_OK;
+}
+
+// Tensor parallelism: the peer memory of the fused step's exchange (its row-split GEMVs
+// store their rows into every rank's region).  Collective: every rank joins with the
+// status of its own set-up so far, and every rank fails if one did.
+static int finalize_peers(Model* m, int local_status) {
+    const int W = m->tp_size;
+    int st = local_status;
+    if (st == IB_OK && W > kMaxRanks) {
+        set_error("model: at most 8 tensor-parallel ranks");
+        st = IB_ERR_UNSUPPORTED;
+    }
+    void* local = nullptr;
+    if ((st = comm_peer_alloc(m->comm, tp_region_bytes(W, m->cfg.dim), st, &local, m->tp_peers)))
+        return st;
+    m->tp_local = (uint8_t*)local;
+    TpExchange& x = m->tpx;
+    for (int q = 0; q < W; ++q) x.region[q] = (uint8_t*)m->tp_peers[q];
+    x.rank = m->tp_rank;
+    x.world = W;
+    x.stride = m->cfg.dim;
+    return IB_OK;
+}
+
+extern "C" int ib_model_finalize(void* h) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    if (m->finalized) return IB_OK;
+    int st = finalize_buffers(m);
+    if (m->tp_size > 1) st = finalize_peers(m, st);
+    if (st) return st;
     m->fused_ok = fused_supported(m);
     if ((st = build_step_plan(m))) return st;
     IB_CUDA_CHECK(cudaMallocHost(&m->host_pinned, 256));
@@ -1278,6 +1293,42 @@ extern "C" int ib_model_load_gguf_tp(const char* path, int precision, int device
                                      void* comm, void** out) {
     IB_REQUIRE(comm, "null communicator");
     return load_gguf(path, precision, device, max_seq, (Comm*)comm, out);
+}
+
+extern "C" int ib_model_tp_exchange_time(void* h, int rounds, float* us_per_round) {
+    IB_REQUIRE(h && us_per_round && rounds > 0, "bad arguments");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized && m->tp_size > 1 && m->tpx.world > 1,
+               "exchange timing: not a finalized tensor-parallel model");
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    IB_CUDA_CHECK(cudaEventCreate(&e0));
+    IB_CUDA_CHECK(cudaEventCreate(&e1));
+    int r = IB_OK;
+    // one untimed round, then the timed ones (every rank runs the same rounds)
+    for (int i = 0; i <= rounds && r == IB_OK; ++i) {
+        if (i == 1 && cudaEventRecord(e0, m->stream) != cudaSuccess) r = IB_ERR_CUDA;
+        if (r == IB_OK)
+            r = tp_probe_launch(m->tpx, m->x, m->cfg.dim, m->slab_kq, m->slab_x, m->stream);
+    }
+    float ms = 0.f;
+    if (r == IB_OK && (cudaEventRecord(e1, m->stream) != cudaSuccess ||
+                       cudaEventSynchronize(e1) != cudaSuccess ||
+                       cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess)) {
+        set_error("exchange timing: event failure");
+        r = IB_ERR_CUDA;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (r) return r;
+    int fault = 0;
+    if ((r = decode_fault_take(&fault))) return r;
+    if (fault) {
+        set_error("exchange timing: a peer's rows did not arrive (fault " + std::to_string(fault) + ")");
+        return IB_ERR_TIMEOUT;
+    }
+    *us_per_round = ms * 1000.f / (float)rounds;
+    return IB_OK;
 }
 
 extern "C" int ib_model_get_config(void* h, ib_model_config* cfg) {

@@ -384,3 +384,113 @@ def test_exchange_wait_is_bounded(cuda):
     W = ib.dequantize(ib.Q4_K, blk, 64, 512).view(64, 512).double()
     assert bool(((y.double() - W @ v.double()).abs() <= 2e-5 * (W.abs() @ v.double().abs()) + 1e-30).all())
     assert ib.check_fault() == 0
+
+
+# ---------------------------------------------------------------------------
+# set-up failures: every rank fails together, nothing is left mapped or waiting
+# ---------------------------------------------------------------------------
+
+def _setup_rank(rank, world, port_no, scenario, q):
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port_no}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        if scenario == "never_joins" and rank == world - 1:
+            q.put((rank, None, "", 0, 0))  # this rank leaves before the set-up
+            return
+
+        def gather(mine: bytes):
+            out = [None] * world
+            dist.all_gather_object(out, mine)
+            return out
+
+        local = ib.IB_ERR_OOM if (scenario == "failed_before" and rank == 1) else 0
+        fail_rank, fail_step = {"export": (1, 1), "map": (0, 2)}.get(scenario, (-1, 0))
+        rc, err, opened, closed = ib.peer_setup_check(rank, world, gather, local, fail_rank,
+                                                      fail_step)
+        q.put((rank, rc, err, opened, closed))
+    finally:
+        if scenario != "never_joins":
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("scenario", ["ok", "failed_before", "export", "map", "never_joins"])
+def test_peer_setup_fails_together_gloo(scenario):
+    """The tensor-parallel peer-memory set-up on world_size-2 gloo ranks, with a
+    host-side stand-in for the IPC calls: a failure injected on one rank (before the
+    set-up, when exporting its handle, when mapping a peer) makes every rank return
+    IB_ERR_COMM naming that rank, and every mapping made is released; a rank that never
+    joins ends the others' set-up with an error instead of a wait."""
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port_no = free_port()
+    procs = [ctx.Process(target=_setup_rank, args=(r, world, port_no, scenario, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    if scenario == "ok":
+        for rank, rc, err, opened, closed in results:
+            assert rc == ib.IB_OK and opened == world - 1 and closed == 0, (rank, err)
+        return
+    if scenario == "never_joins":
+        rank, rc, err, opened, closed = results[0]
+        assert rc == ib.IB_ERR_COMM and "all-gather" in err and opened == closed == 0
+        return
+    failing = {"failed_before": 1, "export": 1, "map": 0}[scenario]
+    for rank, rc, err, opened, closed in results:
+        # a rank that failed before the set-up keeps its own code and message
+        own = scenario == "failed_before" and rank == failing
+        assert rc == (ib.IB_ERR_OOM if own else ib.IB_ERR_COMM), (rank, err)
+        assert opened == closed, rank
+        if rank == failing:
+            assert "injected" in err or "cannot" in err, err
+        else:
+            assert f"rank {failing}" in err and "every rank stops" in err, err
+
+
+_INIT_DEADLINE = """
+import sys, time
+import torch
+sys.path.insert(0, {root!r})
+from conftest import load_package
+ib = load_package()
+ib.init(0)
+uid = ib.Comm.unique_id()
+t0 = time.perf_counter()
+try:
+    ib.Comm(0, 2, uid, device=0, timeout_ms=3000)  # rank 1 never joins
+    print("no error")
+    sys.exit(1)
+except RuntimeError as e:
+    waited = time.perf_counter() - t0
+    assert "did not complete within 3000 ms" in str(e), str(e)
+    assert 2.5 < waited < 90, waited
+blk = ib.synth_device(ib.Q4_K, 64, 512, seed=3)
+v = torch.randn(512, device="cuda")
+y = ib.gemv_q(ib.Q4_K, blk, v, 64, 512)
+W = ib.dequantize(ib.Q4_K, blk, 64, 512).view(64, 512).double()
+assert bool(((y.double() - W @ v.double()).abs() <= 2e-5 * (W.abs() @ v.double().abs()) + 1e-30).all())
+print("deadline ok", round(waited, 2))
+"""
+
+
+@pytest.mark.gpu
+def test_comm_init_deadline_when_a_rank_never_joins(cuda):
+    """NCCL initialisation runs in non-blocking mode with a deadline: rank 0 of a world
+    of two whose rank 1 never joins gets an error once the deadline passes (the
+    communicator is aborted) instead of waiting for good, and the library keeps working.
+    A child process, under an outer limit, so that nothing here can stall the suite."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-c", _INIT_DEADLINE.format(root=root)],
+                       capture_output=True, text=True, timeout=240, env=env)
+    assert r.returncode == 0 and "deadline ok" in r.stdout, r.stdout + r.stderr[-2000:]
