@@ -12,6 +12,10 @@
 // partial with 128-position chunks.  With `pos_dev` the position is read on the
 // device (the grid then spans the whole cache and chunks past the position exit),
 // so a decode step can be captured once in a CUDA graph.
+#include <cuda_fp16.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "ops.cuh"
 #include "pdl.cuh"
@@ -680,201 +684,319 @@ int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos) {
     return IB_OK;
 }
 
-// ---- prefill attention: causal, GQA, FP32 flash attention ---------------------------
-// One CTA per (kv head, 64 query rows): rows r = g * QT + tq are (query head g of the
-// group, query q0 + tq), QT = 64 / G, so the group's heads share every K/V tile.  K and
-// V tiles of 32 positions arrive by cp.async, double-buffered.  Thread (ty, tx) of the
-// 16 x 16 grid holds S for rows ty + 16i, columns tx + 16j (K rows of neighbouring
-// threads are neighbours: conflict-free 16-byte loads with the 4-float row pad), the
-// online-softmax state of its four rows (reduced over the 16 lanes sharing them), and
-// O for the same rows, columns 4 tx + 64 j.  Scores are dot * scale as the reference
-// (src/ops/cuda_kernels.cu attention_batch_kernel); the softmax is rescaled per tile.
-constexpr int AP_BQ = 64, AP_BK = 32;
+// ---- prefill attention: causal, GQA, on the tensor cores ------------------------------
+// Scores and the P.V product run as mma.sync.m16n8k16 (FP16 operands, FP32 accumulate)
+// with every FP32 operand split into two FP16 parts, x = hi + lo (hi = fp16(x), lo =
+// fp16(x - hi)), and the three products hi.hi + hi.lo + lo.hi accumulated in FP32:
+// about 22 bits per operand instead of FP32's 24, the dropped lo.lo term below 2^-22
+// of the product.  K and V of the positions in range are split once per call by
+// kv_planes_kernel into FP16 planes [kv head][position][head_dim] (hi and lo); the
+// query rows are scaled by `scale` (the reference's dot * scale,
+// src/ops/cuda_kernels.cu attention_batch_kernel) and split while they are staged.
+//
+// One CTA of 8 warps per (kv head, block of 128 query rows); rows r = g * QT + tq are
+// (query head g of the group, query q0 + tq), QT = 128 / G, so the group's heads share
+// every K/V tile.  Warp w owns rows 16w..16w+15: their query fragments stay in
+// registers, the scores of a 64-position tile are an 16 x 64 accumulator whose layout
+// is the A-operand layout of the P.V product (no shuffle), the online-softmax state
+// (max, sum) of the lane's two rows is reduced over the 4 lanes of a quad, and O is a
+// 16 x head_dim accumulator.  K/V tiles (4 planes of 64 positions) arrive by cp.async,
+// double-buffered; the first stage's buffer stages the query rows before the loop.
+// Shared-memory rows are padded by 16 bytes, so the 8 rows of an ldmatrix hit distinct
+// banks.
+constexpr int AP_ROWS = 128, AP_BK = 64, AP_WARPS = 8;
+
+template <int HD>
+__host__ __device__ constexpr int ap_ld() { return HD + 8; }  // padded row, halves
 
 template <int HD>
 constexpr size_t attn_prefill_smem() {
-    return ((size_t)AP_BQ * (HD + 4) + 2 * (size_t)AP_BK * (HD + 4) + 2 * (size_t)AP_BK * HD +
-            (size_t)AP_BQ * (AP_BK + 4)) * sizeof(float);
+    return (size_t)2 * 4 * AP_BK * ap_ld<HD>() * 2;  // 2 stages x 4 planes
 }
 
-__device__ __forceinline__ void ap_cp16(float* dst, const float* src, bool valid) {
+__device__ __forceinline__ void ap_cp16(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
                      static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
                  "l"(src), "r"(valid ? 16 : 0)
                  : "memory");
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (x0, x1) -> packed FP16 hi parts and lo parts
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// K and V rows [0, n_pos) of every kv head into FP16 hi/lo planes
+// [n_kv_heads][n_pos][head_dim] (planes: K hi, K lo, V hi, V lo).
+__global__ void kv_planes_kernel(const float* __restrict__ kc, const float* __restrict__ vc,
+                                 __half* __restrict__ planes, int Hkv, int max_seq, int HD,
+                                 int n_pos) {
+    const size_t per = (size_t)Hkv * n_pos * HD;  // elements per plane
+    const size_t n4 = per / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t e = i * 4;
+        const int d = (int)(e % HD);
+        const size_t hp = e / HD;  // kv head * n_pos + position
+        const int pos = (int)(hp % n_pos), hk = (int)(hp / n_pos);
+        const size_t src = ((size_t)hk * max_seq + pos) * HD + d;
+        const float4 k = *reinterpret_cast<const float4*>(kc + src);
+        const float4 v = *reinterpret_cast<const float4*>(vc + src);
+        uint32_t h0, l0, h1, l1;
+        split2(k.x, k.y, h0, l0);
+        split2(k.z, k.w, h1, l1);
+        *reinterpret_cast<uint2*>(planes + e) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(planes + per + e) = make_uint2(l0, l1);
+        split2(v.x, v.y, h0, l0);
+        split2(v.z, v.w, h1, l1);
+        *reinterpret_cast<uint2*>(planes + 2 * per + e) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(planes + 3 * per + e) = make_uint2(l0, l1);
+    }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(256, 2)
-    attn_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                        const float* __restrict__ vc, float* __restrict__ out, int H, int Hkv,
-                        int max_seq, int start, int T, float scale) {
-    constexpr int QS = HD + 4, PS = AP_BK + 4, OC = HD / 64;
-    extern __shared__ __align__(16) float apsm[];
-    float* Qs = apsm;                   // [64][QS]
-    float* Ks = Qs + AP_BQ * QS;        // [2][32][QS]
-    float* Vs = Ks + 2 * AP_BK * QS;    // [2][32][HD]
-    float* Ps = Vs + 2 * AP_BK * HD;    // [64][PS]
-    const int G = H / Hkv, QT = AP_BQ / G;
+__global__ void __launch_bounds__(AP_WARPS * 32, 1)
+    attn_prefill_kernel(const float* __restrict__ q, const __half* __restrict__ planes,
+                        float* __restrict__ out, int H, int Hkv, int n_pos, int start, int T,
+                        float scale) {
+    constexpr int LD = ap_ld<HD>(), KS = HD / 16, NT = HD / 8;
+    constexpr int PLANE = AP_BK * LD;  // halves per plane tile
+    extern __shared__ __align__(128) __half apsm[];
+    const int G = H / Hkv, QT = AP_ROWS / G;
     const int hk = blockIdx.y;
     const int q0 = (gridDim.x - 1 - blockIdx.x) * QT;  // the longest rows first
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    for (int i = tid; i < AP_BQ * HD / 4; i += 256) {
-        const int r = i / (HD / 4), c4 = i - r * (HD / 4);
-        const int t = q0 + r % QT;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < T)
-            v = *reinterpret_cast<const float4*>(q + ((size_t)t * H + hk * G + r / QT) * HD + 4 * c4);
-        *reinterpret_cast<float4*>(Qs + r * QS + 4 * c4) = v;
-    }
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, cq = lane & 3;
+    const size_t per = (size_t)Hkv * n_pos * HD;
+    const __half* kh = planes + (size_t)hk * n_pos * HD;
     const int kv_end = start + (q0 + QT < T ? q0 + QT : T);  // positions [0, kv_end)
     const int n_tiles = (kv_end + AP_BK - 1) / AP_BK;
-    const float* kh = kc + (size_t)hk * max_seq * HD;
-    const float* vh = vc + (size_t)hk * max_seq * HD;
-    auto load_kv = [&](int tile, int buf) {
-        for (int i = tid; i < AP_BK * HD / 4; i += 256) {
-            const int rr = i / (HD / 4), c4 = i - rr * (HD / 4);
+    auto load_tile = [&](int tile, int buf) {
+        __half* dst = apsm + (size_t)buf * 4 * PLANE;
+        constexpr int CH = HD / 8;  // 16-byte chunks per row
+        for (int i = tid; i < 4 * AP_BK * CH; i += AP_WARPS * 32) {
+            const int pl = i / (AP_BK * CH), rem = i - pl * AP_BK * CH;
+            const int rr = rem / CH, c8 = rem - rr * CH;
             const int pos = tile * AP_BK + rr;
             const bool valid = pos < kv_end;
-            const size_t off = (size_t)(valid ? pos : 0) * HD + 4 * c4;
-            ap_cp16(Ks + (buf * AP_BK + rr) * QS + 4 * c4, kh + off, valid);
-            ap_cp16(Vs + (buf * AP_BK + rr) * HD + 4 * c4, vh + off, valid);
+            const __half* src = kh + pl * per + (size_t)(valid ? pos : 0) * HD + 8 * c8;
+            ap_cp16(dst + pl * PLANE + rr * LD + 8 * c8, src, valid);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    int qp[4];
-    float m[4], l[4];
-    float4 o[4][OC];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        qp[i] = start + q0 + (ty + 16 * i) % QT;
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-#pragma unroll
-        for (int j = 0; j < OC; ++j) o[i][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // stage the query rows (scaled, split) in stage 1's buffer: hi rows then lo rows
+    {
+        __half* qh = apsm + 4 * PLANE;
+        __half* ql = qh + AP_ROWS * LD;
+        for (int i = tid; i < AP_ROWS * HD / 2; i += AP_WARPS * 32) {
+            const int r = i / (HD / 2), c2 = i - r * (HD / 2);
+            const int t = q0 + r % QT;
+            float2 v = make_float2(0.f, 0.f);
+            if (t < T) v = *reinterpret_cast<const float2*>(q + ((size_t)t * H + hk * G + r / QT) * HD + 2 * c2);
+            uint32_t h, l;
+            split2(v.x * scale, v.y * scale, h, l);
+            *reinterpret_cast<uint32_t*>(qh + r * LD + 2 * c2) = h;
+            *reinterpret_cast<uint32_t*>(ql + r * LD + 2 * c2) = l;
+        }
     }
-    load_kv(0, 0);
+    load_tile(0, 0);
+    __syncthreads();
+    uint32_t qa[KS][4], qb[KS][4];  // this warp's query fragments, hi and lo
+    {
+        const int mat = lane >> 3, rr = lane & 7;
+        const int row = warp * 16 + (mat & 1) * 8 + rr;
+        const uint32_t base = (uint32_t)__cvta_generic_to_shared(apsm + 4 * PLANE);
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const uint32_t off = (uint32_t)((row * LD + kk * 16 + (mat >> 1) * 8) * 2);
+            ldsm_x4(base + off, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+            ldsm_x4(base + AP_ROWS * LD * 2 + off, qb[kk][0], qb[kk][1], qb[kk][2], qb[kk][3]);
+        }
+    }
+    __syncthreads();  // stage 1's buffer is free for K/V
+    // the lane's two rows: r0 = 16 warp + gq, r1 = r0 + 8
+    int qp[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) qp[h] = start + q0 + (warp * 16 + gq + 8 * h) % QT;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    const int row_min = start + q0;  // the smallest query position of the CTA
     for (int tile = 0; tile < n_tiles; ++tile) {
         const int buf = tile & 1;
         if (tile + 1 < n_tiles) {
-            load_kv(tile + 1, buf ^ 1);
+            load_tile(tile + 1, buf ^ 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        const float* Kb = Ks + buf * AP_BK * QS;
-        const float* Vb = Vs + buf * AP_BK * HD;
-        float sc[4][2];
+        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(apsm + (size_t)buf * 4 * PLANE);
+        const int mat = lane >> 3, rr = lane & 7;
+        // S = Q K^T over the tile's 64 positions (8 n-tiles)
+        float sc[8][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = 0.f;
-#pragma unroll 4
-        for (int k = 0; k < HD; k += 4) {
-            float4 qv[4], kv[2];
+        for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (ty + 16 * i) * QS + k);
+        for (int kk = 0; kk < KS; ++kk) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) kv[j] = *reinterpret_cast<const float4*>(Kb + (tx + 16 * j) * QS + k);
+            for (int jp = 0; jp < 4; ++jp) {
+                const int pos = 16 * jp + (mat >> 1) * 8 + rr;
+                const uint32_t off = (uint32_t)((pos * LD + kk * 16 + (mat & 1) * 8) * 2);
+                uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+                ldsm_x4(sb + off, h0, h1, h2, h3);                  // K hi
+                ldsm_x4(sb + PLANE * 2 + off, l0, l1, l2, l3);      // K lo
+                mma16816(sc[2 * jp], qa[kk], h0, h1);
+                mma16816(sc[2 * jp], qa[kk], l0, l1);
+                mma16816(sc[2 * jp], qb[kk], h0, h1);
+                mma16816(sc[2 * jp + 1], qa[kk], h2, h3);
+                mma16816(sc[2 * jp + 1], qa[kk], l2, l3);
+                mma16816(sc[2 * jp + 1], qb[kk], h2, h3);
+            }
+        }
+        // causal mask on tiles that reach past the CTA's smallest query position
+        const int t0 = tile * AP_BK;
+        if (t0 + AP_BK - 1 > row_min) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int j = 0; j < 8; ++j)
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
-                    sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
-                    sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
-                    sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+                for (int e = 0; e < 4; ++e) {
+                    const int kp = t0 + 8 * j + 2 * cq + (e & 1);
+                    if (kp > qp[e >> 1]) sc[j][e] = -INFINITY;
                 }
         }
+        // online softmax of the lane's two rows (quad reductions)
+        float alpha[2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int h = 0; h < 2; ++h) {
             float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int pos = tile * AP_BK + tx + 16 * j;
-                float v = sc[i][j] * scale;
-                if (pos > qp[i] || pos >= kv_end) v = -INFINITY;
-                sc[i][j] = v;
-                mx = fmaxf(mx, v);
-            }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mn = fmaxf(m[i], mx);  // finite: position 0 is in every row's range
-            const float alpha = expf(m[i] - mn);
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fmaxf(sc[j][2 * h], sc[j][2 * h + 1]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m[h], mx);  // finite: position 0 is in every row's range
+            alpha[h] = expf(m[h] - mn);
             float sum = 0.f;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const float pv = expf(sc[i][j] - mn);
-                Ps[(ty + 16 * i) * PS + tx + 16 * j] = pv;
-                sum += pv;
+            for (int j = 0; j < 8; ++j) {
+                sc[j][2 * h] = expf(sc[j][2 * h] - mn);
+                sc[j][2 * h + 1] = expf(sc[j][2 * h + 1] - mn);
+                sum += sc[j][2 * h] + sc[j][2 * h + 1];
             }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            l[i] = l[i] * alpha + sum;
-            m[i] = mn;
-#pragma unroll
-            for (int j = 0; j < OC; ++j) {
-                o[i][j].x *= alpha;
-                o[i][j].y *= alpha;
-                o[i][j].z *= alpha;
-                o[i][j].w *= alpha;
-            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l[h] = l[h] * alpha[h] + sum;
+            m[h] = mn;
         }
-        __syncthreads();
-#pragma unroll 4
-        for (int sp = 0; sp < AP_BK; ++sp) {
-            float4 vv[OC];
 #pragma unroll
-            for (int j = 0; j < OC; ++j) vv[j] = *reinterpret_cast<const float4*>(Vb + sp * HD + 4 * tx + 64 * j);
+        for (int n = 0; n < NT; ++n) {
+            o[n][0] *= alpha[0];
+            o[n][1] *= alpha[0];
+            o[n][2] *= alpha[1];
+            o[n][3] *= alpha[1];
+        }
+        // O += P V: the score accumulators are the A fragments of P (16 positions per step)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float pv = Ps[(ty + 16 * i) * PS + sp];
+        for (int ks = 0; ks < 4; ++ks) {
+            uint32_t ph[4], pl[4];
+            split2(sc[2 * ks][0], sc[2 * ks][1], ph[0], pl[0]);
+            split2(sc[2 * ks][2], sc[2 * ks][3], ph[1], pl[1]);
+            split2(sc[2 * ks + 1][0], sc[2 * ks + 1][1], ph[2], pl[2]);
+            split2(sc[2 * ks + 1][2], sc[2 * ks + 1][3], ph[3], pl[3]);
+            const int pos = 16 * ks + (mat & 1) * 8 + rr;
 #pragma unroll
-                for (int j = 0; j < OC; ++j) {
-                    o[i][j].x = fmaf(pv, vv[j].x, o[i][j].x);
-                    o[i][j].y = fmaf(pv, vv[j].y, o[i][j].y);
-                    o[i][j].z = fmaf(pv, vv[j].z, o[i][j].z);
-                    o[i][j].w = fmaf(pv, vv[j].w, o[i][j].w);
-                }
+            for (int dp = 0; dp < NT / 2; ++dp) {
+                const uint32_t off = (uint32_t)((pos * LD + dp * 16 + (mat >> 1) * 8) * 2);
+                uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+                ldsm_x4_t(sb + PLANE * 4 + off, h0, h1, h2, h3);  // V hi
+                ldsm_x4_t(sb + PLANE * 6 + off, l0, l1, l2, l3);  // V lo
+                mma16816(o[2 * dp], ph, h0, h1);
+                mma16816(o[2 * dp], ph, l0, l1);
+                mma16816(o[2 * dp], pl, h0, h1);
+                mma16816(o[2 * dp + 1], ph, h2, h3);
+                mma16816(o[2 * dp + 1], ph, l2, l3);
+                mma16816(o[2 * dp + 1], pl, h2, h3);
             }
         }
         __syncthreads();  // this buffer is refilled two tiles on
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = ty + 16 * i, t = q0 + r % QT;
+    for (int h = 0; h < 2; ++h) {
+        const int r = warp * 16 + gq + 8 * h, t = q0 + r % QT;
         if (t >= T) continue;
-        const float inv = 1.0f / l[i];
-        float* dst = out + ((size_t)t * H + hk * G + r / QT) * HD + 4 * tx;
+        const float inv = 1.0f / l[h];
+        float* dst = out + ((size_t)t * H + hk * G + r / QT) * HD + 2 * cq;
 #pragma unroll
-        for (int j = 0; j < OC; ++j)
-            *reinterpret_cast<float4*>(dst + 64 * j) =
-                make_float4(o[i][j].x * inv, o[i][j].y * inv, o[i][j].z * inv, o[i][j].w * inv);
+        for (int n = 0; n < NT; ++n)
+            *reinterpret_cast<float2*>(dst + 8 * n) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
     }
 }
 
 bool attention_prefill_ok(int H, int Hkv, int HD) {
     if (Hkv <= 0 || H % Hkv) return false;
     const int G = H / Hkv;
-    return (HD == 64 || HD == 128) && G >= 1 && G <= 64 && AP_BQ % G == 0;
+    return (HD == 64 || HD == 128) && G >= 1 && G <= AP_ROWS && AP_ROWS % G == 0;
 }
 
 template <int HD>
 static int launch_prefill(const float* q, const float* kc, const float* vc, float* out, int H,
                           int Hkv, int max_seq, int start, int T, float scale, cudaStream_t st) {
+    static std::mutex mu;
     static bool attr[64] = {};
     int dev = 0;
     IB_CUDA_CHECK(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
-        IB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)attn_prefill_smem<HD>()));
-        attr[dev] = true;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 64 && !attr[dev]) {
+            IB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)attn_prefill_smem<HD>()));
+            attr[dev] = true;
+        }
     }
-    const int QT = AP_BQ / (H / Hkv);
+    const int n_pos = start + T;
+    const size_t per = (size_t)Hkv * n_pos * HD;
+    void* ws = nullptr;
+    int r;
+    if ((r = workspace_get(WS_ATTN_PLANES, per * 4 * sizeof(__half), &ws))) return r;
+    __half* planes = (__half*)ws;
+    const size_t n4 = per / 4;
+    const int g = (int)((n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16);
+    kv_planes_kernel<<<g, 256, 0, st>>>(kc, vc, planes, Hkv, max_seq, HD, n_pos);
+    IB_LAUNCH_CHECK("kv_planes_kernel");
+    const int QT = AP_ROWS / (H / Hkv);
     const dim3 grid((T + QT - 1) / QT, Hkv);
     IB_REQUIRE(grid.x <= 0x7FFFFFFF && Hkv <= 65535, "attention: too many rows");
-    attn_prefill_kernel<HD><<<grid, 256, attn_prefill_smem<HD>(), st>>>(q, kc, vc, out, H, Hkv,
-                                                                        max_seq, start, T, scale);
+    attn_prefill_kernel<HD><<<grid, AP_WARPS * 32, attn_prefill_smem<HD>(), st>>>(
+        q, planes, out, H, Hkv, n_pos, start, T, scale);
     IB_LAUNCH_CHECK("attn_prefill_kernel");
     return IB_OK;
 }
@@ -883,6 +1005,8 @@ int attention_prefill(const float* q, const float* kc, const float* vc, float* o
                       int HD, int max_seq, int start, int T, float scale, cudaStream_t st) {
     IB_REQUIRE(attention_prefill_ok(H, Hkv, HD), "attention: unsupported shape for the prefill kernel");
     IB_REQUIRE(T > 0 && start >= 0 && start + T <= max_seq, "attention: positions beyond the cache");
+    IB_REQUIRE(((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out) % 16 == 0,
+               "attention: pointers must be 16-byte aligned");
     if (HD == 128) return launch_prefill<128>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
     return launch_prefill<64>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
 }
