@@ -515,6 +515,8 @@ def main():
                          "(one JSON line each) instead of the decode benchmark")
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1: one tensor-parallel model over the N GPUs (the default)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
+                    help="KV cache element type (f32: the reference's cache, the default)")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: N independent replicas instead of one tensor-parallel "
                          "model")
@@ -547,6 +549,8 @@ def main():
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
     m.set_fused(args.decode_path != "separate")
     m.set_persistent(args.decode_path == "persistent")
+    if args.kv == "f16":
+        m.set_kv_type(ib.F16)
     rng = np.random.default_rng(42)
     prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
 
@@ -656,6 +660,7 @@ def main():
     if rank == 0:
         config = workload_config(cfg, args, world, tp)
         config["decode_path"] = m.decode_path()
+        config["kv_cache"] = args.kv
         line = {
             "metric": metric_for(cfg), "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,

@@ -283,6 +283,14 @@ int ib_model_set_persistent(void* model, int enabled);
 int ib_model_decode_path(void* model, int* path);
 /* The stream the model launches on (a cudaStream_t), e.g. for event timing. */
 int ib_model_stream(void* model, void** stream);
+/* KV cache element type of the native runner: IB_TYPE_F32 (the default, the
+ * reference's FP32 cache, src/models/model_cuda.cpp:204-211) or IB_TYPE_F16 (half the
+ * cache bytes per position; K and V rounded to nearest when written, every attention
+ * kernel reads them back as FP32).  On a finalized model the caches are replaced by
+ * empty ones (positions must be prefilled again) and the persistent decode step is
+ * disabled with FP16 (the fused per-operation step runs). */
+int ib_model_set_kv_type(void* model, int type);
+int ib_model_kv_type(void* model, int* type);
 /* Number of kernels one decode step launches. */
 int ib_model_step_kernels(void* model, int* n_kernels);
 /* Bytes of weights held on the device. */

@@ -71,6 +71,8 @@ SIGNATURES = {
     "ib_comm_abort": [_vp],
     "ib_peer_setup_check": [_i, _i, _i, _i, _i, _vp, _vp, _vp, _vp],
     "ib_model_tp_exchange_time": [_vp, _i, _vp],
+    "ib_model_set_kv_type": [_vp, _i],
+    "ib_model_kv_type": [_vp, _vp],
     "ib_comm_allreduce_f32": [_vp, _vp, _i64, _vp],
     "ib_comm_free": [_vp],
     "ib_tp_shard": [_i, _vp, _i64, _i64, _i, _i, _i, _vp],
@@ -594,6 +596,16 @@ class Model:
         p = ctypes.c_int()
         call("ib_model_decode_path", self.h, ctypes.byref(p))
         return {0: "separate", 1: "fused", 2: "persistent"}[p.value]
+
+    def set_kv_type(self, type_: int):
+        """KV cache element type: F32 (default) or F16.  On a finalized model the caches
+        start empty again (prefill before decoding)."""
+        call("ib_model_set_kv_type", self.h, type_)
+
+    def kv_type(self) -> int:
+        t = ctypes.c_int()
+        call("ib_model_kv_type", self.h, ctypes.byref(t))
+        return t.value
 
     def tp_exchange_us(self, rounds: int = 64) -> float:
         """Device time of one exchange round of the fused tensor-parallel step, in

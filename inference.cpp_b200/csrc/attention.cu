@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kv.cuh"
 #include "ops.cuh"
 #include "pdl.cuh"
 #include "slab.cuh"
@@ -176,9 +177,10 @@ __global__ void __launch_bounds__(128) attn_partial_fast_kernel(
     }
 }
 
-// ---- generic partial (any head_dim <= 256, group <= 16) ---------------------------
+// ---- generic partial (any head_dim <= 256, group <= 16; FP32 or FP16 cache) ---------
+template <typename KV>
 __global__ void __launch_bounds__(128) attn_partial_generic_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ q, const KV* __restrict__ kc, const KV* __restrict__ vc,
     float* __restrict__ part, int n_heads, int n_kv_heads, int head_dim, int max_seq, int pos,
     float scale, int n_chunks, const int* __restrict__ pos_dev) {
     pdl_launch_dependents();
@@ -196,16 +198,16 @@ __global__ void __launch_bounds__(128) attn_partial_generic_kernel(
     for (int i = threadIdx.x; i < G * head_dim; i += blockDim.x)
         qs[i] = q[(size_t)(hk * G) * head_dim + i];
     __syncthreads();
-    const float* kh = kc + (size_t)hk * max_seq * head_dim;
-    const float* vh = vc + (size_t)hk * max_seq * head_dim;
+    const KV* kh = kc + (size_t)hk * max_seq * head_dim;
+    const KV* vh = vc + (size_t)hk * max_seq * head_dim;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int s = warp; s < n; s += 4) {
-        const float* kr = kh + (size_t)(s0 + s) * head_dim;
+        const KV* kr = kh + (size_t)(s0 + s) * head_dim;
         float dots[ATT_MAX_GROUP];
 #pragma unroll
         for (int g = 0; g < ATT_MAX_GROUP; ++g) dots[g] = 0.f;
         for (int d = lane; d < head_dim; d += 32) {
-            const float kv = kr[d];
+            const float kv = kv_at(kr, (size_t)d);
 #pragma unroll
             for (int g = 0; g < ATT_MAX_GROUP; ++g)
                 if (g < G) dots[g] = fmaf(qs[g * head_dim + d], kv, dots[g]);
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(128) attn_partial_generic_kernel(
 #pragma unroll
         for (int g = 0; g < ATT_MAX_GROUP; ++g) acc[g] = 0.f;
         for (int s = 0; s < n; ++s) {
-            const float vv = vh[(size_t)(s0 + s) * head_dim + d];
+            const float vv = kv_at(vh, (size_t)(s0 + s) * head_dim + d);
 #pragma unroll
             for (int g = 0; g < ATT_MAX_GROUP; ++g)
                 if (g < G) acc[g] = fmaf(sc[g * CH + s], vv, acc[g]);
@@ -290,11 +292,11 @@ static bool fast_ok(int H, int Hkv, int HD) {
     return HD % 4 == 0 && HD <= 128 && H / Hkv <= 8;
 }
 
-int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
+int attention_decode(const float* q, const void* kc, const void* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st, const int* pos_dev, bool pdl) {
+                     cudaStream_t st, const int* pos_dev, bool pdl, bool kv_half) {
     const int G = H / Hkv;
-    const bool fast = fast_ok(H, Hkv, HD) && ((uintptr_t)q % 16 == 0) &&
+    const bool fast = !kv_half && fast_ok(H, Hkv, HD) && ((uintptr_t)q % 16 == 0) &&
                       ((uintptr_t)kc % 16 == 0) && ((uintptr_t)vc % 16 == 0);
     const int ch = fast ? ATT_CH_FAST : ATT_CH_GENERIC;
     // with pos_dev the grid covers the whole cache and chunks past *pos_dev exit
@@ -303,12 +305,19 @@ int attention_decode(const float* q, const float* kc, const float* vc, float* ou
     if (fast) {
         auto kern = G <= 1 ? attn_partial_fast_kernel<1> : G <= 2 ? attn_partial_fast_kernel<2> :
                     G <= 4 ? attn_partial_fast_kernel<4> : attn_partial_fast_kernel<8>;
-        IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(128), 0, st, pdl, q, kc, vc, part, H, Hkv, HD,
+        IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(128), 0, st, pdl, q, (const float*)kc,
+                                 (const float*)vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks,
+                                 pos_dev));
+    } else if (kv_half) {
+        const size_t smem = (size_t)(G * HD + G * ATT_CH_GENERIC) * sizeof(float);
+        IB_CUDA_CHECK(launch_pdl(attn_partial_generic_kernel<__half>, grid, dim3(128), smem, st,
+                                 pdl, q, (const __half*)kc, (const __half*)vc, part, H, Hkv, HD,
                                  max_seq, pos, scale, n_chunks, pos_dev));
     } else {
         const size_t smem = (size_t)(G * HD + G * ATT_CH_GENERIC) * sizeof(float);
-        IB_CUDA_CHECK(launch_pdl(attn_partial_generic_kernel, grid, dim3(128), smem, st, pdl, q,
-                                 kc, vc, part, H, Hkv, HD, max_seq, pos, scale, n_chunks, pos_dev));
+        IB_CUDA_CHECK(launch_pdl(attn_partial_generic_kernel<float>, grid, dim3(128), smem, st,
+                                 pdl, q, (const float*)kc, (const float*)vc, part, H, Hkv, HD,
+                                 max_seq, pos, scale, n_chunks, pos_dev));
     }
     IB_LAUNCH_CHECK("attention_partial_kernel");
     IB_CUDA_CHECK(launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, pdl, part, out, HD,
@@ -330,9 +339,9 @@ constexpr int ATT_TILE = 64;
 constexpr int ATT_SPLITS = 64;
 constexpr int ATT_WARPS = 8;
 
-template <int GMAX>
+template <int GMAX, typename KV>
 __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ q, const KV* __restrict__ kc, const KV* __restrict__ vc,
     float* __restrict__ part_acc, float2* __restrict__ part_ml, int* __restrict__ counters,
     float* __restrict__ out, uint8_t* __restrict__ slab, int slab_kq, int n_heads, int n_kv_heads,
     int head_dim, int max_seq, float scale, const int* __restrict__ pos_dev) {
@@ -354,8 +363,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     const int nv = head_dim >> 2;  // float4 per row
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pp = lane / LPP, li = lane % LPP;
-    const float4* k4 = reinterpret_cast<const float4*>(kc) + (size_t)hk * max_seq * nv;
-    const float4* v4 = reinterpret_cast<const float4*>(vc) + (size_t)hk * max_seq * nv;
+    const KV* kb = kc + (size_t)hk * max_seq * head_dim;  // element rows; float4 units below
+    const KV* vb = vc + (size_t)hk * max_seq * head_dim;
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 kr[PASSES][NVL], vr[PASSES][NVL];
 #pragma unroll
@@ -372,8 +381,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
             for (int k = 0; k < NVL; ++k) {
                 const int c = li + LPP * k;
                 if (s < n && c < nv && t0 + s >= lo && t0 + s < hi) {
-                    kr[p][k] = __ldg(k4 + (size_t)(t0 + s) * nv + c);
-                    vr[p][k] = __ldg(v4 + (size_t)(t0 + s) * nv + c);
+                    kr[p][k] = kv_at4(kb, (size_t)(t0 + s) * nv + c);
+                    vr[p][k] = kv_at4(vb, (size_t)(t0 + s) * nv + c);
                 }
             }
         }
@@ -387,8 +396,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
             for (int k = 0; k < NVL; ++k) {
                 const int c = li + LPP * k;
                 const bool ok = s < n && c < nv;
-                kr[p][k] = ok ? __ldg(k4 + (size_t)(t0 + s) * nv + c) : z4;
-                vr[p][k] = ok ? __ldg(v4 + (size_t)(t0 + s) * nv + c) : z4;
+                kr[p][k] = ok ? kv_at4(kb, (size_t)(t0 + s) * nv + c) : z4;
+                vr[p][k] = ok ? kv_at4(vb, (size_t)(t0 + s) * nv + c) : z4;
             }
         }
     };
@@ -645,10 +654,10 @@ size_t attention_fused_part_bytes(int H, int HD) {
     return (size_t)H * ATT_SPLITS * ((size_t)HD * 4 + 8) + 256;
 }
 
-int attention_decode_fused(const float* q, const float* kc, const float* vc, float* out,
+int attention_decode_fused(const float* q, const void* kc, const void* vc, float* out,
                            uint8_t* slab, bool slab_kq, int H, int Hkv, int HD, int max_seq,
                            float scale, float* part, int* counters, cudaStream_t st,
-                           const int* pos_dev, bool pdl) {
+                           const int* pos_dev, bool pdl, bool kv_half) {
     IB_REQUIRE(fast_ok(H, Hkv, HD) && pos_dev && counters && part, "fused attention: bad arguments");
     IB_REQUIRE(((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out | (uintptr_t)part) % 16 == 0,
                "fused attention: pointers must be 16-byte aligned");
@@ -660,11 +669,19 @@ int attention_decode_fused(const float* q, const float* kc, const float* vc, flo
     float* part_acc = part;
     float2* part_ml = reinterpret_cast<float2*>(part + (size_t)H * ATT_SPLITS * HD);
     const dim3 grid(Hkv, ATT_SPLITS);
-    auto kern = G <= 1 ? attn_fused_kernel<1> : G <= 2 ? attn_fused_kernel<2> :
-                G <= 4 ? attn_fused_kernel<4> : attn_fused_kernel<8>;
-    IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(ATT_WARPS * 32), 0, st, pdl, q, kc, vc, part_acc, part_ml,
-                             counters, out, slab, slab_kq ? 1 : 0, H, Hkv, HD, max_seq, scale,
-                             pos_dev));
+    if (kv_half) {
+        auto kern = G <= 1 ? attn_fused_kernel<1, __half> : G <= 2 ? attn_fused_kernel<2, __half> :
+                    G <= 4 ? attn_fused_kernel<4, __half> : attn_fused_kernel<8, __half>;
+        IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(ATT_WARPS * 32), 0, st, pdl, q,
+                                 (const __half*)kc, (const __half*)vc, part_acc, part_ml, counters,
+                                 out, slab, slab_kq ? 1 : 0, H, Hkv, HD, max_seq, scale, pos_dev));
+        return IB_OK;
+    }
+    auto kern = G <= 1 ? attn_fused_kernel<1, float> : G <= 2 ? attn_fused_kernel<2, float> :
+                G <= 4 ? attn_fused_kernel<4, float> : attn_fused_kernel<8, float>;
+    IB_CUDA_CHECK(launch_pdl(kern, grid, dim3(ATT_WARPS * 32), 0, st, pdl, q, (const float*)kc,
+                             (const float*)vc, part_acc, part_ml, counters, out, slab,
+                             slab_kq ? 1 : 0, H, Hkv, HD, max_seq, scale, pos_dev));
     return IB_OK;
 }
 
@@ -755,7 +772,8 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
 
 // K and V rows [0, n_pos) of every kv head into FP16 hi/lo planes
 // [n_kv_heads][n_pos][head_dim] (planes: K hi, K lo, V hi, V lo).
-__global__ void kv_planes_kernel(const float* __restrict__ kc, const float* __restrict__ vc,
+template <typename KV>
+__global__ void kv_planes_kernel(const KV* __restrict__ kc, const KV* __restrict__ vc,
                                  __half* __restrict__ planes, int Hkv, int max_seq, int HD,
                                  int n_pos) {
     const size_t per = (size_t)Hkv * n_pos * HD;  // elements per plane
@@ -767,8 +785,8 @@ __global__ void kv_planes_kernel(const float* __restrict__ kc, const float* __re
         const size_t hp = e / HD;  // kv head * n_pos + position
         const int pos = (int)(hp % n_pos), hk = (int)(hp / n_pos);
         const size_t src = ((size_t)hk * max_seq + pos) * HD + d;
-        const float4 k = *reinterpret_cast<const float4*>(kc + src);
-        const float4 v = *reinterpret_cast<const float4*>(vc + src);
+        const float4 k = kv_at4(kc, src / 4);
+        const float4 v = kv_at4(vc, src / 4);
         uint32_t h0, l0, h1, l1;
         split2(k.x, k.y, h0, l0);
         split2(k.z, k.w, h1, l1);
@@ -967,8 +985,9 @@ bool attention_prefill_ok(int H, int Hkv, int HD) {
 }
 
 template <int HD>
-static int launch_prefill(const float* q, const float* kc, const float* vc, float* out, int H,
-                          int Hkv, int max_seq, int start, int T, float scale, cudaStream_t st) {
+static int launch_prefill(const float* q, const void* kc, const void* vc, float* out, int H,
+                          int Hkv, int max_seq, int start, int T, float scale, cudaStream_t st,
+                          bool kv_half) {
     static std::mutex mu;
     static bool attr[64] = {};
     int dev = 0;
@@ -990,7 +1009,12 @@ static int launch_prefill(const float* q, const float* kc, const float* vc, floa
     __half* planes = (__half*)ws;
     const size_t n4 = per / 4;
     const int g = (int)((n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16);
-    kv_planes_kernel<<<g, 256, 0, st>>>(kc, vc, planes, Hkv, max_seq, HD, n_pos);
+    if (kv_half)  // the lo planes come out zero: FP16 values split exactly
+        kv_planes_kernel<<<g, 256, 0, st>>>((const __half*)kc, (const __half*)vc, planes, Hkv,
+                                            max_seq, HD, n_pos);
+    else
+        kv_planes_kernel<<<g, 256, 0, st>>>((const float*)kc, (const float*)vc, planes, Hkv,
+                                            max_seq, HD, n_pos);
     IB_LAUNCH_CHECK("kv_planes_kernel");
     const int QT = AP_ROWS / (H / Hkv);
     const dim3 grid((T + QT - 1) / QT, Hkv);
@@ -1001,14 +1025,16 @@ static int launch_prefill(const float* q, const float* kc, const float* vc, floa
     return IB_OK;
 }
 
-int attention_prefill(const float* q, const float* kc, const float* vc, float* out, int H, int Hkv,
-                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st) {
+int attention_prefill(const float* q, const void* kc, const void* vc, float* out, int H, int Hkv,
+                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st,
+                      bool kv_half) {
     IB_REQUIRE(attention_prefill_ok(H, Hkv, HD), "attention: unsupported shape for the prefill kernel");
     IB_REQUIRE(T > 0 && start >= 0 && start + T <= max_seq, "attention: positions beyond the cache");
     IB_REQUIRE(((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out) % 16 == 0,
                "attention: pointers must be 16-byte aligned");
-    if (HD == 128) return launch_prefill<128>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
-    return launch_prefill<64>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st);
+    if (HD == 128)
+        return launch_prefill<128>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st, kv_half);
+    return launch_prefill<64>(q, kc, vc, out, H, Hkv, max_seq, start, T, scale, st, kv_half);
 }
 
 }  // namespace ib

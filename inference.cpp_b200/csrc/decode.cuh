@@ -90,8 +90,9 @@ struct FusedGemv {
     // ALLRED: y[row] += the sum over the ranks of their rows (tp exchange)
     float* y;
     float* q;  // QKV: segment 0 after RoPE -> q; segment 1 -> kc; segment 2 -> vc
-    float* kc;
+    float* kc;  // FP32, or FP16 (__half) when kv_half
     float* vc;
+    int kv_half;
     const float* rope;  // [max_seq][head_dim / 2][cos, sin]
     const int* pos;     // device position of the token
     int head_dim, max_seq;

@@ -10,6 +10,7 @@
 
 #include "decode.cuh"
 #include "gemv_math.cuh"
+#include "kv.cuh"
 #include "pipeline.cuh"
 #include "slab.cuh"
 
@@ -199,8 +200,9 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
                 p.q[lr] = out;
             } else {
                 const size_t at = ((size_t)(lr / HD) * p.max_seq + ps) * HD + d;
-                if (seg == 1) p.kc[at] = out;
-                else p.vc[at] = out;
+                float* dst = seg == 1 ? p.kc : p.vc;
+                if (p.kv_half) kv_put((__half*)dst, at, out);
+                else dst[at] = out;
             }
         }
     } else if (EPI == EPI_SWIGLU) {

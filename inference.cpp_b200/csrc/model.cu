@@ -355,6 +355,26 @@ static int alloc_f(Model* m, float** p, size_t n) {
     return IB_OK;
 }
 
+// (Re)allocates every layer's K and V cache, zeroed, in the element type kv_f16 selects.
+static int alloc_kv(Model* m) {
+    const auto& c = m->cfg;
+    const size_t n = (size_t)c.n_kv_heads * c.max_seq * m->HD, eb = m->kv_f16 ? 2 : 4;
+    for (auto& L : m->layers) {
+        for (float** p : {&L.kc, &L.vc}) {
+            if (*p) {
+                for (auto& a : m->allocations)
+                    if (a == *p) a = nullptr;
+                IB_CUDA_CHECK(cudaFree(*p));
+                *p = nullptr;
+            }
+            IB_CUDA_CHECK(cudaMalloc(p, n * eb + 16));
+            m->allocations.push_back(*p);
+            IB_CUDA_CHECK(cudaMemsetAsync(*p, 0, n * eb, m->stream));
+        }
+    }
+    return IB_OK;
+}
+
 // The model's device buffers (everything but the tensor-parallel peer memory).
 static int finalize_buffers(Model* m) {
     IB_CUDA_CHECK(cudaSetDevice(m->device));
@@ -381,7 +401,7 @@ static int finalize_buffers(Model* m) {
     const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn, V = c.vocab;
     const int S = c.max_seq;
     // VRAM preflight as the reference does before upload (model_cuda.cpp:243-252)
-    const size_t kv_bytes = (size_t)c.n_layers * 2 * Hkv * (size_t)S * HD * 4;
+    const size_t kv_bytes = (size_t)c.n_layers * 2 * Hkv * (size_t)S * HD * (m->kv_f16 ? 2 : 4);
     size_t free_b = 0, total_b = 0;
     IB_CUDA_CHECK(cudaMemGetInfo(&free_b, &total_b));
     if (kv_bytes + (64ull << 20) > free_b) {
@@ -390,12 +410,9 @@ static int finalize_buffers(Model* m) {
                   " MB is free. Reduce the context length.");
         return IB_ERR_OOM;
     }
-    for (auto& L : m->layers) {
+    {
         int st;
-        if ((st = alloc_f(m, &L.kc, (size_t)Hkv * S * HD))) return st;
-        if ((st = alloc_f(m, &L.vc, (size_t)Hkv * S * HD))) return st;
-        IB_CUDA_CHECK(cudaMemsetAsync(L.kc, 0, (size_t)Hkv * S * HD * 4, m->stream));
-        IB_CUDA_CHECK(cudaMemsetAsync(L.vc, 0, (size_t)Hkv * S * HD * 4, m->stream));
+        if ((st = alloc_kv(m))) return st;
     }
     // RoPE table, computed on the host exactly as model_cuda.cpp:175-187 does
     const int half = HD / 2;
@@ -547,6 +564,7 @@ static FusedGemv fg_qkv(const Model* m, const Layer& L) {
     p.q = m->q;
     p.kc = L.kc;
     p.vc = L.vc;
+    p.kv_half = m->kv_f16 ? 1 : 0;
     p.rope = m->rope_table;
     p.pos = m->dev_i32 + 1;
     p.head_dim = m->HD;
@@ -644,7 +662,9 @@ static bool pair_member_b(int type) {
 int build_step_plan(Model* m) {
     m->persistent_ok = false;
     const auto& c = m->cfg;
-    if (m->tp_size > 1 || !m->fused_ok || c.n_layers < 1 || m->tok.repr != REPR_PACKED) return IB_OK;
+    if (m->tp_size > 1 || !m->fused_ok || m->kv_f16 || c.n_layers < 1 ||
+        m->tok.repr != REPR_PACKED)
+        return IB_OK;
     const int D = c.dim, H = c.n_heads, Hkv = c.n_kv_heads, HD = m->HD, F = c.ffn;
     const bool kq = m->slab_kq;
     const int GS = kq ? 256 : 32, SE = kq ? 2048 : 1024, BE = kq ? 256 : 32;
@@ -834,11 +854,11 @@ static int decode_launches_fused(Model* m) {
         if (att_slab) {  // attention writes the wo input's limb slab itself
             if ((r = attention_decode_fused(m->q, L.kc, L.vc, m->att, m->slab_att, kq, H, Hkv, HD,
                                             c.max_seq, scale, m->att_fpart, m->att_counters, st,
-                                            pos, true)))
+                                            pos, true, m->kv_f16)))
                 return r;
         } else {
             if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
-                                      m->att_part, st, pos, true)))
+                                      m->att_part, st, pos, true, m->kv_f16)))
                 return r;
             if ((r = xq_slab_launch(m->att, nullptr, H * HD, kq, m->slab_att, nullptr, st, true)))
                 return r;
@@ -880,9 +900,11 @@ static int decode_launches(Model* m) {
         if ((r = L.wk.forward(m->xn, m->k, st))) return r;
         if ((r = L.wv.forward(m->xn, m->v, st))) return r;
         if ((r = rope_launch(m->q, m->k, m->rope_table, H, Hkv, HD, 0, 1, st, pos))) return r;
-        if ((r = kv_write_launch(L.kc, L.vc, m->k, m->v, Hkv, HD, c.max_seq, 0, 1, st, pos))) return r;
+        if ((r = kv_write_launch(L.kc, L.vc, m->k, m->v, Hkv, HD, c.max_seq, 0, 1, st, pos,
+                                 m->kv_f16)))
+            return r;
         if ((r = attention_decode(m->q, L.kc, L.vc, m->att, H, Hkv, HD, c.max_seq, 0, scale,
-                                  m->att_part, st, pos)))
+                                  m->att_part, st, pos, false, m->kv_f16)))
             return r;
         if ((r = L.wo.forward(m->att, m->proj, st))) return r;
         if ((r = tp_residual(m, m->x, m->proj, D, st))) return r;
@@ -1000,9 +1022,11 @@ int prefill(Model* m, const int32_t* host_ids, int T, int start, float* host_log
         if ((r = L.wk.forward_batch(m->pf_xn, m->pf_k, T, st))) return r;
         if ((r = L.wv.forward_batch(m->pf_xn, m->pf_v, T, st))) return r;
         if ((r = rope_launch(m->pf_q, m->pf_k, m->rope_table, H, Hkv, HD, start, T, st, nullptr))) return r;
-        if ((r = kv_write_launch(L.kc, L.vc, m->pf_k, m->pf_v, Hkv, HD, c.max_seq, start, T, st, nullptr))) return r;
+        if ((r = kv_write_launch(L.kc, L.vc, m->pf_k, m->pf_v, Hkv, HD, c.max_seq, start, T, st,
+                                 nullptr, m->kv_f16)))
+            return r;
         if ((r = attention_batch_launch(m->pf_q, L.kc, L.vc, m->pf_att, H, Hkv, HD, c.max_seq, start,
-                                        T, scale, st)))
+                                        T, scale, st, m->kv_f16)))
             return r;
         if ((r = L.wo.forward_batch(m->pf_att, m->pf_proj, T, st))) return r;
         if ((r = tp_residual(m, m->pf_x, m->pf_proj, (size_t)T * D, st))) return r;
@@ -1117,6 +1141,33 @@ extern "C" int ib_model_set_fused(void* h, int enabled) {
         cudaGraphExecDestroy(m->graph_exec);
         m->graph_exec = nullptr;
     }
+    return IB_OK;
+}
+
+extern "C" int ib_model_set_kv_type(void* h, int type) {
+    IB_REQUIRE(h, "null model");
+    IB_REQUIRE(type == IB_TYPE_F32 || type == IB_TYPE_F16, "KV cache type must be F32 or F16");
+    Model* m = (Model*)h;
+    const bool f16 = type == IB_TYPE_F16;
+    if (f16 == m->kv_f16) return IB_OK;
+    m->kv_f16 = f16;
+    if (!m->finalized) return IB_OK;
+    // a finalized model: new, empty caches (positions must be prefilled again)
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    if (m->graph_exec) {
+        cudaGraphExecDestroy(m->graph_exec);
+        m->graph_exec = nullptr;
+    }
+    int r = alloc_kv(m);
+    if (r == IB_OK) r = build_step_plan(m);
+    if (r == IB_OK) IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    return r;
+}
+
+extern "C" int ib_model_kv_type(void* h, int* type) {
+    IB_REQUIRE(h && type, "null pointer argument");
+    *type = ((Model*)h)->kv_f16 ? IB_TYPE_F16 : IB_TYPE_F32;
     return IB_OK;
 }
 

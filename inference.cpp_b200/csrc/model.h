@@ -33,7 +33,7 @@ struct Layer {
     Linear wq, wk, wv, wo, w1, w2, w3;
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
-    float* kc = nullptr;  // [Hkv][max_seq][HD]
+    float* kc = nullptr;  // [Hkv][max_seq][HD]: FP32, or __half when Model::kv_f16
     float* vc = nullptr;
 };
 
@@ -57,6 +57,7 @@ struct Model {
     bool has_output = false;
     bool use_graph = true;
     bool use_fused = true;  // fused decode kernels when every weight supports them
+    bool kv_f16 = false;    // the KV cache in FP16 (ib_model_set_kv_type)
     bool fused_ok = false;
     // persistent decode step (step.cu): one kernel per token, single GPU
     bool use_persistent = false;

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "kv.cuh"
 #include "ops.cuh"
 #include "quant.cuh"
 
@@ -116,7 +117,8 @@ __global__ void embedding_f32_kernel(const float* table, const int32_t* ids, int
 }
 
 // ---- KV write: cache [n_heads][max_seq][head_dim] (cuda_kernels.cu:163-176,403-419)
-__global__ void kv_write_kernel(float* kc, float* vc, const float* k, const float* v,
+template <typename KV>
+__global__ void kv_write_kernel(KV* kc, KV* vc, const float* k, const float* v,
                                 int n_heads, int head_dim, int max_seq, int start, int T,
                                 const int* start_dev) {
     const int t = blockIdx.y;
@@ -126,8 +128,8 @@ __global__ void kv_write_kernel(float* kc, float* vc, const float* k, const floa
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int h = i / head_dim, d = i - h * head_dim;
         const int64_t ci = ((int64_t)h * max_seq + start + t) * head_dim + d;
-        kc[ci] = k[(int64_t)t * total + i];
-        vc[ci] = v[(int64_t)t * total + i];
+        kv_put(kc, ci, k[(int64_t)t * total + i]);
+        kv_put(vc, ci, v[(int64_t)t * total + i]);
     }
 }
 
@@ -149,9 +151,10 @@ __global__ void rope_kernel(float* q, float* k, const float* table, int n_heads,
 
 // ---- attention for a batch of query positions (prefill), causal ----------------
 // q, out: [T][H][HD]; grid (H, T); dynamic shared (start+T) floats of scores.
+template <typename KV>
 __global__ void __launch_bounds__(128) attn_batch_kernel(const float* __restrict__ q,
-                                                         const float* __restrict__ kc,
-                                                         const float* __restrict__ vc,
+                                                         const KV* __restrict__ kc,
+                                                         const KV* __restrict__ vc,
                                                          float* __restrict__ out, int n_heads,
                                                          int n_kv_heads, int head_dim,
                                                          int max_seq, int start, int T,
@@ -165,12 +168,13 @@ __global__ void __launch_bounds__(128) attn_batch_kernel(const float* __restrict
     const float* qh = q + ((int64_t)t * n_heads + h) * head_dim;
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) qsh[d] = qh[d];
     __syncthreads();
-    const float* kh = kc + (int64_t)hk * max_seq * head_dim;
-    const float* vh = vc + (int64_t)hk * max_seq * head_dim;
+    const KV* kh = kc + (int64_t)hk * max_seq * head_dim;
+    const KV* vh = vc + (int64_t)hk * max_seq * head_dim;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int s = warp; s < seq; s += 4) {
         float dot = 0.f;
-        for (int d = lane; d < head_dim; d += 32) dot = fmaf(qsh[d], kh[(int64_t)s * head_dim + d], dot);
+        for (int d = lane; d < head_dim; d += 32)
+            dot = fmaf(qsh[d], kv_at(kh, (size_t)s * head_dim + d), dot);
         dot = warp_sum_f(dot);
         if (lane == 0) sc[s] = dot * scale;
     }
@@ -188,7 +192,7 @@ __global__ void __launch_bounds__(128) attn_batch_kernel(const float* __restrict
     const float inv = 1.0f / l;
     for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
         float acc = 0.f;
-        for (int s = 0; s < seq; ++s) acc = fmaf(sc[s], vh[(int64_t)s * head_dim + d], acc);
+        for (int s = 0; s < seq; ++s) acc = fmaf(sc[s], kv_at(vh, (size_t)s * head_dim + d), acc);
         out[((int64_t)t * n_heads + h) * head_dim + d] = acc * inv;
     }
 }
@@ -420,28 +424,38 @@ int rmsnorm_launch(const float* x, const float* w, float* out, int rows, int dim
     return IB_OK;
 }
 
-int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hkv, int HD,
-                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev) {
+int kv_write_launch(void* kc, void* vc, const float* k, const float* v, int Hkv, int HD,
+                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev,
+                    bool kv_half) {
     const int total = Hkv * HD;
-    kv_write_kernel<<<dim3((total + 255) / 256, T), 256, 0, st>>>(kc, vc, k, v, Hkv, HD,
-                                                                  max_seq, start, T, start_dev);
+    const dim3 grid((total + 255) / 256, T);
+    if (kv_half)
+        kv_write_kernel<<<grid, 256, 0, st>>>((__half*)kc, (__half*)vc, k, v, Hkv, HD, max_seq,
+                                              start, T, start_dev);
+    else
+        kv_write_kernel<<<grid, 256, 0, st>>>((float*)kc, (float*)vc, k, v, Hkv, HD, max_seq,
+                                              start, T, start_dev);
     IB_LAUNCH_CHECK("kv_write_kernel");
     return IB_OK;
 }
 
-int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
+int attention_batch_launch(const float* q, const void* kc, const void* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
-                           cudaStream_t st) {
+                           cudaStream_t st, bool kv_half) {
     if (attention_prefill_ok(H, Hkv, HD) && T > 0)
-        return attention_prefill(q, kc, vc, out, H, Hkv, HD, max_seq, start, T, scale, st);
+        return attention_prefill(q, kc, vc, out, H, Hkv, HD, max_seq, start, T, scale, st, kv_half);
     const size_t smem = (size_t)(start + T) * sizeof(float);
+    const void* kern = kv_half ? (const void*)attn_batch_kernel<__half> : (const void*)attn_batch_kernel<float>;
     if (smem > 48 * 1024) {
-        IB_CUDA_CHECK(cudaFuncSetAttribute(attn_batch_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+        IB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)(smem < 200 * 1024 ? 200 * 1024 : smem)));
     }
-    attn_batch_kernel<<<dim3(H, T), 128, smem, st>>>(q, kc, vc, out, H, Hkv, HD, max_seq, start,
-                                                     T, scale);
+    if (kv_half)
+        attn_batch_kernel<<<dim3(H, T), 128, smem, st>>>(q, (const __half*)kc, (const __half*)vc,
+                                                         out, H, Hkv, HD, max_seq, start, T, scale);
+    else
+        attn_batch_kernel<<<dim3(H, T), 128, smem, st>>>(q, (const float*)kc, (const float*)vc,
+                                                         out, H, Hkv, HD, max_seq, start, T, scale);
     IB_LAUNCH_CHECK("attention_batch_kernel");
     return IB_OK;
 }

@@ -14,30 +14,34 @@ size_t attention_partial_bytes(int H, int HD, int pos);
 // at zero; they are left at zero.  part: attention_fused_part_bytes(H, HD).
 bool attention_fused_ok(int H, int Hkv, int HD);
 size_t attention_fused_part_bytes(int H, int HD);
-int attention_decode_fused(const float* q, const float* kc, const float* vc, float* out,
+// kv_half: the cache holds FP16 (kc, vc then point to __half), else FP32.
+int attention_decode_fused(const float* q, const void* kc, const void* vc, float* out,
                            uint8_t* slab, bool slab_kq, int H, int Hkv, int HD, int max_seq,
                            float scale, float* part, int* counters, cudaStream_t st,
-                           const int* pos_dev, bool pdl);
+                           const int* pos_dev, bool pdl, bool kv_half = false);
 int check_attention_args(int H, int Hkv, int HD, int max_seq, int pos);
 // pos_dev != nullptr: the position is read on the device (graph-capturable) and the
 // partial buffer must hold attention_partial_bytes(H, HD, max_seq - 1).
-int attention_decode(const float* q, const float* kc, const float* vc, float* out, int H,
+// kv_half: FP16 cache (the generic partial kernel).
+int attention_decode(const float* q, const void* kc, const void* vc, float* out, int H,
                      int Hkv, int HD, int max_seq, int pos, float scale, float* part,
-                     cudaStream_t st, const int* pos_dev, bool pdl = false);
-// Prefill attention as flash attention over K/V tiles (attention.cu): head_dim 64 or 128,
-// H a multiple of Hkv with H / Hkv dividing 64.
+                     cudaStream_t st, const int* pos_dev, bool pdl = false, bool kv_half = false);
+// Prefill attention as flash attention over K/V tiles on the tensor cores (attention.cu):
+// head_dim 64 or 128, H a multiple of Hkv with H / Hkv dividing 128.
 bool attention_prefill_ok(int H, int Hkv, int HD);
-int attention_prefill(const float* q, const float* kc, const float* vc, float* out, int H, int Hkv,
-                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st);
-int attention_batch_launch(const float* q, const float* kc, const float* vc, float* out, int H,
+int attention_prefill(const float* q, const void* kc, const void* vc, float* out, int H, int Hkv,
+                      int HD, int max_seq, int start, int T, float scale, cudaStream_t st,
+                      bool kv_half = false);
+int attention_batch_launch(const float* q, const void* kc, const void* vc, float* out, int H,
                            int Hkv, int HD, int max_seq, int start, int T, float scale,
-                           cudaStream_t st);
+                           cudaStream_t st, bool kv_half = false);
 int rope_launch(float* q, float* k, const float* table, int H, int Hkv, int HD, int start,
                 int T, cudaStream_t st, const int* start_dev);
 int rmsnorm_launch(const float* x, const float* w, float* out, int rows, int dim, float eps,
                    cudaStream_t st);
-int kv_write_launch(float* kc, float* vc, const float* k, const float* v, int Hkv, int HD,
-                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev);
+int kv_write_launch(void* kc, void* vc, const float* k, const float* v, int Hkv, int HD,
+                    int max_seq, int start, int T, cudaStream_t st, const int* start_dev,
+                    bool kv_half = false);
 int argmax_launch(const float* x, int n, int32_t* out, cudaStream_t st);
 // op: 0 silu(a), 1 a *= b, 2 a += b
 int elementwise_launch(int op, float* a, const float* b, int n, cudaStream_t st);

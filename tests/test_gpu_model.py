@@ -118,6 +118,35 @@ def test_fused_decode_matches_oracle(cuda, port, cfg):
     b.close()
 
 
+FP16_KV_RTOL = 5e-3
+
+
+@pytest.mark.parametrize("cfg", tiny_cfgs() + tma_cfgs(), ids=lambda c: c.name)
+def test_fp16_kv_matches_oracle(cuda, port, cfg):
+    """The FP16 KV cache (ib_model_set_kv_type): fused and separate decode kernels and
+    the prefill kernels reproduce the oracle's greedy tokens, with logits within
+    5e-3 * max|l_ref| (K and V rounded to FP16: a relative 2^-11 per element)."""
+    tensors = synth(cfg, 77)
+    om = port.model(cfg, tensors)
+    prompt = np.array([2, 9, 4, 27, 1, 8], dtype=np.int32) % cfg.vocab
+    n_new = min(24, cfg.ctx - prompt.size)
+    want, want_logits = om.generate(prompt, n_new, want_logits=True)
+    for fused in (True, False):
+        m = ib.Model.from_tensors(cfg, tensors)
+        m.set_kv_type(ib.F16)
+        m.set_fused(fused)
+        assert m.kv_type() == ib.F16 and m.decode_path() != "persistent"
+        assert list(m.generate(prompt, n_new)[0]) == list(want), fused
+        for i in range(1, n_new):
+            tok, p = int(want[prompt.size + i - 1]), prompt.size + i - 1
+            nxt, lg = m.decode(tok, p, want_logits=True)
+            assert nxt == want[prompt.size + i], (fused, i)
+            scale = np.abs(want_logits[i]).max()
+            assert np.abs(lg - want_logits[i]).max() <= FP16_KV_RTOL * scale, (fused, i)
+        assert ib.check_fault() == 0
+        m.close()
+
+
 def test_graph_and_direct_launches_agree(cuda):
     cfg = tiny_cfgs()[1]
     tensors = synth(cfg, 5)

@@ -20,7 +20,9 @@ and prefill kernels the benchmark times, at its widths, inside a model step:
 
 Criteria as in test_gpu_model.py: identical greedy tokens, logits within
 max|l_gpu - l_ref| <= 1e-3 * max|l_ref| per row.  The oracle runs its row and head
-loops on every host core (its results do not depend on the thread count).
+loops on every host core (its results do not depend on the thread count).  The FP16
+KV-cache option is checked at the 8B widths too: identical tokens, logits within
+5e-3 * max|l_ref| (K and V rounded to FP16, a relative 2^-11 per element).
 """
 import dataclasses
 import os
@@ -37,10 +39,13 @@ pytestmark = pytest.mark.gpu
 LOGIT_RTOL = 1e-3
 
 
-def close_logits(a, b):
+FP16_KV_RTOL = 5e-3
+
+
+def close_logits(a, b, rtol=LOGIT_RTOL):
     a, b = np.atleast_2d(a), np.atleast_2d(b)
     scale = np.abs(b).max(axis=1, keepdims=True)
-    return bool(np.all(np.abs(a - b) <= LOGIT_RTOL * scale))
+    return bool(np.all(np.abs(a - b) <= rtol * scale))
 
 
 def synth(cfg, seed):
@@ -55,7 +60,8 @@ def port_mt(port):
     port.set_threads(1)
 
 
-def _greedy_vs_oracle(port, cfg, seed, n_prompt, n_new, prompt_seed):
+def _greedy_vs_oracle(port, cfg, seed, n_prompt, n_new, prompt_seed, kv_type=None,
+                      rtol=LOGIT_RTOL):
     tensors = synth(cfg, seed)
     rng = np.random.default_rng(prompt_seed)
     prompt = rng.integers(1, cfg.vocab, size=n_prompt).astype(np.int32)
@@ -64,16 +70,19 @@ def _greedy_vs_oracle(port, cfg, seed, n_prompt, n_new, prompt_seed):
     del om
     m = ib.Model.from_tensors(cfg, tensors, max_seq=cfg.ctx)
     del tensors
+    if kv_type is not None:
+        m.set_kv_type(kv_type)
+        assert m.kv_type() == kv_type
     assert m.uses_fused()
     got, stats = m.generate(prompt, n_new)
     assert list(got) == list(want)
     # per-step logits of the decode steps, the fused step replayed at each position
     nxt, lg = m.prefill(prompt, 0, want_logits=True)
-    assert nxt == want[n_prompt] and close_logits(lg, want_logits[0])
+    assert nxt == want[n_prompt] and close_logits(lg, want_logits[0], rtol)
     for i in range(1, n_new):
         nxt, lg = m.decode(int(want[n_prompt + i - 1]), n_prompt + i - 1, want_logits=True)
         assert nxt == want[n_prompt + i], i
-        assert close_logits(lg, want_logits[i]), i
+        assert close_logits(lg, want_logits[i], rtol), i
     assert ib.check_fault() == 0
     m.close()
 
@@ -87,6 +96,13 @@ def test_llama3_8b_widths_past_2048_match_oracle(cuda, port_mt):
     """Llama-3-8B widths, 2 layers, decode at positions 2049..2054."""
     cfg = dataclasses.replace(gw.LLAMA3_8B, name="llama-3-8b-2l", n_layers=2, ctx=2064)
     _greedy_vs_oracle(port_mt, cfg, seed=808, n_prompt=2049, n_new=6, prompt_seed=8)
+
+
+def test_llama3_8b_widths_fp16_kv_match_oracle(cuda, port_mt):
+    """The FP16 KV cache at Llama-3-8B widths, 2 layers, decode past position 2048."""
+    cfg = dataclasses.replace(gw.LLAMA3_8B, name="llama-3-8b-2l", n_layers=2, ctx=2064)
+    _greedy_vs_oracle(port_mt, cfg, seed=808, n_prompt=2049, n_new=6, prompt_seed=8,
+                      kv_type=ib.F16, rtol=FP16_KV_RTOL)
 
 
 def test_llama3_70b_widths_match_oracle(cuda, port_mt):
