@@ -405,6 +405,90 @@ def run_reference(args, cfg, world, rank, ib):
     return 0
 
 
+def run_attention(ib, args, cfg):
+    """Decode and prefill attention of the workload's shape timed alone: one JSON line
+    each.  Decode: the step's split kernel (ib_attention_split) at position `prompt`,
+    CUDA-graph replays over 16 distinct FP32 caches (larger than L2 together), against
+    the HBM peak on its K/V bytes.  Prefill: ib_attention_batch over `prompt` tokens
+    from position 0 (the tensor-core kernel), against the measured bf16 peak on its
+    useful flops."""
+    import torch
+    H, Hkv, HD = cfg.n_heads, cfg.n_kv_heads, cfg.dim // cfg.n_heads
+    P = args.prompt
+    S = P + 16
+    peak, peak_kind = measured_peaks()
+    tpeak, tpeak_kind = measured_tensor_peak()
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    n = 16
+    q = torch.randn(H * HD, device="cuda", generator=gen)
+    kcs = [torch.randn(Hkv * S * HD, device="cuda", generator=gen) * 0.5 for _ in range(n)]
+    vcs = [torch.randn(Hkv * S * HD, device="cuda", generator=gen) for _ in range(n)]
+    out = torch.empty(H * HD, device="cuda")
+    part = torch.empty(ib.attention_split_part_bytes(H, HD) // 4 + 64, device="cuda")
+    cnt = torch.zeros(Hkv + 16, dtype=torch.int32, device="cuda")
+    pd = torch.tensor([P], dtype=torch.int32, device="cuda")
+    scale = 1.0 / HD ** 0.5
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(n):
+            ib.attention_split(q, kcs[i], vcs[i], out, H, Hkv, HD, S, pd, scale, part, cnt, stream=s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(n):
+            ib.attention_split(q, kcs[i], vcs[i], out, H, Hkv, HD, S, pd, scale, part, cnt, stream=s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    with torch.cuda.stream(s):
+        g.replay()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("attention_decode")
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+    kv_bytes = 2 * Hkv * (P + 1) * HD * 4
+    print(json.dumps({"op": "attention_decode", "kernel": "attn_fused_kernel", "workload": cfg.name,
+                      "position": P, "heads": [H, Hkv, HD], "us": us, "kv_bytes": kv_bytes,
+                      "achieved_gbs": kv_bytes / (us * 1e-6) / 1e9, "peak": peak,
+                      "frac": kv_bytes / (us * 1e-6) / 1e9 / peak, "peak_kind": peak_kind,
+                      "timing": f"graph replays of {n} launches over distinct caches, no PDL"}),
+          flush=True)
+    del g, kcs, vcs
+    # prefill: T = P query rows against positions 0..P-1
+    T = P
+    qb = torch.randn(T * H * HD, device="cuda", generator=gen)
+    kc = torch.randn(Hkv * T * HD, device="cuda", generator=gen) * 0.5
+    vc = torch.randn(Hkv * T * HD, device="cuda", generator=gen)
+    ob = torch.empty(T * H * HD, device="cuda")
+    for _ in range(3):
+        ib.attention_batch(qb, kc, vc, ob, H, Hkv, HD, T, 0, T, scale)
+    torch.cuda.synchronize()
+    runs = []
+    for _ in range(5):
+        torch.cuda.nvtx.range_push("attention_prefill")
+        e0.record()
+        ib.attention_batch(qb, kc, vc, ob, H, Hkv, HD, T, 0, T, scale)
+        e1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        runs.append(e0.elapsed_time(e1))
+    ms = sorted(runs)[2]
+    flops = 4.0 * H * HD * T * (T + 1) / 2
+    print(json.dumps({"op": "attention_prefill", "kernel": "kv_planes_kernel + attn_prefill_kernel",
+                      "workload": cfg.name, "tokens": T, "heads": [H, Hkv, HD], "ms": ms,
+                      "tflops": flops / (ms * 1e-3) / 1e12, "peak": tpeak, "peak_kind": tpeak_kind,
+                      "frac": flops / (ms * 1e-3) / 1e12 / tpeak,
+                      "note": "useful flops 4*H*HD*T*(T+1)/2 (causal); the kernel issues 3 fp16 "
+                              "mma.sync per product (hi/lo operand pairs)",
+                      "timing": "median of 5 after 3 warm-ups"}), flush=True)
+    return 0
+
+
 def run_sweep(ib, args):
     """Per-format decode GEMV and dequantisation GB/s over the op-sweep shapes, with the
     reference's own CPU dequantisation and matvec (oracle/_ref, one thread) on the
@@ -513,6 +597,9 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="per-format GEMV / dequantisation GB/s over the op-sweep shapes "
                          "(one JSON line each) instead of the decode benchmark")
+    ap.add_argument("--attention", action="store_true",
+                    help="decode and prefill attention of the workload's shape timed alone "
+                         "(one JSON line each) instead of the decode benchmark")
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1: one tensor-parallel model over the N GPUs (the default)")
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
@@ -544,6 +631,8 @@ def main():
     ib.init(local)
     if args.sweep:
         return run_sweep(ib, args) if rank == 0 else 0
+    if args.attention:
+        return run_attention(ib, args, cfg) if rank == 0 else 0
     tp = world > 1 and not args.replicas
     comm = make_comm(ib, world, rank, local) if tp else None
     m = build_model(ib, cfg, args.prompt, args.steps, args.warmup, local, comm=comm)
