@@ -146,7 +146,10 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
     __shared__ __align__(8) uint64_t full[TM_STAGES], empty[TM_STAGES], acc_full;
     __shared__ uint32_t tmem_base;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * TM_M, n0 = blockIdx.y * TM_N;
+    // token tiles vary fastest: the CTAs resident together share weight strips (each
+    // strip's planes come from DRAM once and serve every token tile from L2), and the
+    // X planes (2 x T x cols x 2 bytes) stay in L2
+    const int n0 = blockIdx.x * TM_N, m0 = blockIdx.y * TM_M;
     const int n_k = cols / TM_BK;
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     if (threadIdx.x == 0) {
@@ -287,8 +290,8 @@ static int planes_for(const void* W, __half* Wh, __half* Wl, int64_t rows, int64
 
 bool gemm_planes_supported(int type, int64_t T, int64_t rows, int64_t cols) {
     return is_block_quant(type) && T >= 1 && rows >= 1 && cols % TM_BK == 0 &&
-           T * cols < (1ll << 31) && rows * cols < (1ll << 34) && rows < (1 << 30) &&
-           (T + TM_N - 1) / TM_N <= 65535;
+           T * cols < (1ll << 31) && rows * cols < (1ll << 34) &&
+           (rows + TM_M - 1) / TM_M <= 65535;
 }
 
 int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
@@ -338,7 +341,7 @@ int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int 
             attr_set[dev] = true;
         }
     }
-    const dim3 grid((rows + TM_M - 1) / TM_M, (T + TM_N - 1) / TM_N);
+    const dim3 grid((T + TM_N - 1) / TM_N, (rows + TM_M - 1) / TM_M);
     gemm_planes_kernel<<<grid, TM_THREADS, TM_SMEM, st>>>(mWh, mWl, mXh, mXl, Y, T, rows, cols);
     IB_LAUNCH_CHECK("gemm_planes_kernel");
     return IB_OK;
