@@ -274,9 +274,23 @@ def time_gemm(ib, cfg, T, seed=20261201):
     ib.gemm_q(t, W, X, T, rows, cols, Y=Y)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
+    # the same product on weights decoded once (ib_gemm_prepare_planes): the X split and
+    # the tcgen05 kernel, without the per-call weight decoding
+    planes_ms = None
+    if T >= 128 and cols % 32 == 0:
+        P = ib.gemm_prepare_planes(t, W, rows, cols)
+        ib.gemm_planes(P, X, T, rows, cols, Y=Y)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            ib.gemm_planes(P, X, T, rows, cols, Y=Y)
+        e1.record(s)
+        torch.cuda.synchronize()
+        planes_ms = e0.elapsed_time(e1) / reps
+        del P
     del W, X, Y
     torch.cuda.empty_cache()
-    return 2.0 * T * rows * cols, ms
+    return 2.0 * T * rows * cols, ms, planes_ms
 
 
 def measured_tensor_peak():
@@ -604,6 +618,9 @@ def main():
                     help="with N > 1: one tensor-parallel model over the N GPUs (the default)")
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
                     help="KV cache element type (f32: the reference's cache, the default)")
+    ap.add_argument("--prefill-planes", action="store_true",
+                    help="keep the weights decoded as FP16 planes for the prompt GEMMs "
+                         "(ib_model_set_prefill_planes; 4 bytes per weight)")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: N independent replicas instead of one tensor-parallel "
                          "model")
@@ -640,6 +657,8 @@ def main():
     m.set_persistent(args.decode_path == "persistent")
     if args.kv == "f16":
         m.set_kv_type(ib.F16)
+    if args.prefill_planes:
+        m.set_prefill_planes(True)
     rng = np.random.default_rng(42)
     prompt = rng.integers(1, cfg.vocab, size=args.prompt).astype(np.int32)
 
@@ -728,7 +747,7 @@ def main():
                               "plus the receiving slab kernel), max over ranks; in the step "
                               "the push is the row-split GEMV's epilogue"}
     nbytes, gemv_ms, gemv_solo_ms, gemv_reps = time_gemv(ib, cfg)
-    gemm_flops, gemm_ms = time_gemm(ib, cfg, args.prompt)
+    gemm_flops, gemm_ms, gemm_planes_ms = time_gemm(ib, cfg, args.prompt)
     tpeak, tpeak_kind = measured_tensor_peak()
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (gemv_ms * 1e-3) / 1e9
@@ -750,6 +769,7 @@ def main():
         config = workload_config(cfg, args, world, tp)
         config["decode_path"] = m.decode_path()
         config["kv_cache"] = args.kv
+        config["prefill_planes"] = bool(args.prefill_planes)
         line = {
             "metric": metric_for(cfg), "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
@@ -778,8 +798,16 @@ def main():
                                  "ms": gemm_ms, "tflops": gemm_flops / (gemm_ms * 1e-3) / 1e12,
                                  "peak": tpeak, "peak_kind": tpeak_kind,
                                  "frac": gemm_flops / (gemm_ms * 1e-3) / 1e12 / tpeak,
-                                 "note": "useful flops 2*T*rows*cols; the kernel issues 3 fp16 "
-                                         "MMAs per product (hi/lo operand pairs)"}},
+                                 "prepared_weights": None if gemm_planes_ms is None else {
+                                     "ms": gemm_planes_ms,
+                                     "tflops": gemm_flops / (gemm_planes_ms * 1e-3) / 1e12,
+                                     "frac": gemm_flops / (gemm_planes_ms * 1e-3) / 1e12 / tpeak,
+                                     "note": "ib_gemm_planes on weights decoded once "
+                                             "(ib_gemm_prepare_planes): X split + the tcgen05 "
+                                             "kernel"},
+                                 "note": "useful flops 2*T*rows*cols; the call decodes the "
+                                         "weights into FP16 hi/lo planes, splits X, and the "
+                                         "kernel issues 3 fp16 MMAs per product"}},
             "cpu_baseline": cpu,
             "exchange": exchange,
             "clocks": clk,

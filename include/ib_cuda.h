@@ -150,6 +150,16 @@ int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float* dev_Y, int
  *   3  the planes kernel where it applies
  * No counterpart in the reference. */
 int ib_gemm_set_path(int path);
+/* Prepared weights for repeated prompt GEMMs: the packed [rows, cols] weights decoded
+ * once (bit-exact values) into FP16 hi/lo planes of ib_gemm_planes_bytes(rows, cols)
+ * bytes (4 per weight) at a 16-byte aligned dev_planes, then Y[T, rows] = X Wᵀ on them
+ * with the tcgen05 kernel of ib_gemm_q's automatic path (same result bit for bit, without
+ * the per-call decoding).  cols % 32 == 0. */
+size_t ib_gemm_planes_bytes(int64_t rows, int64_t cols);
+int ib_gemm_prepare_planes(int type, const void* dev_W, int64_t rows, int64_t cols,
+                           void* dev_planes, void* stream);
+int ib_gemm_planes(const void* dev_planes, const float* dev_X, float* dev_Y, int64_t T,
+                   int64_t rows, int64_t cols, void* stream);
 
 /* Embedding gather with dequantisation: out[t, :] = dequant(table[ids[t], :]).
  * Replaces embedding / embedding_batch (include/ops/cuda_backend.hpp:44-50) for a
@@ -290,6 +300,11 @@ int ib_model_stream(void* model, void** stream);
  * empty ones (positions must be prefilled again) and the persistent decode step is
  * disabled with FP16 (the fused per-operation step runs). */
 int ib_model_set_kv_type(void* model, int type);
+/* enabled != 0: keep every packed linear of the layers decoded once as FP16 hi/lo planes
+ * (ib_gemm_prepare_planes; 4 bytes per weight, 28 GB for the Llama-3-8B shape) so prompt
+ * GEMMs of 128 tokens and more skip the per-call decoding (same results); IB_ERR_OOM
+ * when they do not fit.  0 releases them.  On a finalized model. */
+int ib_model_set_prefill_planes(void* model, int enabled);
 int ib_model_kv_type(void* model, int* type);
 /* Number of kernels one decode step launches. */
 int ib_model_step_kernels(void* model, int* n_kernels);

@@ -78,6 +78,10 @@ SIGNATURES = {
     "ib_tp_shard": [_i, _vp, _i64, _i64, _i, _i, _i, _vp],
     "ib_gemm_q": [_i, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ib_gemm_set_path": [_i],
+    "ib_gemm_planes_bytes": [_i64, _i64],
+    "ib_gemm_prepare_planes": [_i, _vp, _i64, _i64, _vp, _vp],
+    "ib_gemm_planes": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ib_model_set_prefill_planes": [_vp, _i],
     "ib_embedding_q": [_i, _vp, _vp, _vp, _i, _i64, _i64, _vp],
     "ib_gemv": [_vp, _vp, _vp, _i, _i, _vp],
     "ib_gemv_i16": [_vp, _vp, _vp, _vp, _i, _i, _vp],
@@ -104,7 +108,8 @@ SIGNATURES = {
     "ib_synth_device": [_i, _i64, _i64, _u64, _f, _vp, _vp],
     "ib_synth_values_host": [_i64, _u64, _f, _vp],
 }
-_RESTYPE = {"ib_last_error": _c.c_char_p, "ib_attention_split_part_bytes": _c.c_size_t}
+_RESTYPE = {"ib_last_error": _c.c_char_p, "ib_attention_split_part_bytes": _c.c_size_t,
+            "ib_gemm_planes_bytes": _c.c_size_t}
 
 _lib = None
 
@@ -318,6 +323,23 @@ def peer_setup_check(rank: int, world: int, gather, local_status: int = 0, fail_
                                    ctypes.cast(fn, ctypes.c_void_p), None, ctypes.byref(opened),
                                    ctypes.byref(closed))
     return rc, (last_error() if rc else ""), opened.value, closed.value
+
+
+def gemm_prepare_planes(type_: int, W, rows: int, cols: int, stream=None):
+    """The packed weights decoded once into FP16 hi/lo planes (a uint8 CUDA tensor of
+    ib_gemm_planes_bytes bytes) for gemm_planes."""
+    import torch
+    P = torch.empty(lib().ib_gemm_planes_bytes(rows, cols), dtype=torch.uint8, device="cuda")
+    call("ib_gemm_prepare_planes", type_, _ptr(W), rows, cols, _ptr(P), _stream(stream))
+    return P
+
+
+def gemm_planes(P, X, T: int, rows: int, cols: int, Y=None, stream=None):
+    import torch
+    if Y is None:
+        Y = torch.empty(T * rows, dtype=torch.float32, device="cuda")
+    call("ib_gemm_planes", _ptr(P), _ptr(X), _ptr(Y), T, rows, cols, _stream(stream))
+    return Y
 
 
 def gemm_q(type_: int, W, X, T: int, rows: int, cols: int, Y=None, stream=None):
@@ -596,6 +618,11 @@ class Model:
         p = ctypes.c_int()
         call("ib_model_decode_path", self.h, ctypes.byref(p))
         return {0: "separate", 1: "fused", 2: "persistent"}[p.value]
+
+    def set_prefill_planes(self, enabled: bool):
+        """Keep every packed linear's weights decoded as FP16 hi/lo planes (4 bytes per
+        weight) for the prompt GEMMs, or release them."""
+        call("ib_model_set_prefill_planes", self.h, 1 if enabled else 0)
 
     def set_kv_type(self, type_: int):
         """KV cache element type: F32 (default) or F16.  On a finalized model the caches

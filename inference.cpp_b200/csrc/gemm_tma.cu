@@ -294,32 +294,37 @@ bool gemm_planes_supported(int type, int64_t T, int64_t rows, int64_t cols) {
            (rows + TM_M - 1) / TM_M <= 65535;
 }
 
-int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
-                  cudaStream_t st) {
-    IB_REQUIRE(gemm_planes_supported(type, T, rows, cols), "gemm: shape not supported by the planes kernel");
+int gemm_decode_planes(int type, const void* W, void* planes, int64_t rows, int64_t cols,
+                       cudaStream_t st) {
+    __half* Wh = (__half*)planes;
+    __half* Wl = Wh + (size_t)rows * cols;
+    switch (type) {
+        case IB_TYPE_Q4_0: return planes_for<IB_TYPE_Q4_0>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q5_0: return planes_for<IB_TYPE_Q5_0>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q5_1: return planes_for<IB_TYPE_Q5_1>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q8_0: return planes_for<IB_TYPE_Q8_0>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q4_K: return planes_for<IB_TYPE_Q4_K>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q6_K: return planes_for<IB_TYPE_Q6_K>(W, Wh, Wl, rows, cols, st);
+    }
+    set_error("gemm: unsupported type");
+    return IB_ERR_UNSUPPORTED;
+}
+
+int gemm_on_planes(const void* planes, const float* X, float* Y, int T, int rows, int cols,
+                   cudaStream_t st) {
+    IB_REQUIRE(planes && ((uintptr_t)planes & 15) == 0, "gemm: weight planes must be 16-byte aligned");
+    IB_REQUIRE(T >= 1 && rows >= 1 && cols % TM_BK == 0 && (int64_t)T * cols < (1ll << 31) &&
+                   (int64_t)rows * cols < (1ll << 34) && (rows + TM_M - 1) / TM_M <= 65535,
+               "gemm: shape not supported by the planes kernel");
     const size_t nx = (size_t)T * cols, nw = (size_t)rows * cols;
     void* wsx = nullptr;
-    void* wsw = nullptr;
     int r = workspace_get(WS_GEMM, 2 * nx * sizeof(__half) + 256, &wsx);
     if (r) return r;
-    if ((r = workspace_get(WS_GEMM_W, 2 * nw * sizeof(__half) + 256, &wsw))) return r;
     __half* Xh = (__half*)wsx;
     __half* Xl = Xh + nx;
-    __half* Wh = (__half*)wsw;
-    __half* Wl = Wh + nw;
+    const __half* Wh = (const __half*)planes;
+    const __half* Wl = Wh + nw;
     if ((r = gemm_split_x(X, Xh, Xl, nx, st))) return r;
-    switch (type) {
-        case IB_TYPE_Q4_0: r = planes_for<IB_TYPE_Q4_0>(W, Wh, Wl, rows, cols, st); break;
-        case IB_TYPE_Q5_0: r = planes_for<IB_TYPE_Q5_0>(W, Wh, Wl, rows, cols, st); break;
-        case IB_TYPE_Q5_1: r = planes_for<IB_TYPE_Q5_1>(W, Wh, Wl, rows, cols, st); break;
-        case IB_TYPE_Q8_0: r = planes_for<IB_TYPE_Q8_0>(W, Wh, Wl, rows, cols, st); break;
-        case IB_TYPE_Q4_K: r = planes_for<IB_TYPE_Q4_K>(W, Wh, Wl, rows, cols, st); break;
-        case IB_TYPE_Q6_K: r = planes_for<IB_TYPE_Q6_K>(W, Wh, Wl, rows, cols, st); break;
-        default:
-            set_error("gemm: unsupported type");
-            return IB_ERR_UNSUPPORTED;
-    }
-    if (r) return r;
     CUtensorMap mWh, mWl, mXh, mXl;
     if ((r = tensor_map_2d(&mWh, Wh, cols, rows, TM_M))) return r;
     if ((r = tensor_map_2d(&mWl, Wl, cols, rows, TM_M))) return r;
@@ -347,6 +352,17 @@ int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int 
     return IB_OK;
 }
 
+int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
+                  cudaStream_t st) {
+    IB_REQUIRE(gemm_planes_supported(type, T, rows, cols), "gemm: shape not supported by the planes kernel");
+    const size_t nw = (size_t)rows * cols;
+    void* wsw = nullptr;
+    int r = workspace_get(WS_GEMM_W, 2 * nw * sizeof(__half) + 256, &wsw);
+    if (r) return r;
+    if ((r = gemm_decode_planes(type, W, wsw, rows, cols, st))) return r;
+    return gemm_on_planes(wsw, X, Y, T, rows, cols, st);
+}
+
 int gemm_planes_fault_take(int* code) {
     int v = 0, z = 0;
     IB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_gemm_tma_fault, sizeof(int)));
@@ -356,3 +372,28 @@ int gemm_planes_fault_take(int* code) {
 }
 
 }  // namespace ib
+
+using namespace ib;
+
+extern "C" size_t ib_gemm_planes_bytes(int64_t rows, int64_t cols) {
+    return rows > 0 && cols > 0 ? (size_t)rows * cols * 4 : 0;
+}
+
+extern "C" int ib_gemm_prepare_planes(int type, const void* dev_W, int64_t rows, int64_t cols,
+                                      void* dev_planes, void* stream) {
+    IB_REQUIRE(dev_W && dev_planes && rows > 0 && cols > 0, "bad arguments");
+    IB_REQUIRE(gemm_planes_supported(type, 1, rows, cols), "gemm: shape not supported by the planes kernel");
+    IB_REQUIRE(((uintptr_t)dev_planes & 15) == 0, "gemm: weight planes must be 16-byte aligned");
+    return gemm_decode_planes(type, dev_W, dev_planes, rows, cols, as_stream(stream));
+}
+
+extern "C" int ib_gemm_planes(const void* dev_planes, const float* dev_X, float* dev_Y, int64_t T,
+                              int64_t rows, int64_t cols, void* stream) {
+    IB_REQUIRE(dev_planes && dev_X && dev_Y, "null pointer argument");
+    if (T == 0 || rows == 0) return IB_OK;
+    IB_REQUIRE(T > 0 && rows > 0 && cols > 0 && T < (1ll << 31) && rows < (1ll << 31) &&
+                   cols < (1ll << 31),
+               "bad shape");
+    return gemm_on_planes(dev_planes, dev_X, dev_Y, (int)T, (int)rows, (int)cols,
+                          as_stream(stream));
+}

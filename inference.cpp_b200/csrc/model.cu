@@ -109,7 +109,10 @@ int Linear::forward(const float* x, float* y, cudaStream_t st) const {
 
 int Linear::forward_batch(const float* X, float* Y, int T, cudaStream_t st) const {
     switch (repr) {
-        case REPR_PACKED: return ib_gemm_q(type, w, X, Y, T, rows, cols, st);
+        case REPR_PACKED:
+            // prepared planes: the automatic path's kernel for prompts of 128 tokens and more
+            if (planes && T >= 128) return gemm_on_planes(planes, X, Y, T, (int)rows, (int)cols, st);
+            return ib_gemm_q(type, w, X, Y, T, rows, cols, st);
         case REPR_I16: return ib_gemm_i16(q, s, X, Y, T, (int)rows, (int)cols, st);
         case REPR_F32: return ib_gemm(f, X, Y, T, (int)rows, (int)cols, st);
     }
@@ -117,6 +120,8 @@ int Linear::forward_batch(const float* X, float* Y, int T, cudaStream_t st) cons
 }
 
 void Linear::release() {
+    if (planes) cudaFree(planes);
+    planes = nullptr;
     if (w) cudaFree(w);
     if (q) cudaFree(q);
     if (s) cudaFree(s);
@@ -1141,6 +1146,46 @@ extern "C" int ib_model_set_fused(void* h, int enabled) {
         cudaGraphExecDestroy(m->graph_exec);
         m->graph_exec = nullptr;
     }
+    return IB_OK;
+}
+
+extern "C" int ib_model_set_prefill_planes(void* h, int enabled) {
+    IB_REQUIRE(h, "null model");
+    Model* m = (Model*)h;
+    IB_REQUIRE(m->finalized, "prefill planes: finalize the model first");
+    IB_CUDA_CHECK(cudaSetDevice(m->device));
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
+    std::vector<Linear*> lins;
+    for (auto& L : m->layers)
+        for (Linear* l : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w2, &L.w3}) lins.push_back(l);
+    if (!enabled) {
+        for (Linear* l : lins)
+            if (l->planes) {
+                cudaFree(l->planes);
+                l->planes = nullptr;
+            }
+        return IB_OK;
+    }
+    size_t need = 0;
+    for (Linear* l : lins)
+        if (l->repr == REPR_PACKED && !l->planes && gemm_planes_supported(l->type, 128, l->rows, l->cols))
+            need += (size_t)l->rows * l->cols * 4 + 16;
+    size_t free_b = 0, total_b = 0;
+    IB_CUDA_CHECK(cudaMemGetInfo(&free_b, &total_b));
+    if (need + (1ull << 30) > free_b) {
+        set_error("prefill planes: need ~" + std::to_string(need >> 20) + " MB but only " +
+                  std::to_string(free_b >> 20) + " MB is free");
+        return IB_ERR_OOM;
+    }
+    for (Linear* l : lins) {
+        if (l->repr != REPR_PACKED || l->planes ||
+            !gemm_planes_supported(l->type, 128, l->rows, l->cols))
+            continue;
+        IB_CUDA_CHECK(cudaMalloc(&l->planes, (size_t)l->rows * l->cols * 4 + 16));
+        int r = gemm_decode_planes(l->type, l->w, l->planes, l->rows, l->cols, m->stream);
+        if (r) return r;
+    }
+    IB_CUDA_CHECK(cudaStreamSynchronize(m->stream));
     return IB_OK;
 }
 

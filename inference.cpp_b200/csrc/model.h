@@ -24,6 +24,7 @@ struct Linear {
     int16_t* q = nullptr;    // INT16 values
     float* s = nullptr;      // INT16 row scales
     float* f = nullptr;      // FP32 values
+    void* planes = nullptr;  // PACKED, optional: the weights as FP16 hi/lo planes (prefill)
     int forward(const float* x, float* y, cudaStream_t st) const;
     int forward_batch(const float* X, float* Y, int T, cudaStream_t st) const;
     void release();

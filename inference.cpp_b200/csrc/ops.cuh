@@ -54,6 +54,12 @@ bool gemm_planes_supported(int type, int64_t T, int64_t rows, int64_t cols);
 int gemm_q_planes(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
                   cudaStream_t st);
 int gemm_planes_fault_take(int* code);
+// The weights decoded once into FP16 hi/lo planes (4 bytes per weight: hi [rows][cols]
+// then lo), and the GEMM on such planes.
+int gemm_decode_planes(int type, const void* W, void* planes, int64_t rows, int64_t cols,
+                       cudaStream_t st);
+int gemm_on_planes(const void* planes, const float* X, float* Y, int T, int rows, int cols,
+                   cudaStream_t st);
 int gemm_q_tc(int type, const void* W, const float* X, float* Y, int T, int rows, int cols,
               cudaStream_t st);
 int gemm_fault_take(int* code);

@@ -79,6 +79,10 @@ def test_new_entry_points_validate_without_gpu():
     assert L.ib_gemv_q_slab_chained(ib.Q4_K, None, None, None, 4, 256, None) == 1
     assert L.ib_attention_split_part_bytes(32, 128) == 32 * 64 * (128 * 4 + 8) + 256
     assert L.ib_attention_split_part_bytes(0, 128) == 0
+    assert L.ib_gemm_planes_bytes(300, 2048) == 300 * 2048 * 4
+    assert L.ib_gemm_planes_bytes(0, 2048) == 0
+    assert L.ib_gemm_planes(None, None, None, 4, 8, 64, None) == 1
+    assert L.ib_gemm_prepare_planes(ib.Q4_K, None, 8, 256, None, None) == 1
     assert L.ib_attention_split(None, None, None, None, 32, 8, 128, 16, None, 1.0, None, None,
                                 None) == 1
     assert "null pointer" in ib.last_error()

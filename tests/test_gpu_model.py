@@ -121,6 +121,25 @@ def test_fused_decode_matches_oracle(cuda, port, cfg):
 FP16_KV_RTOL = 5e-3
 
 
+def test_prefill_planes_give_identical_results(cuda):
+    """Weights kept as decoded planes for the prompt GEMMs (ib_model_set_prefill_planes)
+    change nothing: the prompt's logits are bit-identical, and releasing them again too."""
+    cfg = tma_cfgs()[0]
+    tensors = synth(cfg, 31)
+    m = ib.Model.from_tensors(cfg, tensors, max_seq=160)
+    prompt = (np.arange(140, dtype=np.int32) * 7 + 3) % cfg.vocab  # >= 128: the planes path
+    n0, l0 = m.prefill(prompt, 0, want_logits=True)
+    m.set_prefill_planes(True)
+    n1, l1 = m.prefill(prompt, 0, want_logits=True)
+    m.set_prefill_planes(False)
+    n2, l2 = m.prefill(prompt, 0, want_logits=True)
+    assert n0 == n1 == n2
+    assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+    assert np.array_equal(l0.view(np.uint32), l2.view(np.uint32))
+    assert ib.check_fault() == 0
+    m.close()
+
+
 @pytest.mark.parametrize("cfg", tiny_cfgs() + tma_cfgs(), ids=lambda c: c.name)
 def test_fp16_kv_matches_oracle(cuda, port, cfg):
     """The FP16 KV cache (ib_model_set_kv_type): fused and separate decode kernels and

@@ -157,6 +157,26 @@ def test_gemm_q_paths_vs_oracle(cuda, port, type_, path):
 
 
 @pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
+def test_gemm_on_prepared_planes_matches_gemm_q(cuda, type_):
+    """ib_gemm_planes on weights decoded once (ib_gemm_prepare_planes) gives ib_gemm_q's
+    planes-path result bit for bit, at every prompt length (short ones included)."""
+    rng = np.random.default_rng(900 + type_)
+    try:
+        ib.gemm_set_path(ib.GEMM_TC_PLANES)
+        for T, rows, cols in [(257, 300, 2048), (1, 130, 768), (40, 513, 1536)]:
+            blk = to_dev(cuda, ib.synth_host(type_, rows, cols, seed=9000 + T + rows + type_))
+            X = to_dev(cuda, rng.standard_normal((T, cols)).astype(np.float32))
+            want = ib.gemm_q(type_, blk, X, T, rows, cols)
+            P = ib.gemm_prepare_planes(type_, blk, rows, cols)
+            assert P.numel() == rows * cols * 4
+            got = ib.gemm_planes(P, X, T, rows, cols)
+            assert bool((got == want).all()), (T, rows, cols)
+        assert ib.check_fault() == 0
+    finally:
+        ib.gemm_set_path(ib.GEMM_TENSOR_CORES)
+
+
+@pytest.mark.parametrize("type_", FORMATS, ids=FNAME.get)
 def test_embedding_q(cuda, port, type_):
     vocab, dim = 300, 512
     blk = ib.synth_host(type_, vocab, dim, seed=6000 + type_)
