@@ -46,6 +46,14 @@ extern "C" {
 #define IB_TYPE_Q4_K 12
 #define IB_TYPE_Q6_K 14
 #define IB_TYPE_I16 17
+/* Sized by the reference (include/core/tensor.hpp:204-262) but not decoded by it
+ * (src/gguf/quantization.cpp:201-204 throw); here decoded from the published GGUF
+ * layouts by ib_dequant_f32 / ib_dequant_i16 / ib_embedding_q / ib_gemv_q / ib_gemm_q
+ * and usable as model weights (the per-operation decode step). */
+#define IB_TYPE_Q4_1 3
+#define IB_TYPE_Q2_K 10
+#define IB_TYPE_Q3_K 11
+#define IB_TYPE_Q5_K 13
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* ib_last_error(void);

@@ -23,15 +23,23 @@ HEADER_DIR = os.path.join(os.path.dirname(HERE), "include")
 
 # GGUF tensor types (reference include/core/tensor.hpp:16-37)
 F32, F16, Q4_0, Q5_0, Q5_1, Q8_0, Q4_K, Q6_K, I16 = 0, 1, 2, 6, 7, 8, 12, 14, 17
+# formats the reference sizes but does not decode (its dequantisers throw): decoded here
+# from the published GGUF layouts
+Q4_1, Q2_K, Q3_K, Q5_K = 3, 10, 11, 13
+EXTRA_QUANT_TYPES = (Q4_1, Q2_K, Q3_K, Q5_K)
 QUANT_TYPES = (Q4_0, Q5_0, Q5_1, Q8_0, Q4_K, Q6_K)
 TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q5_0: "Q5_0", Q5_1: "Q5_1",
-              Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", I16: "I16"}
+              Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", I16: "I16", Q4_1: "Q4_1",
+              Q2_K: "Q2_K", Q3_K: "Q3_K", Q5_K: "Q5_K"}
 TYPE_BY_NAME = {v: k for k, v in TYPE_NAMES.items()}
-BLOCK_ELEMS = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256, F32: 1, F16: 1}
-BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q6_K: 210, F32: 4, F16: 2}
+BLOCK_ELEMS = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256, F32: 1, F16: 1,
+               Q4_1: 32, Q2_K: 256, Q3_K: 256, Q5_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q6_K: 210, F32: 4, F16: 2,
+               Q4_1: 20, Q2_K: 84, Q3_K: 110, Q5_K: 176}
 COMM_DEFAULT_TIMEOUT_MS = 300000  # IB_COMM_DEFAULT_TIMEOUT_MS
 # byte alignment the GEMV entry points require of a weight base
-GEMV_ALIGN = {Q4_0: 2, Q5_0: 2, Q5_1: 8, Q8_0: 2, Q4_K: 16, Q6_K: 2}
+GEMV_ALIGN = {Q4_0: 2, Q5_0: 2, Q5_1: 8, Q8_0: 2, Q4_K: 16, Q6_K: 2,
+              Q4_1: 4, Q2_K: 4, Q3_K: 2, Q5_K: 16}
 
 IB_OK = 0
 IB_ERR_INVALID, IB_ERR_CUDA, IB_ERR_UNSUPPORTED, IB_ERR_OOM, IB_ERR_TIMEOUT, IB_ERR_COMM = range(1, 7)

@@ -18,6 +18,8 @@ inline int block_elems(int type) {
     switch (type) {
         case IB_TYPE_Q4_0: case IB_TYPE_Q5_0: case IB_TYPE_Q5_1: case IB_TYPE_Q8_0: return 32;
         case IB_TYPE_Q4_K: case IB_TYPE_Q6_K: return 256;
+        case IB_TYPE_Q4_1: return 32;
+        case IB_TYPE_Q2_K: case IB_TYPE_Q3_K: case IB_TYPE_Q5_K: return 256;
         case IB_TYPE_F32: case IB_TYPE_F16: case IB_TYPE_I16: return 1;
         default: return 0;
     }
@@ -33,13 +35,26 @@ inline int block_bytes(int type) {
         case IB_TYPE_Q8_0: return 34;
         case IB_TYPE_Q4_K: return 144;
         case IB_TYPE_Q6_K: return 210;
+        case IB_TYPE_Q4_1: return 20;
+        case IB_TYPE_Q2_K: return 84;
+        case IB_TYPE_Q3_K: return 110;
+        case IB_TYPE_Q5_K: return 176;
         default: return 0;
     }
 }
+// The six formats the reference decodes (every kernel family takes them).
 inline bool is_block_quant(int type) {
     return type == IB_TYPE_Q4_0 || type == IB_TYPE_Q5_0 || type == IB_TYPE_Q5_1 ||
            type == IB_TYPE_Q8_0 || type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K;
 }
+// Formats the reference sizes but does not decode (src/gguf/quantization.cpp:201-204
+// throw), decoded here from the published GGUF layouts: dequantisation, embedding,
+// a generic decode-as-you-go GEMV and the weight-planes GEMM take them.
+inline bool is_extra_quant(int type) {
+    return type == IB_TYPE_Q4_1 || type == IB_TYPE_Q2_K || type == IB_TYPE_Q3_K ||
+           type == IB_TYPE_Q5_K;
+}
+inline bool is_quant(int type) { return is_block_quant(type) || is_extra_quant(type); }
 inline const char* type_name(int type) {
     switch (type) {
         case IB_TYPE_F32: return "F32";
@@ -50,6 +65,10 @@ inline const char* type_name(int type) {
         case IB_TYPE_Q8_0: return "Q8_0";
         case IB_TYPE_Q4_K: return "Q4_K";
         case IB_TYPE_Q6_K: return "Q6_K";
+        case IB_TYPE_Q4_1: return "Q4_1";
+        case IB_TYPE_Q2_K: return "Q2_K";
+        case IB_TYPE_Q3_K: return "Q3_K";
+        case IB_TYPE_Q5_K: return "Q5_K";
         case IB_TYPE_I16: return "I16";
         default: return "?";
     }

@@ -13,10 +13,7 @@ namespace ib {
 
 template <int TYPE>
 __device__ __forceinline__ void deq_group(const uint8_t* W, int64_t gidx, float* y) {
-    constexpr int BE = (TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K) ? 256 : 32;
-    constexpr int BB = TYPE == IB_TYPE_Q4_0 ? 18 : TYPE == IB_TYPE_Q5_0 ? 22 :
-                       TYPE == IB_TYPE_Q5_1 ? 24 : TYPE == IB_TYPE_Q8_0 ? 34 :
-                       TYPE == IB_TYPE_Q4_K ? 144 : 210;
+    constexpr int BE = QFmt<TYPE>::BE, BB = QFmt<TYPE>::BB;
     constexpr int GPB = BE / 8;
     const int64_t b = gidx / GPB;
     deq8<TYPE>(W + b * BB, (int)(gidx % GPB), y);
@@ -186,6 +183,10 @@ static unsigned grid_for(int64_t n, int per_block = 256, int64_t cap = 148 * 32)
         case IB_TYPE_Q8_0: { constexpr int QT = IB_TYPE_Q8_0; KERNEL_CALL; break; }   \
         case IB_TYPE_Q4_K: { constexpr int QT = IB_TYPE_Q4_K; KERNEL_CALL; break; }   \
         case IB_TYPE_Q6_K: { constexpr int QT = IB_TYPE_Q6_K; KERNEL_CALL; break; }   \
+        case IB_TYPE_Q4_1: { constexpr int QT = IB_TYPE_Q4_1; KERNEL_CALL; break; }   \
+        case IB_TYPE_Q2_K: { constexpr int QT = IB_TYPE_Q2_K; KERNEL_CALL; break; }   \
+        case IB_TYPE_Q3_K: { constexpr int QT = IB_TYPE_Q3_K; KERNEL_CALL; break; }   \
+        case IB_TYPE_Q5_K: { constexpr int QT = IB_TYPE_Q5_K; KERNEL_CALL; break; }   \
         default: break;                                                               \
     }
 
@@ -251,7 +252,7 @@ extern "C" int ib_dequant_i16(int type, const void* dev_blocks, int16_t* dev_q,
     }
     int st = check_shape(type, dev_blocks, dev_q, rows, cols);
     if (st != IB_OK) return st;
-    if (!is_block_quant(type)) {
+    if (!is_quant(type)) {
         set_error("INT16 requantisation needs a block-quantised or F32 tensor");
         return IB_ERR_UNSUPPORTED;
     }

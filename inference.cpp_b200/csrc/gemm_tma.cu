@@ -53,10 +53,7 @@ __global__ void __launch_bounds__(256) dequant_planes_kernel(const uint8_t* __re
                                                              __half* __restrict__ Wh,
                                                              __half* __restrict__ Wl,
                                                              int64_t n8, int64_t cols) {
-    constexpr int BE = (TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K) ? 256 : 32;
-    constexpr int BB = TYPE == IB_TYPE_Q4_0 ? 18 : TYPE == IB_TYPE_Q5_0 ? 22 :
-                       TYPE == IB_TYPE_Q5_1 ? 24 : TYPE == IB_TYPE_Q8_0 ? 34 :
-                       TYPE == IB_TYPE_Q4_K ? 144 : 210;
+    constexpr int BE = QFmt<TYPE>::BE, BB = QFmt<TYPE>::BB;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t e = i * 8, blk = e / BE;  // rows are whole blocks: e indexes the blocks
@@ -289,7 +286,7 @@ static int planes_for(const void* W, __half* Wh, __half* Wl, int64_t rows, int64
 }
 
 bool gemm_planes_supported(int type, int64_t T, int64_t rows, int64_t cols) {
-    return is_block_quant(type) && T >= 1 && rows >= 1 && cols % TM_BK == 0 &&
+    return is_quant(type) && T >= 1 && rows >= 1 && cols % TM_BK == 0 &&
            T * cols < (1ll << 31) && rows * cols < (1ll << 34) &&
            (rows + TM_M - 1) / TM_M <= 65535;
 }
@@ -305,6 +302,10 @@ int gemm_decode_planes(int type, const void* W, void* planes, int64_t rows, int6
         case IB_TYPE_Q8_0: return planes_for<IB_TYPE_Q8_0>(W, Wh, Wl, rows, cols, st);
         case IB_TYPE_Q4_K: return planes_for<IB_TYPE_Q4_K>(W, Wh, Wl, rows, cols, st);
         case IB_TYPE_Q6_K: return planes_for<IB_TYPE_Q6_K>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q4_1: return planes_for<IB_TYPE_Q4_1>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q2_K: return planes_for<IB_TYPE_Q2_K>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q3_K: return planes_for<IB_TYPE_Q3_K>(W, Wh, Wl, rows, cols, st);
+        case IB_TYPE_Q5_K: return planes_for<IB_TYPE_Q5_K>(W, Wh, Wl, rows, cols, st);
     }
     set_error("gemm: unsupported type");
     return IB_ERR_UNSUPPORTED;

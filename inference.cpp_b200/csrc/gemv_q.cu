@@ -315,6 +315,62 @@ static int launch_gemv_q(const uint8_t* W, const float* x, float* y, int64_t row
     return IB_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Q4_1, Q2_K, Q3_K, Q5_K: decode-as-you-go GEMV, lanes striding over the row's
+// 8-element groups (the bit-exact deq8 of quant.cuh), NR rows per warp sharing each
+// x load, FP32 accumulation and a shuffle reduction.
+// ---------------------------------------------------------------------------
+template <int TYPE, int NR>
+__global__ void __launch_bounds__(128) gemv_deq_kernel(const uint8_t* __restrict__ W,
+                                                       const float* __restrict__ x,
+                                                       float* __restrict__ y, int64_t rows,
+                                                       int64_t cols) {
+    constexpr int BE = QFmt<TYPE>::BE, BB = QFmt<TYPE>::BB, GPB = BE / 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * NR;
+    if (row0 >= rows) return;
+    const int64_t gpr = cols / 8, row_bytes = cols / BE * BB;
+    float acc[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+    for (int64_t g = lane; g < gpr; g += 32) {
+        const float4 a = ldx4(x + g * 8), b = ldx4(x + g * 8 + 4);
+        const int64_t blk = g / GPB;
+        const int sub = (int)(g - blk * GPB);
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            if (row0 + r >= rows) break;
+            float v[8];
+            deq8<TYPE>(W + (row0 + r) * row_bytes + blk * BB, sub, v);
+            float t = acc[r];
+            t = fmaf(v[0], a.x, t);
+            t = fmaf(v[1], a.y, t);
+            t = fmaf(v[2], a.z, t);
+            t = fmaf(v[3], a.w, t);
+            t = fmaf(v[4], b.x, t);
+            t = fmaf(v[5], b.y, t);
+            t = fmaf(v[6], b.z, t);
+            t = fmaf(v[7], b.w, t);
+            acc[r] = t;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const float v = warp_sum(acc[r]);
+        if (lane == 0 && row0 + r < rows) y[row0 + r] = v;
+    }
+}
+
+template <int TYPE>
+static int launch_gemv_deq(const uint8_t* W, const float* x, float* y, int64_t rows,
+                           int64_t cols, cudaStream_t st) {
+    constexpr int WARPS = 4, NR = 2;
+    const int64_t grid = (rows + WARPS * NR - 1) / (WARPS * NR);
+    gemv_deq_kernel<TYPE, NR><<<(unsigned)grid, WARPS * 32, 0, st>>>(W, x, y, rows, cols);
+    IB_LAUNCH_CHECK("gemv_deq_kernel");
+    return IB_OK;
+}
+
 }  // namespace ib
 
 using namespace ib;
@@ -326,13 +382,22 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     IB_REQUIRE(rows > 0 && cols > 0, "bad GEMV shape");
     IB_REQUIRE(((uintptr_t)dev_x & 15) == 0, "x must be 16-byte aligned");
     const int be = block_elems(type);
-    if (!is_block_quant(type)) {
+    if (!is_quant(type)) {
         set_error(std::string("ib_gemv_q: unsupported type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }
     IB_REQUIRE(cols % be == 0, "cols must be a multiple of the block size");
     cudaStream_t st = as_stream(stream);
     const uint8_t* W = (const uint8_t*)dev_W;
+    if (is_extra_quant(type)) {
+        IB_REQUIRE(((uintptr_t)W & 1) == 0, "weights must be 2-byte aligned");
+        switch (type) {
+            case IB_TYPE_Q4_1: return launch_gemv_deq<IB_TYPE_Q4_1>(W, dev_x, dev_y, rows, cols, st);
+            case IB_TYPE_Q2_K: return launch_gemv_deq<IB_TYPE_Q2_K>(W, dev_x, dev_y, rows, cols, st);
+            case IB_TYPE_Q3_K: return launch_gemv_deq<IB_TYPE_Q3_K>(W, dev_x, dev_y, rows, cols, st);
+            default: return launch_gemv_deq<IB_TYPE_Q5_K>(W, dev_x, dev_y, rows, cols, st);
+        }
+    }
     if (cols <= (1 << 30) && rows < (1ll << 31) && gemv_mma_supported(type)) {
         // limb slab of x, then the TMA-staged GEMV (decode.cu)
         const bool kq = slab_kquant(type);

@@ -155,13 +155,13 @@ using namespace ib;
 // rows/tp_size rows, 1 = the rank's cols/tp_size columns of every row (whole blocks).
 static int set_linear(Model* m, Linear& L, int type, int64_t rows, int64_t cols,
                       const void* data, int on_device, int axis = -1) {
-    if (!is_block_quant(type) && type != IB_TYPE_F32 && type != IB_TYPE_F16) {
+    if (!is_quant(type) && type != IB_TYPE_F32 && type != IB_TYPE_F16) {
         set_error(std::string("model: unsupported tensor type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }
     const int N = m->tp_size, rk = m->tp_rank;
-    const int64_t be = is_block_quant(type) ? block_elems(type) : 1;
-    const int64_t eb = is_block_quant(type) ? block_bytes(type) : (type == IB_TYPE_F32 ? 4 : 2);
+    const int64_t be = is_quant(type) ? block_elems(type) : 1;
+    const int64_t eb = is_quant(type) ? block_bytes(type) : (type == IB_TYPE_F32 ? 4 : 2);
     const int64_t row_bytes = cols / be * eb;
     int64_t lrows = rows, lcols = cols, off = 0;
     if (N > 1 && axis == 0) {
@@ -194,7 +194,7 @@ static int set_linear(Model* m, Linear& L, int type, int64_t rows, int64_t cols,
                                     (size_t)row_bytes, (size_t)lrow_bytes, (size_t)lrows,
                                     on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                                     m->stream));
-    const bool packed_ok = is_block_quant(type) && m->cfg.precision == IB_PRECISION_NATIVE;
+    const bool packed_ok = is_quant(type) && m->cfg.precision == IB_PRECISION_NATIVE;
     if (packed_ok) {
         L.repr = REPR_PACKED;
         L.w = dev;

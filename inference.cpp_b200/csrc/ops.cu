@@ -272,10 +272,7 @@ __device__ __forceinline__ void load_w8(const void* W, int64_t K, int64_t row, i
 #pragma unroll
         for (int i = 0; i < 8; ++i) y[i] = (float)p[i];
     } else {
-        constexpr int BE = (TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K) ? 256 : 32;
-        constexpr int BB = TYPE == IB_TYPE_Q4_0 ? 18 : TYPE == IB_TYPE_Q5_0 ? 22 :
-                           TYPE == IB_TYPE_Q5_1 ? 24 : TYPE == IB_TYPE_Q8_0 ? 34 :
-                           TYPE == IB_TYPE_Q4_K ? 144 : 210;
+        constexpr int BE = QFmt<TYPE>::BE, BB = QFmt<TYPE>::BB;
         const uint8_t* blk = (const uint8_t*)W + (row * (K / BE) + k0 / BE) * BB;
         deq8<TYPE>(blk, (int)((k0 % BE) / 8), y);
     }
@@ -404,6 +401,10 @@ int gemm_q_simt(int type, const void* W, const float* X, float* Y, int T, int M,
         case IB_TYPE_Q8_0: return launch_gemm<IB_TYPE_Q8_0>(W, nullptr, X, Y, T, M, K, st);
         case IB_TYPE_Q4_K: return launch_gemm<IB_TYPE_Q4_K>(W, nullptr, X, Y, T, M, K, st);
         case IB_TYPE_Q6_K: return launch_gemm<IB_TYPE_Q6_K>(W, nullptr, X, Y, T, M, K, st);
+        case IB_TYPE_Q4_1: return launch_gemm<IB_TYPE_Q4_1>(W, nullptr, X, Y, T, M, K, st);
+        case IB_TYPE_Q2_K: return launch_gemm<IB_TYPE_Q2_K>(W, nullptr, X, Y, T, M, K, st);
+        case IB_TYPE_Q3_K: return launch_gemm<IB_TYPE_Q3_K>(W, nullptr, X, Y, T, M, K, st);
+        case IB_TYPE_Q5_K: return launch_gemm<IB_TYPE_Q5_K>(W, nullptr, X, Y, T, M, K, st);
         case IB_TYPE_F32: return launch_gemm<IB_TYPE_F32>(W, nullptr, X, Y, T, M, K, st);
     }
     set_error("gemm: unsupported weight type");
@@ -648,7 +649,7 @@ extern "C" int ib_gemm_q(int type, const void* dev_W, const float* dev_X, float*
     if (T == 0 || rows == 0) return IB_OK;
     IB_REQUIRE(dev_W && dev_X && dev_Y && T > 0 && rows > 0 && cols > 0, "bad gemm_q arguments");
     IB_REQUIRE(T <= 65535 * 64 && rows < (1ll << 31) && cols < (1ll << 31), "gemm_q too large");
-    if (!is_block_quant(type)) {
+    if (!is_quant(type)) {
         set_error(std::string("ib_gemm_q: unsupported type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }

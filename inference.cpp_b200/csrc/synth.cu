@@ -35,7 +35,7 @@ using namespace ib;
 static int synth_check(int type, int64_t rows, int64_t cols) {
     IB_REQUIRE(rows >= 0 && cols >= 0, "negative shape");
     if (type == IB_TYPE_F32) return IB_OK;
-    if (!is_block_quant(type)) {
+    if (!is_quant(type)) {
         set_error("synth: unsupported type");
         return IB_ERR_UNSUPPORTED;
     }

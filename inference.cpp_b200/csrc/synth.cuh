@@ -13,7 +13,9 @@
 // src/gguf/quantization.cpp:270-352).  Q5_0, Q5_1, Q4_K and Q6_K have no encoder
 // in the reference; the ones below are this project's own simple min/max
 // encoders, and produce any valid block of the layouts decoded at
-// src/gguf/quantization.cpp:83-245.
+// src/gguf/quantization.cpp:83-245.  Q4_1, Q2_K, Q3_K and Q5_K (sized by the
+// reference, not decoded by it) get encoders of the same kind for the published GGUF
+// layouts.
 #pragma once
 #include <stdint.h>
 #include <math.h>
@@ -308,10 +310,151 @@ SY_HD void enc_q6_k(const float* x, uint8_t* out) {
     }
 }
 
-SY_HD int block_elems(int type) { return (type == 12 || type == 14) ? 256 : 32; }
+// Q4_1 (20 B): d = (max-min)/15, m = min, q = round((x-m)/d) in [0,15].
+SY_HD void enc_q4_1(const float* x, uint8_t* out) {
+    float mn = x[0], mx = x[0];
+    for (int j = 1; j < 32; ++j) { mn = fmin_(mn, x[j]); mx = fmax_(mx, x[j]); }
+    uint16_t dh = f2h_rne(fdiv(fsub(mx, mn), 15.0f));
+    uint16_t mh = f2h_rne(mn);
+    float df = h2f(dh), mf = h2f(mh);
+    out[0] = (uint8_t)(dh & 0xFF);
+    out[1] = (uint8_t)(dh >> 8);
+    out[2] = (uint8_t)(mh & 0xFF);
+    out[3] = (uint8_t)(mh >> 8);
+    int q[32];
+    for (int j = 0; j < 32; ++j) {
+        int v = df > 0.0f ? (int)round_away(fdiv(fsub(x[j], mf), df)) : 0;
+        q[j] = clampi(v, 0, 15);
+    }
+    for (int j = 0; j < 16; ++j) out[4 + j] = (uint8_t)(q[j] | (q[j + 16] << 4));
+}
+
+// Q5_K (176 B): as Q4_K with 5-bit quants (sub-block scale (max-min)/31).
+SY_HD void enc_q5_k(const float* x, uint8_t* out) {
+    float scale[8], minv[8];
+    float msc = 0.0f, mmn = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        float mn = 0.0f, mx = x[32 * j];
+        for (int l = 0; l < 32; ++l) { mn = fmin_(mn, x[32 * j + l]); mx = fmax_(mx, x[32 * j + l]); }
+        scale[j] = fdiv(fsub(mx, mn), 31.0f);
+        minv[j] = -mn;
+        msc = fmax_(msc, scale[j]);
+        mmn = fmax_(mmn, minv[j]);
+    }
+    uint16_t dh = f2h_rne(fdiv(msc, 63.0f)), mh = f2h_rne(fdiv(mmn, 63.0f));
+    float df = h2f(dh), mf = h2f(mh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; ++j) {
+        sc[j] = df > 0.0f ? clampi((int)round_away(fdiv(scale[j], df)), 0, 63) : 0;
+        m[j] = mf > 0.0f ? clampi((int)round_away(fdiv(minv[j], mf)), 0, 63) : 0;
+    }
+    out[0] = (uint8_t)(dh & 0xFF);
+    out[1] = (uint8_t)(dh >> 8);
+    out[2] = (uint8_t)(mh & 0xFF);
+    out[3] = (uint8_t)(mh >> 8);
+    uint8_t* s = out + 4;
+    for (int k = 0; k < 4; ++k) {
+        s[k] = (uint8_t)((sc[k] & 63) | ((sc[k + 4] >> 4) << 6));
+        s[k + 4] = (uint8_t)((m[k] & 63) | ((m[k + 4] >> 4) << 6));
+        s[k + 8] = (uint8_t)((sc[k + 4] & 0xF) | ((m[k + 4] & 0xF) << 4));
+    }
+    uint8_t* qh = out + 16;
+    uint8_t* qs = out + 48;
+    for (int l = 0; l < 32; ++l) qh[l] = 0;
+    for (int p = 0; p < 4; ++p) {
+        int q[64];
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * p + h;
+            const float a = fmul(mf, (float)m[j]);
+            const float b = fmul(df, (float)sc[j]);
+            for (int l = 0; l < 32; ++l) {
+                int v = b > 0.0f ? (int)round_away(fdiv(fadd(x[32 * j + l], a), b)) : 0;
+                q[32 * h + l] = clampi(v, 0, 31);
+                qh[l] |= (uint8_t)(((q[32 * h + l] >> 4) & 1) << j);
+            }
+        }
+        for (int l = 0; l < 32; ++l) qs[32 * p + l] = (uint8_t)((q[l] & 0xF) | ((q[32 + l] & 0xF) << 4));
+    }
+}
+
+// Q2_K (84 B): 16 sub-blocks of 16, 4-bit scale and min, 2-bit quants.  Sub-block
+// b = 8h + 2j + k holds elements 16b.. at bits 2j of qs[32h + 16k + l].
+SY_HD void enc_q2_k(const float* x, uint8_t* out) {
+    float scale[16], minv[16], msc = 0.0f, mmn = 0.0f;
+    for (int b = 0; b < 16; ++b) {
+        float mn = 0.0f, mx = x[16 * b];
+        for (int l = 0; l < 16; ++l) { mn = fmin_(mn, x[16 * b + l]); mx = fmax_(mx, x[16 * b + l]); }
+        scale[b] = fdiv(fsub(mx, mn), 3.0f);
+        minv[b] = -mn;
+        msc = fmax_(msc, scale[b]);
+        mmn = fmax_(mmn, minv[b]);
+    }
+    uint16_t dh = f2h_rne(fdiv(msc, 15.0f)), mh = f2h_rne(fdiv(mmn, 15.0f));
+    float df = h2f(dh), mf = h2f(mh);
+    for (int i = 16; i < 80; ++i) out[i] = 0;
+    for (int b = 0; b < 16; ++b) {
+        int sc = df > 0.0f ? clampi((int)round_away(fdiv(scale[b], df)), 0, 15) : 0;
+        int m = mf > 0.0f ? clampi((int)round_away(fdiv(minv[b], mf)), 0, 15) : 0;
+        out[b] = (uint8_t)(sc | (m << 4));
+        const float a = fmul(mf, (float)m), dd = fmul(df, (float)sc);
+        const int h = b >> 3, j = (b >> 1) & 3, k = b & 1;
+        for (int l = 0; l < 16; ++l) {
+            int v = dd > 0.0f ? (int)round_away(fdiv(fadd(x[16 * b + l], a), dd)) : 0;
+            out[16 + 32 * h + 16 * k + l] |= (uint8_t)(clampi(v, 0, 3) << (2 * j));
+        }
+    }
+    out[80] = (uint8_t)(dh & 0xFF);
+    out[81] = (uint8_t)(dh >> 8);
+    out[82] = (uint8_t)(mh & 0xFF);
+    out[83] = (uint8_t)(mh >> 8);
+}
+
+// Q3_K (110 B): 16 sub-blocks of 16 with 6-bit scales (stored + 32), 3-bit signed
+// quants in [-4, 3]: the low 2 bits in qs, the sign-side bit in hmask (set: q >= 0).
+SY_HD void enc_q3_k(const float* x, uint8_t* out) {
+    float scale[16], msc = 0.0f;
+    for (int b = 0; b < 16; ++b) {
+        float amax = 0.0f;
+        for (int l = 0; l < 16; ++l) amax = fmax_(amax, fabs_(x[16 * b + l]));
+        scale[b] = fdiv(amax, 4.0f);
+        msc = fmax_(msc, scale[b]);
+    }
+    uint16_t dh = f2h_rne(fdiv(msc, 31.0f));
+    float df = h2f(dh);
+    for (int i = 0; i < 108; ++i) out[i] = 0;
+    uint8_t* hm = out;
+    uint8_t* qs = out + 32;
+    uint8_t* sc = out + 96;
+    for (int b = 0; b < 16; ++b) {
+        int s = df > 0.0f ? clampi((int)round_away(fdiv(scale[b], df)), 0, 31) : 0;
+        const int u = s + 32;
+        if (b < 8) sc[b] |= (uint8_t)(u & 0xF);
+        else sc[b - 8] |= (uint8_t)((u & 0xF) << 4);
+        sc[8 + (b & 3)] |= (uint8_t)((u >> 4) << (2 * (b >> 2)));
+        const float dd = fmul(df, (float)s);
+        const int h = b >> 3, j = (b >> 1) & 3, k = b & 1;
+        for (int l = 0; l < 16; ++l) {
+            int v = dd > 0.0f ? (int)round_away(fdiv(x[16 * b + l], dd)) : 0;
+            v = clampi(v, -4, 3);
+            const int q2 = v < 0 ? v + 4 : v;
+            qs[32 * h + 16 * k + l] |= (uint8_t)(q2 << (2 * j));
+            if (v >= 0) hm[16 * k + l] |= (uint8_t)(1 << (4 * h + j));
+        }
+    }
+    out[108] = (uint8_t)(dh & 0xFF);
+    out[109] = (uint8_t)(dh >> 8);
+}
+
+SY_HD int block_elems(int type) {
+    return (type == 10 || type == 11 || type == 12 || type == 13 || type == 14) ? 256 : 32;
+}
 SY_HD int block_bytes(int type) {
     switch (type) {
         case 2: return 18;
+        case 3: return 20;
+        case 10: return 84;
+        case 11: return 110;
+        case 13: return 176;
         case 6: return 22;
         case 7: return 24;
         case 8: return 34;
@@ -332,6 +475,10 @@ SY_HD bool encode_block(int type, uint64_t seed, float stdv, int64_t cols, int64
     for (int i = 0; i < be; ++i) x[i] = value(seed, (uint64_t)(r * cols + c0 + i), stdv);
     switch (type) {
         case 2: enc_q4_0(x, out); return true;
+        case 3: enc_q4_1(x, out); return true;
+        case 10: enc_q2_k(x, out); return true;
+        case 11: enc_q3_k(x, out); return true;
+        case 13: enc_q5_k(x, out); return true;
         case 6: enc_q5_0(x, out); return true;
         case 7: enc_q5_1(x, out); return true;
         case 8: enc_q8_0(x, out); return true;

@@ -25,14 +25,14 @@
 #include <string.h>
 
 /* GGUF type codes (include/core/tensor.hpp:16-37) */
-enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8,
-       T_Q4_K = 12, T_Q6_K = 14, T_I16 = 17 };
+enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8,
+       T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_I16 = 17 };
 
 /* Elements per block: include/core/tensor.hpp:246-262 */
 int orc_block_size(int t) {
     switch (t) {
-        case T_Q4_0: case T_Q5_0: case T_Q5_1: case T_Q8_0: return 32;
-        case T_Q4_K: case T_Q6_K: return 256;
+        case T_Q4_0: case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_Q8_0: return 32;
+        case T_Q2_K: case T_Q3_K: case T_Q4_K: case T_Q5_K: case T_Q6_K: return 256;
         default: return 1;
     }
 }
@@ -43,6 +43,10 @@ int orc_block_bytes(int t) {
         case T_F32: return 4;
         case T_F16: return 2;
         case T_Q4_0: return 18;
+        case T_Q4_1: return 20;
+        case T_Q2_K: return 84;
+        case T_Q3_K: return 110;
+        case T_Q5_K: return 176;
         case T_Q5_0: return 22;
         case T_Q5_1: return 24;
         case T_Q8_0: return 34;
@@ -189,6 +193,97 @@ static void dq_q6_k(const uint8_t* b, float* y, int64_t n) {
     }
 }
 
+/* ---- formats the reference sizes (include/core/tensor.hpp:204-223) but does not
+ * decode (src/gguf/quantization.cpp:201-204 throw): restated from the published GGUF
+ * block layouts (the `gguf` Python package, 0.19.0, decodes them the same way; the CPU
+ * tests pin these functions to it).  Every value is one exact product (fp16 scale x
+ * small integers) plus at most one rounding, so evaluation order cannot change it. */
+
+/* Q4_1 (20 B): d, m (fp16), qs[16]; element j = qs[j] low nibble, j + 16 high nibble;
+ * y = d * q + m */
+static void dq_q4_1(const uint8_t* b, float* y, int64_t n) {
+    for (int64_t i = 0; i < n / 32; ++i) {
+        const uint8_t* blk = b + i * 20;
+        float d = orc_fp16_to_fp32(rd16(blk)), m = orc_fp16_to_fp32(rd16(blk + 2));
+        for (int j = 0; j < 16; ++j) {
+            y[i * 32 + j] = (float)(blk[4 + j] & 0x0F) * d + m;
+            y[i * 32 + j + 16] = (float)(blk[4 + j] >> 4) * d + m;
+        }
+    }
+}
+
+/* Q5_K (176 B): d, dmin (fp16), scales[12] (6-bit scale/min pairs as Q4_K), qh[32],
+ * qs[128].  Chunk p of 64: sub-blocks 2p (low nibbles of qs[32p..], high bit qh bit 2p)
+ * and 2p + 1 (high nibbles, qh bit 2p + 1); y = (d*sc) * q5 - dmin*m */
+static void dq_q5_k(const uint8_t* b, float* y, int64_t n) {
+    for (int64_t sb = 0; sb < n / 256; ++sb) {
+        const uint8_t* blk = b + sb * 176;
+        float d = orc_fp16_to_fp32(rd16(blk)), dmin = orc_fp16_to_fp32(rd16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const uint8_t* qh = blk + 16;
+        const uint8_t* q = blk + 48;
+        float* o = y + sb * 256;
+        for (int p = 0; p < 4; ++p) {
+            int s0, m0, s1, m1;
+            scale_min_k4(2 * p, sc, &s0, &m0);
+            scale_min_k4(2 * p + 1, sc, &s1, &m1);
+            float d1 = d * s0, mm1 = dmin * m0, d2 = d * s1, mm2 = dmin * m1;
+            for (int l = 0; l < 32; ++l)
+                *o++ = d1 * ((q[l] & 0x0F) + (((qh[l] >> (2 * p)) & 1) << 4)) - mm1;
+            for (int l = 0; l < 32; ++l)
+                *o++ = d2 * ((q[l] >> 4) + (((qh[l] >> (2 * p + 1)) & 1) << 4)) - mm2;
+            q += 32;
+        }
+    }
+}
+
+/* Q2_K (84 B): scales[16] (low nibble scale, high nibble min), qs[64], d, dmin (fp16).
+ * Element e = 128h + 32j + 16k + l: 2-bit q = qs[32h + 16k + l] >> 2j, sub-block
+ * 8h + 2j + k; y = (d*sc) * q - dmin*m */
+static void dq_q2_k(const uint8_t* b, float* y, int64_t n) {
+    for (int64_t sb = 0; sb < n / 256; ++sb) {
+        const uint8_t* blk = b + sb * 84;
+        float d = orc_fp16_to_fp32(rd16(blk + 80)), dmin = orc_fp16_to_fp32(rd16(blk + 82));
+        float* o = y + sb * 256;
+        for (int e = 0; e < 256; ++e) {
+            int h = e >> 7, j = (e >> 5) & 3, k = (e >> 4) & 1, l = e & 15;
+            int scm = blk[8 * h + 2 * j + k];
+            int q = (blk[16 + 32 * h + 16 * k + l] >> (2 * j)) & 3;
+            float dl = d * (scm & 0xF), ml = dmin * (scm >> 4);
+            o[e] = dl * q - ml;
+        }
+    }
+}
+
+/* Q3_K (110 B): hmask[32], qs[64], scales[12] (16 signed 6-bit scales: low nibbles in
+ * bytes 0-7, scale i >= 8 in the high nibble of byte i - 8, the top 2 bits of scale i
+ * in byte 8 + i%4 at bit 2(i/4); value - 32), d (fp16).  Element e = 128h + 32j + 16k +
+ * l: q = (qs[32h + 16k + l] >> 2j & 3) - (hmask[16k + l] bit 4h + j ? 0 : 4), sub-block
+ * 8h + 2j + k; y = (d*s) * q */
+static int q3k_scale(const uint8_t* sc, int i) {
+    int lo = i < 8 ? (sc[i] & 0xF) : (sc[i - 8] >> 4);
+    int hi = (sc[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+static void dq_q3_k(const uint8_t* b, float* y, int64_t n) {
+    for (int64_t sb = 0; sb < n / 256; ++sb) {
+        const uint8_t* blk = b + sb * 110;
+        const uint8_t* hm = blk;
+        const uint8_t* qs = blk + 32;
+        const uint8_t* sc = blk + 96;
+        float d = orc_fp16_to_fp32(rd16(blk + 108));
+        float* o = y + sb * 256;
+        for (int e = 0; e < 256; ++e) {
+            int h = e >> 7, j = (e >> 5) & 3, k = (e >> 4) & 1, l = e & 15;
+            int q = ((qs[32 * h + 16 * k + l] >> (2 * j)) & 3) -
+                    (((hm[16 * k + l] >> (4 * h + j)) & 1) ? 0 : 4);
+            float dl = d * q3k_scale(sc, 8 * h + 2 * j + k);
+            o[e] = dl * q;
+        }
+    }
+}
+
 /* dequantize dispatch: src/gguf/quantization.cpp:250-267 (+ F32/F16 from
  * src/models/transformer.cpp:176-199).  Returns 0, or -1 for an unsupported type. */
 int orc_dequantize(int t, const void* src, float* dst, int64_t n) {
@@ -203,6 +298,10 @@ int orc_dequantize(int t, const void* src, float* dst, int64_t n) {
         case T_Q5_1: dq_q5_1(b, dst, n); return 0;
         case T_Q8_0: dq_q8_0(b, dst, n); return 0;
         case T_Q4_K: dq_q4_k(b, dst, n); return 0;
+        case T_Q4_1: dq_q4_1(b, dst, n); return 0;
+        case T_Q5_K: dq_q5_k(b, dst, n); return 0;
+        case T_Q2_K: dq_q2_k(b, dst, n); return 0;
+        case T_Q3_K: dq_q3_k(b, dst, n); return 0;
         case T_Q6_K: dq_q6_k(b, dst, n); return 0;
         default: return -1;
     }

@@ -45,7 +45,10 @@ def test_type_info_table():
     for t in ib.QUANT_TYPES:
         ib.call("ib_type_info", t, ctypes.byref(be), ctypes.byref(bb))
         assert (be.value, bb.value) == (ib.BLOCK_ELEMS[t], ib.BLOCK_BYTES[t])
-    assert ib.lib().ib_type_info(13, ctypes.byref(be), ctypes.byref(bb)) == 3  # Q5_K unsupported
+    for t in ib.EXTRA_QUANT_TYPES:
+        ib.call("ib_type_info", t, ctypes.byref(be), ctypes.byref(bb))
+        assert (be.value, bb.value) == (ib.BLOCK_ELEMS[t], ib.BLOCK_BYTES[t])
+    assert ib.lib().ib_type_info(15, ctypes.byref(be), ctypes.byref(bb)) == 3  # Q8_K unsupported
 
 
 def test_argument_validation_without_gpu():
