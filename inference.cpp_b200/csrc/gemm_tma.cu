@@ -135,10 +135,23 @@ __device__ __forceinline__ void tma_load2d(uint32_t dst, const CUtensorMap* map,
         : "memory");
 }
 
+// Work of CTA b (one-dimensional grid): b < n_full is the whole tile b (token tiles vary
+// fastest); the rest are `split` parts along K of each tile of the last, partly filled
+// wave, whose FP32 partial tiles go to `part` ([tail tile][part][token][row]) for
+// gemm_tail_reduce_kernel.  Splitting the tail keeps every SM busy to the end: 896
+// tiles on 148 SMs are six full waves and 8 tiles, which would hold one wave alone.
+struct TmWork {
+    int n_ntiles;  // token tiles per row tile
+    int n_full;    // tiles computed whole
+    int split;     // parts per tail tile (1: no tail split)
+    int kps;       // k-steps per part
+    float* part;
+};
+
 __global__ void __launch_bounds__(TM_THREADS, 1)
     gemm_planes_kernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                        const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
-                       float* __restrict__ Y, int T, int rows, int cols) {
+                       float* __restrict__ Y, int T, int rows, int cols, const TmWork wk) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full[TM_STAGES], empty[TM_STAGES], acc_full;
     __shared__ uint32_t tmem_base;
@@ -146,8 +159,16 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
     // token tiles vary fastest: the CTAs resident together share weight strips (each
     // strip's planes come from DRAM once and serve every token tile from L2), and the
     // X planes (2 x T x cols x 2 bytes) stay in L2
-    const int n0 = blockIdx.x * TM_N, m0 = blockIdx.y * TM_M;
-    const int n_k = cols / TM_BK;
+    const int b = (int)blockIdx.x;
+    const bool is_part = b >= wk.n_full;
+    const int tail = is_part ? (b - wk.n_full) / wk.split : 0;
+    const int pi = is_part ? (b - wk.n_full) - tail * wk.split : 0;
+    const int tile = is_part ? wk.n_full + tail : b;
+    const int n0 = (tile % wk.n_ntiles) * TM_N, m0 = (tile / wk.n_ntiles) * TM_M;
+    const int n_k_all = cols / TM_BK;
+    const int k_begin = is_part ? pi * wk.kps : 0;
+    const int k_end = is_part ? min(n_k_all, k_begin + wk.kps) : n_k_all;
+    const int n_k = k_end - k_begin;  // >= 1: the host sizes the parts
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     if (threadIdx.x == 0) {
         for (int s = 0; s < TM_STAGES; ++s) {
@@ -179,7 +200,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
                 if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, &g_gemm_tma_fault, 41)) break;
                 const uint32_t st = base + (uint32_t)(s * TM_STAGE);
                 mbar_arrive_expect_tx(&full[s], (uint32_t)TM_STAGE);
-                const int k0 = kt * TM_BK;
+                const int k0 = (k_begin + kt) * TM_BK;
                 tma_load2d(st, &mWh, k0, m0, &full[s]);
                 tma_load2d(st + TM_A, &mWl, k0, m0, &full[s]);
                 tma_load2d(st + 2 * TM_A, &mXh, k0, n0, &full[s]);
@@ -205,7 +226,7 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
                     const uint64_t ah = tm_desc(st + off), al = tm_desc(st + TM_A + off);
                     const uint64_t bh = tm_desc(st + 2 * TM_A + off);
                     const uint64_t bl = tm_desc(st + 2 * TM_A + TM_B + off);
-                    tm_mma(tmem, ah, bh, idesc, (kt | kk) != 0);
+                    tm_mma(tmem, ah, bh, idesc, (kt | kk) != 0);  // kt counts from k_begin
                     tm_mma(tmem, ah, bl, idesc, 1u);
                     tm_mma(tmem, al, bh, idesc, 1u);
                 }
@@ -220,11 +241,16 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
         tm_fence_after();
         if (have) {
             const int q = warp & 3, orow = m0 + 32 * q + lane;
+            float* pt = is_part ? wk.part + ((size_t)(tail * wk.split + pi) * TM_N) * TM_M : nullptr;
             for (int c0 = 0; c0 < TM_N; c0 += 32) {
                 if (n0 + c0 >= T) break;  // warp-uniform
                 uint32_t v[32];
                 tm_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-                if (orow < rows) {
+                if (is_part) {  // the whole partial tile, rows contiguous
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        pt[(size_t)(c0 + jj) * TM_M + 32 * q + lane] = __uint_as_float(v[jj]);
+                } else if (orow < rows) {
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) {
                         const int t = n0 + c0 + jj;
@@ -240,6 +266,25 @@ __global__ void __launch_bounds__(TM_THREADS, 1)
         tm_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TM_N)
                      : "memory");
+    }
+}
+
+// Y <- the sum of each tail tile's parts, in part order (deterministic).
+__global__ void gemm_tail_reduce_kernel(const float* __restrict__ part, float* __restrict__ Y,
+                                        int T, int rows, int n_ntiles, int n_full, int n_tail,
+                                        int split) {
+    const int64_t per = (int64_t)TM_N * TM_M;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)n_tail * per;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / per);
+        const int rem = (int)(i - (int64_t)t * per), c = rem / TM_M, r = rem - c * TM_M;
+        const int tile = n_full + t;
+        const int tok = (tile % n_ntiles) * TM_N + c, row = (tile / n_ntiles) * TM_M + r;
+        if (tok >= T || row >= rows) continue;
+        const float* p = part + ((size_t)t * split * TM_N + c) * TM_M + r;
+        float acc = 0.f;
+        for (int k = 0; k < split; ++k) acc += p[(size_t)k * per];
+        Y[(size_t)tok * rows + row] = acc;
     }
 }
 
@@ -333,6 +378,7 @@ int gemm_on_planes(const void* planes, const float* X, float* Y, int T, int rows
     if ((r = tensor_map_2d(&mXl, Xl, cols, T, TM_N))) return r;
     static std::mutex mu;
     static bool attr_set[64] = {};
+    static int n_sm[64] = {};
     int dev = 0;
     IB_CUDA_CHECK(cudaGetDevice(&dev));
     {
@@ -344,12 +390,40 @@ int gemm_on_planes(const void* planes, const float* X, float* Y, int T, int rows
         if (!attr_set[dev]) {
             IB_CUDA_CHECK(cudaFuncSetAttribute(gemm_planes_kernel,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TM_SMEM));
+            IB_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev));
             attr_set[dev] = true;
         }
     }
-    const dim3 grid((T + TM_N - 1) / TM_N, (rows + TM_M - 1) / TM_M);
-    gemm_planes_kernel<<<grid, TM_THREADS, TM_SMEM, st>>>(mWh, mWl, mXh, mXl, Y, T, rows, cols);
+    // the last wave: when it is at most half full, its tiles are split along K so that
+    // every SM has work to the end (one CTA per SM)
+    const int n_ntiles = (T + TM_N - 1) / TM_N, n_mtiles = (rows + TM_M - 1) / TM_M;
+    const int64_t n_tiles = (int64_t)n_ntiles * n_mtiles;
+    const int n_k = cols / TM_BK, sms = n_sm[dev];
+    const int tail = (int)(n_tiles % sms);
+    TmWork wk{n_ntiles, (int)n_tiles, 1, n_k, nullptr};
+    if (n_tiles > sms && tail > 0 && 2 * tail <= sms && n_k >= 8) {
+        int split = sms / tail;
+        if (split > n_k / 4) split = n_k / 4;  // parts of four k-steps at least
+        const int kps = (n_k + split - 1) / split;
+        split = (n_k + kps - 1) / kps;        // every part non-empty
+        if (split >= 2) {
+            void* wp = nullptr;
+            if ((r = workspace_get(WS_GEMM_PART, (size_t)tail * split * TM_N * TM_M * 4, &wp)))
+                return r;
+            wk = TmWork{n_ntiles, (int)(n_tiles - tail), split, kps, (float*)wp};
+        }
+    }
+    const int64_t grid = wk.split > 1 ? wk.n_full + (int64_t)tail * wk.split : n_tiles;
+    IB_REQUIRE(grid <= 0x7FFFFFFF, "gemm: too many tiles");
+    gemm_planes_kernel<<<(unsigned)grid, TM_THREADS, TM_SMEM, st>>>(mWh, mWl, mXh, mXl, Y, T, rows,
+                                                                   cols, wk);
     IB_LAUNCH_CHECK("gemm_planes_kernel");
+    if (wk.split > 1) {
+        const int64_t n = (int64_t)tail * TM_N * TM_M;
+        gemm_tail_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+            wk.part, Y, T, rows, n_ntiles, wk.n_full, tail, wk.split);
+        IB_LAUNCH_CHECK("gemm_tail_reduce_kernel");
+    }
     return IB_OK;
 }
 

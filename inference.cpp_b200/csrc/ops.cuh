@@ -6,7 +6,7 @@
 
 namespace ib {
 
-enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_GEMM = 2, WS_GEMM_W = 3, WS_ATTN_PLANES = 4, WS_SLOTS = 5 };
+enum { WS_ATTENTION = 0, WS_GEMV = 1, WS_GEMM = 2, WS_GEMM_W = 3, WS_ATTN_PLANES = 4, WS_GEMM_PART = 5, WS_SLOTS = 6 };
 int workspace_get(int slot, size_t bytes, void** out);
 size_t attention_partial_bytes(int H, int HD, int pos);
 // Decode attention in one launch (split flash-decode, last-CTA combine); also writes

@@ -94,7 +94,7 @@ def test_gemm_q_vs_float64(cuda, port, type_, path):
     rng = np.random.default_rng(700 + type_)
     try:
         ib.gemm_set_path(path)
-        for T, rows, cols in [(1, 64, 512), (130, 70, 768), (257, 300, 2048)]:
+        for T, rows, cols in [(1, 64, 512), (130, 70, 768), (257, 300, 2048), (300, 10240, 1024)]:
             blk = ib.synth_host(type_, rows, cols, seed=700 + T + rows + type_)
             X = rng.standard_normal((T, cols)).astype(np.float32)
             W = port.dequantize(type_, blk, rows * cols).reshape(rows, cols).astype(np.float64)

@@ -142,7 +142,10 @@ def test_gemm_q_paths_vs_oracle(cuda, port, type_, path):
     rng = np.random.default_rng(700 + type_)
     try:
         ib.gemm_set_path(path)
-        for T, rows, cols in [(257, 300, 2048), (128, 128, 4096), (17, 513, 1536), (600, 130, 768)]:
+        # (300, 10240, 1024): 160 tiles on 148 SMs, so the planes kernel splits the last
+        # wave's 12 tiles along K and reduces their parts
+        for T, rows, cols in [(257, 300, 2048), (128, 128, 4096), (17, 513, 1536), (600, 130, 768),
+                              (300, 10240, 1024)]:
             blk = ib.synth_host(type_, rows, cols, seed=7000 + T + rows + type_)
             X = rng.standard_normal((T, cols)).astype(np.float32)
             W = port.dequantize(type_, blk, rows * cols).reshape(rows, cols)
@@ -163,7 +166,7 @@ def test_gemm_on_prepared_planes_matches_gemm_q(cuda, type_):
     rng = np.random.default_rng(900 + type_)
     try:
         ib.gemm_set_path(ib.GEMM_TC_PLANES)
-        for T, rows, cols in [(257, 300, 2048), (1, 130, 768), (40, 513, 1536)]:
+        for T, rows, cols in [(257, 300, 2048), (1, 130, 768), (40, 513, 1536), (300, 10240, 1024)]:
             blk = to_dev(cuda, ib.synth_host(type_, rows, cols, seed=9000 + T + rows + type_))
             X = to_dev(cuda, rng.standard_normal((T, cols)).astype(np.float32))
             want = ib.gemm_q(type_, blk, X, T, rows, cols)
