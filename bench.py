@@ -568,12 +568,14 @@ def run_sweep(ib, args):
             e1.record()
             torch.cuda.synchronize()
             dq_ms = e0.elapsed_time(e1) / 4
+            i16_ms = time_dequant_i16(ib, t, Ws, rows, cols)
             line = {"sweep": "gemv", "format": fname, "rows": rows, "cols": cols,
                     "gemv_bytes": nbytes, "gemv_us_chained": res[True] * 1e3,
                     "gemv_gbs_chained": nbytes / (res[True] * 1e-3) / 1e9,
                     "gemv_us_standalone": res[False] * 1e3,
                     "gemv_gbs_standalone": nbytes / (res[False] * 1e-3) / 1e9,
                     "dequant_f32_gbs": (packed + 4 * rows * cols) / (dq_ms * 1e-3) / 1e9,
+                    "dequant_i16_gbs": (packed + 2 * rows * cols + 4 * rows) / (i16_ms * 1e-3) / 1e9,
                     "peak_gbs": peak, "peak_kind": peak_kind}
             if ref is not None and (rows, cols) == (4096, 4096):
                 blk = Ws[0].cpu().numpy()
@@ -589,7 +591,61 @@ def run_sweep(ib, args):
             print(json.dumps(line), flush=True)
             del Ws, out, slab
             torch.cuda.empty_cache()
+    # the formats the reference sizes but does not decode: the decode-as-you-go GEMV
+    extra = {t: ib.TYPE_NAMES[t] for t in ib.EXTRA_QUANT_TYPES}
+    for t, fname in extra.items():
+        for rows, cols in shapes:
+            packed = ib.packed_nbytes(t, rows, cols)
+            n = max(2, math.ceil(260e6 / packed))
+            Ws = [ib.synth_device(t, rows, cols, gw.tensor_seed(7, f"sweep{t}_{i}"), 0.02)
+                  for i in range(n)]
+            x = torch.randn(cols, device="cuda")
+            y = torch.empty(rows, device="cuda")
+            reps = max(4 * n, 16)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for i in range(n):
+                    ib.gemv_q(t, Ws[i], x, rows, cols, y=y, stream=s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    ib.gemv_q(t, Ws[i % n], x, rows, cols, y=y, stream=s)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                g.replay()
+                torch.cuda.synchronize()
+                e0.record(s)
+                g.replay()
+                e1.record(s)
+            torch.cuda.synchronize()
+            gemv_ms = e0.elapsed_time(e1) / reps
+            del g
+            nbytes = packed + 4 * cols + 4 * rows
+            i16_ms = time_dequant_i16(ib, t, Ws, rows, cols)
+            print(json.dumps({"sweep": "gemv", "format": fname, "rows": rows, "cols": cols,
+                              "kernel": "gemv_deq_kernel", "gemv_bytes": nbytes,
+                              "gemv_us_standalone": gemv_ms * 1e3,
+                              "gemv_gbs_standalone": nbytes / (gemv_ms * 1e-3) / 1e9,
+                              "dequant_i16_gbs": (packed + 2 * rows * cols + 4 * rows) / (i16_ms * 1e-3) / 1e9,
+                              "peak_gbs": peak, "peak_kind": peak_kind}), flush=True)
+            del Ws
+            torch.cuda.empty_cache()
     return 0
+
+
+def time_dequant_i16(ib, t, Ws, rows, cols):
+    """Dequantisation to the reference's per-row INT16 (make_weight), ms per matrix over
+    distinct copies (algorithmic bytes: packed in, 2 per element and 4 per row out)."""
+    import torch
+    ib.dequantize_i16(t, Ws[0], rows, cols)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(4):
+        ib.dequantize_i16(t, Ws[i % len(Ws)], rows, cols)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 4
 
 
 def main():
