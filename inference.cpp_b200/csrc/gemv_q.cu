@@ -317,23 +317,108 @@ static int launch_gemv_q(const uint8_t* W, const float* x, float* y, int64_t row
 
 // ---------------------------------------------------------------------------
 // Q4_1, Q2_K, Q3_K, Q5_K: decode-as-you-go GEMV, lanes striding over the row's
-// 8-element groups (the bit-exact deq8 of quant.cuh), NR rows per warp sharing each
-// x load, FP32 accumulation and a shuffle reduction.
+// 8-element groups (deq8w: the bit-exact values of quant.cuh's deq8), NR rows per warp
+// sharing each x load, FP32 accumulation and a shuffle reduction.
 // ---------------------------------------------------------------------------
+// deq8 of quant.cuh for the added formats with word loads instead of byte loads (the
+// GEMV's blocks are aligned: Q5_K 16 bytes, Q4_1 and Q2_K 4, Q3_K 2); the same float
+// operations in the same order, so the same values.
+__device__ __forceinline__ uint32_t ldg32(const uint8_t* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
+__device__ __forceinline__ uint32_t ldg16(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+template <int TYPE>
+__device__ __forceinline__ void deq8w(const uint8_t* blk, int g, float* y) {
+    if constexpr (TYPE == IB_TYPE_Q4_1) {
+        const uint32_t hm = ldg32(blk);
+        const float d = h2f(hm & 0xFFFF), m = h2f(hm >> 16);
+        const uint8_t* qs = blk + 4 + 8 * (g & 1);
+        const uint32_t w0 = ldg32(qs), w1 = ldg32(qs + 4);
+        const int sh = (g >> 1) * 4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t byte = byte_of(i < 4 ? w0 : w1, i & 3);
+            y[i] = __fadd_rn(__fmul_rn((float)((byte >> sh) & 0xF), d), m);
+        }
+    } else if constexpr (TYPE == IB_TYPE_Q5_K) {
+        const uint32_t hm = ldg32(blk);
+        const float d = h2f(hm & 0xFFFF), dmin = h2f(hm >> 16);
+        const int p = g >> 3, h = (g >> 2) & 1, l0 = 8 * (g & 3), j = 2 * p + h;
+        const uint32_t s0 = ldg32(blk + 4), s1 = ldg32(blk + 8), s2 = ldg32(blk + 12);
+        // get_scale_min_k4(j) on the 12 scale bytes
+        auto sb = [&](int i) { return i < 4 ? byte_of(s0, i) : i < 8 ? byte_of(s1, i - 4) : byte_of(s2, i - 8); };
+        int sc, m;
+        if (j < 4) {
+            sc = (int)(sb(j) & 63);
+            m = (int)(sb(j + 4) & 63);
+        } else {
+            sc = (int)((sb(j + 4) & 0xF) | ((sb(j - 4) >> 6) << 4));
+            m = (int)((sb(j + 4) >> 4) | ((sb(j) >> 6) << 4));
+        }
+        const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(blk + 48 + 32 * p + l0));
+        const uint2 qh = __ldg(reinterpret_cast<const uint2*>(blk + 16 + l0));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t qb = byte_of(i < 4 ? q.x : q.y, i & 3);
+            const uint32_t hb = byte_of(i < 4 ? qh.x : qh.y, i & 3);
+            const int v = (int)(((qb >> (4 * h)) & 0xF) | (((hb >> j) & 1) << 4));
+            y[i] = __fsub_rn(__fmul_rn(d1, (float)v), m1);
+        }
+    } else if constexpr (TYPE == IB_TYPE_Q2_K) {
+        const uint32_t dd = ldg32(blk + 80);
+        const float d = h2f(dd & 0xFFFF), dmin = h2f(dd >> 16);
+        const int e0 = 8 * g, h = e0 >> 7, j = (e0 >> 5) & 3, k = (e0 >> 4) & 1, l0 = e0 & 15;
+        const int scm = (int)__ldg(blk + (e0 >> 4));
+        const float dl = __fmul_rn(d, (float)(scm & 0xF)), ml = __fmul_rn(dmin, (float)(scm >> 4));
+        const uint8_t* q = blk + 16 + 32 * h + 16 * k + l0;
+        const uint32_t w0 = ldg32(q), w1 = ldg32(q + 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            y[i] = __fsub_rn(__fmul_rn(dl, (float)((byte_of(i < 4 ? w0 : w1, i & 3) >> (2 * j)) & 3)), ml);
+    } else {
+        static_assert(TYPE == IB_TYPE_Q3_K, "deq8w: unsupported type");
+        const float d = h2f(ldg16(blk + 108));
+        const int e0 = 8 * g, h = e0 >> 7, j = (e0 >> 5) & 3, k = (e0 >> 4) & 1, l0 = e0 & 15;
+        const int si = e0 >> 4;
+        const int lo = si < 8 ? (int)(__ldg(blk + 96 + si) & 0xF) : (int)(__ldg(blk + 96 + si - 8) >> 4);
+        const int hi = (int)((__ldg(blk + 104 + (si & 3)) >> (2 * (si >> 2))) & 3);
+        const float dl = __fmul_rn(d, (float)((lo | (hi << 4)) - 32));
+        const uint8_t* q = blk + 32 + 32 * h + 16 * k + l0;
+        const uint8_t* hm = blk + 16 * k + l0;
+        uint32_t qw[4], hw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qw[i] = ldg16(q + 2 * i);
+            hw[i] = ldg16(hm + 2 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t qb = (qw[i >> 1] >> (8 * (i & 1))) & 0xFFu;
+            const uint32_t hb = (hw[i >> 1] >> (8 * (i & 1))) & 0xFFu;
+            const int v = (int)((qb >> (2 * j)) & 3) - (((hb >> (4 * h + j)) & 1) ? 0 : 4);
+            y[i] = __fmul_rn(dl, (float)v);
+        }
+    }
+}
+
 template <int TYPE, int NR>
 __global__ void __launch_bounds__(128) gemv_deq_kernel(const uint8_t* __restrict__ W,
                                                        const float* __restrict__ x,
                                                        float* __restrict__ y, int64_t rows,
                                                        int64_t cols) {
+    // the CTA's 4 warps split the NR rows' groups (short dependent chains per warp); the
+    // loop is unrolled so each lane has several groups' loads in flight
     constexpr int BE = QFmt<TYPE>::BE, BB = QFmt<TYPE>::BB, GPB = BE / 8;
+    __shared__ float red[4][NR];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * NR;
-    if (row0 >= rows) return;
+    const int64_t row0 = (int64_t)blockIdx.x * NR;
     const int64_t gpr = cols / 8, row_bytes = cols / BE * BB;
     float acc[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) acc[r] = 0.f;
-    for (int64_t g = lane; g < gpr; g += 32) {
+#pragma unroll 2
+    for (int64_t g = threadIdx.x; g < gpr; g += 128) {
         const float4 a = ldx4(x + g * 8), b = ldx4(x + g * 8 + 4);
         const int64_t blk = g / GPB;
         const int sub = (int)(g - blk * GPB);
@@ -341,7 +426,7 @@ __global__ void __launch_bounds__(128) gemv_deq_kernel(const uint8_t* __restrict
         for (int r = 0; r < NR; ++r) {
             if (row0 + r >= rows) break;
             float v[8];
-            deq8<TYPE>(W + (row0 + r) * row_bytes + blk * BB, sub, v);
+            deq8w<TYPE>(W + (row0 + r) * row_bytes + blk * BB, sub, v);
             float t = acc[r];
             t = fmaf(v[0], a.x, t);
             t = fmaf(v[1], a.y, t);
@@ -357,16 +442,21 @@ __global__ void __launch_bounds__(128) gemv_deq_kernel(const uint8_t* __restrict
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
         const float v = warp_sum(acc[r]);
-        if (lane == 0 && row0 + r < rows) y[row0 + r] = v;
+        if (lane == 0) red[warp][r] = v;
     }
+    __syncthreads();
+    if (threadIdx.x < NR && row0 + threadIdx.x < rows)
+        y[row0 + threadIdx.x] = (red[0][threadIdx.x] + red[1][threadIdx.x]) +
+                                (red[2][threadIdx.x] + red[3][threadIdx.x]);
 }
 
 template <int TYPE>
 static int launch_gemv_deq(const uint8_t* W, const float* x, float* y, int64_t rows,
                            int64_t cols, cudaStream_t st) {
-    constexpr int WARPS = 4, NR = 2;
-    const int64_t grid = (rows + WARPS * NR - 1) / (WARPS * NR);
-    gemv_deq_kernel<TYPE, NR><<<(unsigned)grid, WARPS * 32, 0, st>>>(W, x, y, rows, cols);
+    constexpr int NR = 2;
+    const int64_t grid = (rows + NR - 1) / NR;
+    IB_REQUIRE(grid <= 0x7FFFFFFF, "gemv: too many rows");
+    gemv_deq_kernel<TYPE, NR><<<(unsigned)grid, 128, 0, st>>>(W, x, y, rows, cols);
     IB_LAUNCH_CHECK("gemv_deq_kernel");
     return IB_OK;
 }
@@ -390,7 +480,9 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     cudaStream_t st = as_stream(stream);
     const uint8_t* W = (const uint8_t*)dev_W;
     if (is_extra_quant(type)) {
-        IB_REQUIRE(((uintptr_t)W & 1) == 0, "weights must be 2-byte aligned");
+        const uintptr_t align = type == IB_TYPE_Q5_K ? 16 : type == IB_TYPE_Q3_K ? 2 : 4;
+        IB_REQUIRE(((uintptr_t)W & (align - 1)) == 0,
+                   "weights must be aligned to " + std::to_string(align) + " bytes");
         switch (type) {
             case IB_TYPE_Q4_1: return launch_gemv_deq<IB_TYPE_Q4_1>(W, dev_x, dev_y, rows, cols, st);
             case IB_TYPE_Q2_K: return launch_gemv_deq<IB_TYPE_Q2_K>(W, dev_x, dev_y, rows, cols, st);
