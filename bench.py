@@ -513,7 +513,7 @@ def run_sweep(ib, args):
     from inference_cpp_b200 import gguf_writer as gw
     peak, peak_kind = measured_peaks()
     names = {ib.Q4_0: "Q4_0", ib.Q5_0: "Q5_0", ib.Q5_1: "Q5_1", ib.Q8_0: "Q8_0",
-             ib.Q4_K: "Q4_K", ib.Q6_K: "Q6_K"}
+             ib.Q4_K: "Q4_K", ib.Q5_K: "Q5_K", ib.Q6_K: "Q6_K"}
     shapes = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
     ref = None
     if not args.no_cpu_baseline:
@@ -577,7 +577,7 @@ def run_sweep(ib, args):
                     "dequant_f32_gbs": (packed + 4 * rows * cols) / (dq_ms * 1e-3) / 1e9,
                     "dequant_i16_gbs": (packed + 2 * rows * cols + 4 * rows) / (i16_ms * 1e-3) / 1e9,
                     "peak_gbs": peak, "peak_kind": peak_kind}
-            if ref is not None and (rows, cols) == (4096, 4096):
+            if ref is not None and (rows, cols) == (4096, 4096) and t not in ib.EXTRA_QUANT_TYPES:
                 blk = Ws[0].cpu().numpy()
                 xs = np.random.default_rng(0).standard_normal(cols).astype(np.float32)
                 t0 = time.perf_counter()
@@ -591,8 +591,8 @@ def run_sweep(ib, args):
             print(json.dumps(line), flush=True)
             del Ws, out, slab
             torch.cuda.empty_cache()
-    # the formats the reference sizes but does not decode: the decode-as-you-go GEMV
-    extra = {t: ib.TYPE_NAMES[t] for t in ib.EXTRA_QUANT_TYPES}
+    # the other formats the reference sizes but does not decode: the decode-as-you-go GEMV
+    extra = {t: ib.TYPE_NAMES[t] for t in ib.EXTRA_QUANT_TYPES if t not in names}
     for t, fname in extra.items():
         for rows, cols in shapes:
             packed = ib.packed_nbytes(t, rows, cols)

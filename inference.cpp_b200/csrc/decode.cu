@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "gemv_math.cuh"
+#include "gemv_mma.cuh"
 #include "pdl.cuh"
 #include "pipeline.cuh"
 #include "slab.cuh"
@@ -36,7 +37,11 @@ namespace ib {
 
 static __device__ int g_decode_fault;
 
-bool slab_kquant(int type) { return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K; }
+bool slab_kquant(int type) {
+    return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K || type == IB_TYPE_Q5_K;
+}
+
+bool slab_supported(int type) { return gemv_mma_supported(type) || type == IB_TYPE_Q5_K; }
 
 // After a head GEMV with an ARGMAX exchange: *best <- the maximum key over the ranks.
 __global__ void tp_key_max_kernel(const TpExchange x, unsigned long long* best) {
@@ -352,22 +357,36 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
 // boundaries), a multiple of 16, and congruent to 32 (Q4_K's 8-byte loads) or 16 (the
 // 2/4-byte loads of the other formats) modulo 128.
 static int ring_slot(int type, int chunk, bool pad) {
-    const int want = type == IB_TYPE_Q4_K ? 32 : 16;
+    const int want = (type == IB_TYPE_Q4_K || type == IB_TYPE_Q5_K) ? 32 : 16;
     int s = (chunk + (pad ? 16 : 0) + 15) / 16 * 16;
     while (s % 128 != want) s += 16;
     return s;
 }
 
-static int pair_of(int type) {  // 0: K-quants, 1: Q4_0/Q8_0, 2: Q5_0/Q5_1, -1: none
-    switch (type) {
-        case IB_TYPE_Q4_K:
-        case IB_TYPE_Q6_K: return 0;
-        case IB_TYPE_Q4_0:
-        case IB_TYPE_Q8_0: return 1;
-        case IB_TYPE_Q5_0:
-        case IB_TYPE_Q5_1: return 2;
+// Format pairs of the fused kernels: 0 Q4_K/Q6_K, 1 Q4_0/Q8_0, 2 Q5_0/Q5_1, 3 Q5_K/Q6_K
+// (Q6_K serves both K-quant pairs).
+static bool in_pair(int type, int pr) {
+    switch (pr) {
+        case 0: return type == IB_TYPE_Q4_K || type == IB_TYPE_Q6_K;
+        case 1: return type == IB_TYPE_Q4_0 || type == IB_TYPE_Q8_0;
+        case 2: return type == IB_TYPE_Q5_0 || type == IB_TYPE_Q5_1;
+        case 3: return type == IB_TYPE_Q5_K || type == IB_TYPE_Q6_K;
     }
-    return -1;
+    return false;
+}
+
+// The pair of a GEMV's segments (-1: none): Q5_K anywhere selects pair 3.
+static int pair_of(const FusedGemv& p) {
+    int pr = -1;
+    for (int s = 0; s < p.n_seg && s < 3; ++s) {
+        const int t = p.type[s];
+        const int q = t == IB_TYPE_Q5_K ? 3 : t == IB_TYPE_Q4_K || t == IB_TYPE_Q6_K ? 0
+                    : t == IB_TYPE_Q4_0 || t == IB_TYPE_Q8_0 ? 1
+                    : t == IB_TYPE_Q5_0 || t == IB_TYPE_Q5_1 ? 2 : -1;
+        if (q < 0) return -1;
+        if (q == 3 || pr < 0) pr = q;
+    }
+    return pr;
 }
 
 struct OccKey {
@@ -406,12 +425,12 @@ static int max_ctas(const void* f, int threads, size_t smem, int* out) {
 
 bool fused_gemv_supported(const FusedGemv& p, int epi) {
     if (p.n_seg < 1 || p.n_seg > 3 || p.K <= 0 || !p.slab || ((uintptr_t)p.slab & 15)) return false;
-    const int pr = pair_of(p.type[0]);
+    const int pr = pair_of(p);
     if (pr < 0) return false;
-    const int be = pr == 0 ? 256 : 32;
+    const int be = (pr == 0 || pr == 3) ? 256 : 32;
     if (p.K % be) return false;
     for (int s = 0; s < p.n_seg; ++s) {
-        if (pair_of(p.type[s]) != pr || !p.W[s] || p.rows[s] <= 0) return false;
+        if (!in_pair(p.type[s], pr) || !p.W[s] || p.rows[s] <= 0) return false;
         if (((uintptr_t)p.W[s] % 16) != 0) return false;
         if (!p.paired && s < p.n_seg - 1 && p.rows[s] % 16) return false;
     }
@@ -503,8 +522,9 @@ int fused_gemv_launch(const FusedGemv& p, int pro, int epi, cudaStream_t st, boo
         set_error("fused GEMV: a normed input needs its sums of squares");
         return IB_ERR_INVALID;
     }
-    switch (pair_of(p.type[0])) {
+    switch (pair_of(p)) {
         case 0: return launch_pair<IB_TYPE_Q4_K, IB_TYPE_Q6_K>(p, pro, epi, st, pdl);
+        case 3: return launch_pair<IB_TYPE_Q5_K, IB_TYPE_Q6_K>(p, pro, epi, st, pdl);
         case 1: return launch_pair<IB_TYPE_Q4_0, IB_TYPE_Q8_0>(p, pro, epi, st, pdl);
         case 2: return launch_pair<IB_TYPE_Q5_0, IB_TYPE_Q5_1>(p, pro, epi, st, pdl);
     }

@@ -61,6 +61,9 @@ __host__ __device__ inline size_t slab_total_bytes(int K, bool kquant) {
 // True for the K-quant formats (slab geometry SE 2048 / GS 256).
 bool slab_kquant(int type);
 
+// True for the formats the fused limb-slab GEMV decodes (the six of gemv_mma and Q5_K).
+bool slab_supported(int type);
+
 // slab <- limbs of x (norm == nullptr) or of x * norm; ssq[g] <- sum of x^2 over scale
 // group g (when ssq != nullptr; the RMSNorm of x is then applied in the GEMV
 // epilogue as 1 / sqrt(sum(ssq) / K + eps)).  K must be a multiple of GS.

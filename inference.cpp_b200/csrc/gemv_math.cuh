@@ -187,6 +187,62 @@ __device__ __forceinline__ void block_q4k(const uint8_t* ba, const uint8_t* bb, 
     }
 }
 
+// Q5_K block kb: Q4_K's arithmetic with 5-bit quants.  The same d, dmin and 6-bit scale /
+// min header, qs at byte 48 (Q4_K: 16), and the fifth bit of element 64p + 32h + l in
+// qh[l] (byte 16 + l) at bit 2p + h.  Lane t's bytes [8t, 8t+8) of each 32-byte chunk
+// pair with qh bytes [8t, 8t+8): the bits go in at bit 4 of each quant byte, so the
+// MMA's unsigned-fitting s8 operands hold q in [0, 31] (GGUF block layout; the reference
+// sizes this format but does not decode it).
+template <bool SMEM, bool XS>
+__device__ __forceinline__ void block_q5k(const uint8_t* ba, const uint8_t* bb, int kb,
+                                          const XLimbs& xb, const LaneCtx& c, float& acc_a,
+                                          float& acc_b) {
+    using L = Ld<SMEM>;
+    const uint4 ha = L::u128(ba), hb = L::u128(bb);
+    const uint2 qha = L::u64(ba + 16 + 8 * c.t), qhb = L::u64(bb + 16 + 8 * c.t);
+    uint2 qa[4], qb[4], lx[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        qa[p] = L::u64(ba + 48 + 32 * p + 8 * c.t);
+        qb[p] = L::u64(bb + 48 + 32 * p + 8 * c.t);
+        lx[p] = LdX<XS>::u64(xb.limbs + ((size_t)kb * 8 + 2 * p + c.upper) * 128 + c.lim * 32 +
+                             8 * c.t);
+    }
+    const float s = LdX<XS>::f(xb.scale + kb);
+    const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
+    const uint32_t sca_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+    const uint32_t ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+    const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
+    const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+    const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+    const float da = h2f_fast(ha.x & 0xFFFF) * s * c.cw, dma = -h2f_fast(ha.x >> 16) * c.tm;
+    const float db = h2f_fast(hb.x & 0xFFFF) * s * c.cw, dmb = -h2f_fast(hb.x >> 16) * c.tm;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t M = 0x0F0F0F0Fu, H = 0x01010101u;
+        // fifth bits of this chunk's low (2p) and high (2p + 1) sub-blocks, at bit 4
+        const uint32_t la0 = ((qha.x >> (2 * p)) & H) << 4, ua0 = ((qha.x >> (2 * p + 1)) & H) << 4;
+        const uint32_t la1 = ((qha.y >> (2 * p)) & H) << 4, ua1 = ((qha.y >> (2 * p + 1)) & H) << 4;
+        const uint32_t lb0 = ((qhb.x >> (2 * p)) & H) << 4, ub0 = ((qhb.x >> (2 * p + 1)) & H) << 4;
+        const uint32_t lb1 = ((qhb.y >> (2 * p)) & H) << 4, ub1 = ((qhb.y >> (2 * p + 1)) & H) << 4;
+        int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+        mma_k32_acc((qa[p].x & M) | la0, (qb[p].x & M) | lb0, ((qa[p].x >> 4) & M) | ua0,
+                    ((qb[p].x >> 4) & M) | ub0, c.upper ? 0u : lx[p].x, c.upper ? lx[p].x : 0u,
+                    d0, d1, d2, d3);
+        mma_k32_acc((qa[p].y & M) | la1, (qb[p].y & M) | lb1, ((qa[p].y >> 4) & M) | ua1,
+                    ((qb[p].y >> 4) & M) | ub1, c.upper ? 0u : lx[p].y, c.upper ? lx[p].y : 0u,
+                    d0, d1, d2, d3);
+        const int sub = 2 * p + c.half, bi = sub & 3;
+        const float sum = LdX<XS>::f(xb.sum32 + (size_t)kb * 8 + sub);
+        const uint32_t swa = p < 2 ? sca_lo : sca_hi, mwa = p < 2 ? ma_lo : ma_hi;
+        const uint32_t swb = p < 2 ? scb_lo : scb_hi, mwb = p < 2 ? mb_lo : mb_hi;
+        acc_a = fmaf(da * byte_f(swa, bi), (float)(d0 * 128 + d1), acc_a);
+        acc_a = fmaf(dma * byte_f(mwa, bi), sum, acc_a);
+        acc_b = fmaf(db * byte_f(swb, bi), (float)(d2 * 128 + d3), acc_b);
+        acc_b = fmaf(dmb * byte_f(mwb, bi), sum, acc_b);
+    }
+}
+
 // Q6_K block kb.  Element e = 128c + 32gg + l, 16-element sub-block 8c + 2gg + l/16.
 // For (c, h = l/16) lane t covers l = 16h + 4t + i: ql bytes at 64c + 16h + 4t (gg 0:
 // low, gg 2: high nibbles) and 64c + 32 + 16h + 4t (gg 1, 3), qh at 128 + 32c + 16h +
@@ -450,10 +506,10 @@ template <int TYPE>
 struct Fmt {
     static constexpr int BB = TYPE == IB_TYPE_Q4_0 ? 18 : TYPE == IB_TYPE_Q5_0 ? 22 :
                               TYPE == IB_TYPE_Q5_1 ? 24 : TYPE == IB_TYPE_Q8_0 ? 34 :
-                              TYPE == IB_TYPE_Q4_K ? 144 : 210;
-    static constexpr bool K = TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K;
-    // blocks per TMA stage (per row): 1152 B (Q4_K), 1680 B (Q6_K), 32 blocks otherwise
-    static constexpr int KB = TYPE == IB_TYPE_Q4_K ? 8 : TYPE == IB_TYPE_Q6_K ? 8 : 32;
+                              TYPE == IB_TYPE_Q4_K ? 144 : TYPE == IB_TYPE_Q5_K ? 176 : 210;
+    static constexpr bool K = TYPE == IB_TYPE_Q4_K || TYPE == IB_TYPE_Q6_K || TYPE == IB_TYPE_Q5_K;
+    // blocks per TMA stage (per row): 1152 B (Q4_K), 1408 B (Q5_K), 1680 B (Q6_K), 32 blocks otherwise
+    static constexpr int KB = K ? 8 : 32;
     static constexpr int CHUNK = KB * BB;
     static constexpr int UNIT = K ? 1 : 2;  // blocks handled per block_math call
 };
@@ -464,6 +520,7 @@ __device__ __forceinline__ void block_math(const uint8_t* ba, const uint8_t* bb,
                                            float& acc_b) {
     if constexpr (TYPE == IB_TYPE_Q4_K) block_q4k<SMEM, XS>(ba, bb, kb, xb, c, acc_a, acc_b);
     else if constexpr (TYPE == IB_TYPE_Q6_K) block_q6k<SMEM, XS>(ba, bb, kb, xb, c, acc_a, acc_b);
+    else if constexpr (TYPE == IB_TYPE_Q5_K) block_q5k<SMEM, XS>(ba, bb, kb, xb, c, acc_a, acc_b);
     else block_q32<TYPE, SMEM, XS>(ba, bb, kb, kb + 1 < nb, xb, c, acc_a, acc_b);
 }
 

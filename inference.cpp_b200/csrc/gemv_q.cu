@@ -479,18 +479,7 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
     IB_REQUIRE(cols % be == 0, "cols must be a multiple of the block size");
     cudaStream_t st = as_stream(stream);
     const uint8_t* W = (const uint8_t*)dev_W;
-    if (is_extra_quant(type)) {
-        const uintptr_t align = type == IB_TYPE_Q5_K ? 16 : type == IB_TYPE_Q3_K ? 2 : 4;
-        IB_REQUIRE(((uintptr_t)W & (align - 1)) == 0,
-                   "weights must be aligned to " + std::to_string(align) + " bytes");
-        switch (type) {
-            case IB_TYPE_Q4_1: return launch_gemv_deq<IB_TYPE_Q4_1>(W, dev_x, dev_y, rows, cols, st);
-            case IB_TYPE_Q2_K: return launch_gemv_deq<IB_TYPE_Q2_K>(W, dev_x, dev_y, rows, cols, st);
-            case IB_TYPE_Q3_K: return launch_gemv_deq<IB_TYPE_Q3_K>(W, dev_x, dev_y, rows, cols, st);
-            default: return launch_gemv_deq<IB_TYPE_Q5_K>(W, dev_x, dev_y, rows, cols, st);
-        }
-    }
-    if (cols <= (1 << 30) && rows < (1ll << 31) && gemv_mma_supported(type)) {
+    if (cols <= (1 << 30) && rows < (1ll << 31) && slab_supported(type)) {
         // limb slab of x, then the TMA-staged GEMV (decode.cu)
         const bool kq = slab_kquant(type);
         FusedGemv f = {};
@@ -509,6 +498,17 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
                 return r;
             f.slab = (const uint8_t*)ws;
             return fused_gemv_launch(f, PRO_PLAIN, EPI_STORE, st, false);
+        }
+    }
+    if (is_extra_quant(type)) {  // the decode-as-you-go GEMV (Q5_K: bases off 16 bytes)
+        const uintptr_t align = type == IB_TYPE_Q5_K ? 16 : type == IB_TYPE_Q3_K ? 2 : 4;
+        IB_REQUIRE(((uintptr_t)W & (align - 1)) == 0,
+                   "weights must be aligned to " + std::to_string(align) + " bytes");
+        switch (type) {
+            case IB_TYPE_Q4_1: return launch_gemv_deq<IB_TYPE_Q4_1>(W, dev_x, dev_y, rows, cols, st);
+            case IB_TYPE_Q2_K: return launch_gemv_deq<IB_TYPE_Q2_K>(W, dev_x, dev_y, rows, cols, st);
+            case IB_TYPE_Q3_K: return launch_gemv_deq<IB_TYPE_Q3_K>(W, dev_x, dev_y, rows, cols, st);
+            default: return launch_gemv_deq<IB_TYPE_Q5_K>(W, dev_x, dev_y, rows, cols, st);
         }
     }
     if (gemv_mma_supported(type) && ((uintptr_t)W % gemv_mma_align(type)) == 0 &&
@@ -546,7 +546,7 @@ extern "C" int ib_gemv_q(int type, const void* dev_W, const float* dev_x, float*
 
 extern "C" int ib_slab_bytes(int type, int64_t cols, size_t* bytes) {
     IB_REQUIRE(bytes && cols > 0 && cols <= (1 << 30), "bad arguments");
-    if (!gemv_mma_supported(type)) {
+    if (!slab_supported(type)) {
         set_error(std::string("ib_slab_bytes: unsupported type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }
@@ -557,7 +557,7 @@ extern "C" int ib_slab_bytes(int type, int64_t cols, size_t* bytes) {
 extern "C" int ib_limb_slab(int type, const float* dev_x, int64_t cols, void* dev_slab, void* stream) {
     IB_REQUIRE(dev_x && dev_slab && cols > 0 && cols <= (1 << 30), "bad arguments");
     IB_REQUIRE(((uintptr_t)dev_slab & 15) == 0, "slab must be 16-byte aligned");
-    if (!gemv_mma_supported(type)) {
+    if (!slab_supported(type)) {
         set_error(std::string("ib_limb_slab: unsupported type ") + type_name(type));
         return IB_ERR_UNSUPPORTED;
     }

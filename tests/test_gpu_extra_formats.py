@@ -2,8 +2,9 @@
 decode (src/gguf/quantization.cpp:201-204 throw).  The oracle's restatement of their
 GGUF layouts is pinned to the `gguf` package in tests/test_extra_formats_cpu.py; here the
 device paths are checked against it: dequantisation (FP32 and the INT16 requantisation)
-bit-exact, the embedding gather bit-exact, the decode-as-you-go GEMV and both prompt-GEMM
-kernels within 2e-5 * sum|w x| of a float64 product, and a model with these weights
+bit-exact, the embedding gather bit-exact, the GEMVs (decode-as-you-go; Q5_K on the fused
+int8 tensor-core kernel) and both prompt-GEMM kernels within 2e-5 * sum|w x| of a float64
+product, and a model with these weights
 decoding the oracle's greedy tokens with logits within 1e-3 of the row maximum.
 """
 import numpy as np
@@ -87,6 +88,26 @@ def test_gemv_q_vs_float64(cuda, port, type_):
         assert np.all(np.abs(y - W @ x.astype(np.float64)) <= bound), (rows, cols)
 
 
+def test_q5k_limb_slab_gemv(cuda, port):
+    """Q5_K on the limb-slab API (one slab shared by two matrices, the second launch a
+    chained link) within the GEMV bound; the other added formats have no slab path."""
+    torch = cuda
+    rng = np.random.default_rng(5)
+    for rows, cols in [(64, 512), (4096, 4096), (1000, 14336)]:
+        x = rng.standard_normal(cols).astype(np.float32)
+        slab = ib.limb_slab(ib.Q5_K, to_dev(cuda, x), cols)
+        for k in range(2):
+            blk = ib.synth_host(ib.Q5_K, rows, cols, seed=900 + 31 * k + rows)
+            y = ib.gemv_q_slab(ib.Q5_K, to_dev(cuda, blk), slab, rows, cols, chained=k == 1)
+            W = port.dequantize(ib.Q5_K, blk, rows * cols).reshape(rows, cols).astype(np.float64)
+            bound = RTOL * (np.abs(W) @ np.abs(x.astype(np.float64))) + 1e-30
+            err = np.abs(y.cpu().numpy() - W @ x.astype(np.float64))
+            assert np.all(err <= bound), (rows, cols, k)
+    for t in (ib.Q4_1, ib.Q2_K, ib.Q3_K):
+        with pytest.raises(RuntimeError, match="unsupported"):
+            ib.limb_slab(t, torch.zeros(256, device="cuda"), 256)
+
+
 @pytest.mark.parametrize("type_", FORMATS, ids=NAME.get)
 @pytest.mark.parametrize("path", [ib.GEMM_TENSOR_CORES, ib.GEMM_CUDA_CORES, ib.GEMM_TC_PLANES],
                          ids=["auto", "simt", "tc-planes"])
@@ -116,7 +137,16 @@ def extra_cfgs():
         gw.LlamaConfig("tiny-q2k-q41", 2, 256, 4, 4, 512, 300, 160, 10000.0, 1e-5,
                        embed_type=ib.Q4_1, linear_type=ib.Q2_K, attn_v_type=ib.Q4_1,
                        ffn_down_type=ib.Q4_1, output_type=ib.Q2_K),
+        # the Q5_K_M mix: Q5_K linears, Q6_K attn_v / ffn_down / output
+        gw.LlamaConfig("tiny-q5k-q6k", 2, 512, 8, 2, 1024, 300, 160, 10000.0, 1e-5,
+                       embed_type=ib.Q5_K, linear_type=ib.Q5_K, attn_v_type=ib.Q6_K,
+                       ffn_down_type=ib.Q6_K, output_type=ib.Q6_K),
     ]
+
+
+# Q5_K with Q6_K runs on the fused int8 tensor-core GEMVs; the other mixes take the
+# decode-as-you-go GEMV.
+EXPECT_PATH = {"tiny-q5k-q3k": "separate", "tiny-q2k-q41": "separate", "tiny-q5k-q6k": "fused"}
 
 
 @pytest.mark.parametrize("cfg", extra_cfgs(), ids=lambda c: c.name)
@@ -126,7 +156,7 @@ def test_model_with_extra_formats_matches_oracle(cuda, port, cfg):
     n_new = 16
     want, want_logits = port.model(cfg, tensors).generate(prompt, n_new, want_logits=True)
     m = ib.Model.from_tensors(cfg, tensors)
-    assert m.decode_path() == "separate"  # no fused kernel takes these formats
+    assert m.decode_path() == EXPECT_PATH[cfg.name]
     assert list(m.generate(prompt, n_new)[0]) == list(want)
     for i in range(1, n_new):
         tok, p = int(want[prompt.size + i - 1]), prompt.size + i - 1
