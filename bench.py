@@ -13,13 +13,15 @@ no flush is needed between steps.
 
 value:  decode tok/s timed with CUDA events around K device-side steps
         (ib_model_decode_loop: inputs resident, argmax fed back on the device).
-e2e:    the same K steps through the public per-token call ib_model_decode with
-        host buffers (token + position in, next id out every step), wall clock.
+e2e:    the same K steps (same positions and tokens, so the same work) through the
+        public per-token call ib_model_decode with host buffers (token + position in,
+        next id out every step), wall clock.
 roofline: the dominant kernel, the Q4_K fused dequant-GEMV of ffn_gate/ffn_up
         (14336 x 4096), timed alone with CUDA events over all layers' weights.
-cpu_baseline / --impl reference: the reference's own CPU matvec (oracle/_ref, or
-        the C restatement where it was not built) on a bounded sample: one layer's
-        seven projections plus 1/16 of the output head, extrapolated per token.
+cpu_baseline / --impl reference: the reference's own CPU forward (oracle/_ref:
+        Model::forward, one thread) on a bounded sample: a 2-layer copy of the workload
+        (same widths, vocabulary and quant mix), a few single-token forwards,
+        extrapolated to the full layer count (cpu_forward_sample).
 With torchrun (N > 1) the N ranks hold one tensor-parallel model (Megatron split:
 q/k/v and gate/up rows, attn_output and ffn_down input columns, the head's vocabulary
 rows; one exchange of the row-split projections' rows per sublayer over NVLink peer
@@ -770,15 +772,14 @@ def main():
         pos = pos0 + args.steps
         tok = int(toks[-1])
 
-        # e2e: the per-token public call with host buffers
-        m.decode_loop(tok, pos, 2)  # settle
-        pos += 2
+        # e2e: the per-token public call with host buffers, over the timed steps' positions
+        # from the same token (greedy: the same tokens, the same KV rows rewritten)
         torch.cuda.synchronize()
         barrier(world)
         t0 = time.perf_counter()
-        nxt = tok
+        nxt = tok0
         for i in range(e2e_steps):
-            nxt = m.decode(nxt, pos + i)
+            nxt = m.decode(nxt, pos0 + i)
         torch.cuda.synchronize()
         e2e_s = all_max(world, time.perf_counter() - t0)
         clk = clocks.stop()

@@ -633,16 +633,14 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         constexpr int GS = SlabG<true>::GS;
         for (int gl = warp; gl < n_el / GS; gl += ATT_WARPS) {
             float v[GS / 32];
-#pragma unroll
-            for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
+            slab_load<true>(ovals, gl, lane, v);
             slab_write_group<true>(v, (base_el + gl * GS) / GS, slab, lane);
         }
     } else {
         constexpr int GS = SlabG<false>::GS;
         for (int gl = warp; gl < n_el / GS; gl += ATT_WARPS) {
             float v[GS / 32];
-#pragma unroll
-            for (int j = 0; j < GS / 32; ++j) v[j] = ovals[gl * GS + j * 32 + lane];
+            slab_load<false>(ovals, gl, lane, v);
             slab_write_group<false>(v, (base_el + gl * GS) / GS, slab, lane);
         }
     }

@@ -83,33 +83,32 @@ __global__ void __launch_bounds__(256) xq_slab_kernel(float* __restrict__ x,
     const int gi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (gi * GS >= K) return;
     float v[PER];
-#pragma unroll
-    for (int j = 0; j < PER; ++j) v[j] = x[(gi * PER + j) * 32 + lane];
+    slab_load<KQ>(x, gi, lane, v);
     if constexpr (TP) {
         // x += every rank's rows in rank order; a rank's PER words are loaded together
         // (one round trip when they have landed), then any stragglers are polled
         unsigned long long t0 = 0ull;
         bool ok = true;
         for (int q = 0; q < tp.world && ok; ++q) {
-            const uint64_t* src = parts + (size_t)q * tp.stride + gi * GS + lane;
+            const uint64_t* src = parts + (size_t)q * tp.stride;
             uint64_t wv[PER];
 #pragma unroll
-            for (int j = 0; j < PER; ++j) wv[j] = ld_relaxed_sys(src + j * 32);
+            for (int j = 0; j < PER; ++j) wv[j] = ld_relaxed_sys(src + slab_elem<KQ>(gi, j, lane));
 #pragma unroll
             for (int j = 0; j < PER; ++j) {
                 uint32_t w = (uint32_t)wv[j];
                 if ((uint32_t)(wv[j] >> 32) != tag && ok)
-                    ok = wait_tagged(src + j * 32, tag, w, t0, &g_decode_fault);
+                    ok = wait_tagged(src + slab_elem<KQ>(gi, j, lane), tag, w, t0, &g_decode_fault);
                 v[j] += __uint_as_float(w);
             }
         }
 #pragma unroll
-        for (int j = 0; j < PER; ++j) x[(gi * PER + j) * 32 + lane] = v[j];
+        for (int j = 0; j < PER; ++j) x[slab_elem<KQ>(gi, j, lane)] = v[j];
     }
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int i = (gi * PER + j) * 32 + lane;
+        const int i = slab_elem<KQ>(gi, j, lane);
         float t = v[j];
         ss = fmaf(t, t, ss);
         if (norm) t *= norm[i];

@@ -139,7 +139,7 @@ __device__ __forceinline__ void build_group(const float* src, const float* norm,
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int i = gi * GS + 32 * j + lane;
+        const int i = slab_elem<KQ>(gi, j, lane);
         float t = __ldcg(src + i);
         ss = fmaf(t, t, ss);
         if (norm) t *= norm[i];
@@ -412,8 +412,7 @@ __device__ bool attn_task(const StepParams& P, const StepPhase* gph, int t, uint
     const int inst = gph->out_inst;
     for (int gl = warp; gl < n_out / GS; gl += kNWC) {
         float v[PER];
-#pragma unroll
-        for (int j = 0; j < PER; ++j) v[j] = ov[gl * GS + 32 * j + lane];
+        slab_load<KQ>(ov, gl, lane, v);
         const int gi = (base_el + gl * GS) / GS;
         slab_write_group<KQ>(v, gi, slab, lane);
         publish_group<KQ>(P, inst, gi, lane);
