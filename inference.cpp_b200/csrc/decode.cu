@@ -168,7 +168,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     using P = Pair<TA, TB>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], rfull[2], rfree[2];
-    __shared__ int stage_rg[kMaxStages];
+    __shared__ int stage_rg[kMaxStages], stage_st[kMaxStages];
     __shared__ int warps_done;
     __shared__ float red[2][kNWC][16];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -176,6 +176,9 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     const int spg = GEN ? (nb + P::KB - 1) / P::KB : nb / P::KB;  // GEN: the last may be short
     const int stage_bytes = wbytes + P::SLICE;
     const int n_rg = p.paired ? p.rows[0] / 8 : (total_rows(p) + 15) / 16;
+    // work units: row groups, or (K split) halves of row groups, unit u = 2 rg + half
+    const bool ks = k_split<EPI>(p, spg);
+    const int n_units = ks ? 2 * n_rg : n_rg, mid = (spg + 1) >> 1;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -191,9 +194,9 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     __syncthreads();
     pdl_launch_dependents();
     if (warp == kNWC) {
-        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Row groups come
+        // producer: lanes 0..15 copy weight rows, lane 16 the limb slice.  Work units come
         // from the work counter (or the static stride); stage_rg[s] tells the consumers
-        // which row group a stage holds, -1 ends their loop.  Stage slot s and its phase
+        // which unit a stage holds, -1 ends their loop (stage_st[s]: its stage index).  Stage slot s and its phase
         // advance incrementally (no divisions in the loop).  A row that does not start on
         // a 16-byte boundary is copied from the boundary below it (the offset is the same
         // in every stage: a full stage is a multiple of 16 bytes) and its copy length
@@ -206,14 +209,16 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         int s = 0, ph = 0, it = 0, k = 0;
         bool waited = false, ok = true;
         for (;;) {
-            int rg = (int)blockIdx.x + k * (int)gridDim.x;
+            int u = (int)blockIdx.x + k * (int)gridDim.x;
             if (p.work) {
                 int r = 0;
                 if (lane == 0) r = atomicAdd(p.work, 1);
-                rg = __shfl_sync(0xffffffffu, r, 0);
+                u = __shfl_sync(0xffffffffu, r, 0);
             }
             ++k;
-            if (rg >= n_rg) break;
+            if (u >= n_units) break;
+            const int rg = ks ? u >> 1 : u;
+            const int st0 = ks && (u & 1) ? mid : 0, st1 = ks && !(u & 1) ? mid : spg;
             const bool isb = group_is_b<TA, TB>(p, rg);
             const int bb = isb ? Fmt<TB>::BB : Fmt<TA>::BB;
             const int chunk = P::KB * bb;
@@ -230,7 +235,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                     src -= off;
                 }
             }
-            for (int st = 0; st < spg; ++st, ++it) {
+            for (int st = st0; st < st1; ++st, ++it) {
                 if (it >= S && !mbar_wait(&empty[s], ph ^ 1, &g_decode_fault, 11)) {
                     ok = false;
                     break;
@@ -244,7 +249,8 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                     for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
                 }
                 if (lane == 0) {
-                    stage_rg[s] = rg;
+                    stage_rg[s] = u;
+                    stage_st[s] = st;
                     mbar_arrive_expect_tx(&full[s], tot + (uint32_t)P::SLICE);
                 }
                 __syncwarp();
@@ -258,7 +264,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
                     // the previous kernel before reading its limb slab
                     pdl_wait();
                     waited = true;
-                    for (int j = 0; j < S; ++j) limbs(j, j % spg);
+                    for (int j = 0; j < S; ++j) limbs(j, stage_st[j]);
                 }
                 if (++s == S) {
                     s = 0;
@@ -269,7 +275,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         }
         if (!waited) {
             pdl_wait();
-            for (int j = 0; j < it; ++j) limbs(j, j % spg);
+            for (int j = 0; j < it; ++j) limbs(j, stage_st[j]);
         }
         // every issued copy lands before the CTA can exit
         for (int j = it > S ? it - S : 0; j < it; ++j)
@@ -290,8 +296,10 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     bool ok = true;
     while (ok) {
         if (!mbar_wait(&full[s], ph, &g_decode_fault, 13)) break;
-        const int rg = stage_rg[s];
-        if (rg < 0) break;
+        const int u = stage_rg[s];
+        if (u < 0) break;
+        const int rg = ks ? u >> 1 : u;
+        const int st0 = ks && (u & 1) ? mid : 0, st1 = ks && !(u & 1) ? mid : spg;
         const bool isb = group_is_b<TA, TB>(p, rg);
         const int n = group_rows(p, rg);
         const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
@@ -304,8 +312,8 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
             tile_row(p, rg, rb, seg, lr);
             ob = (int)((uintptr_t)(p.W[seg] + (size_t)lr * rbytes) & 15u);
         }
-        for (int st = 0; st < spg; ++st) {
-            if (st > 0 && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) {
+        for (int st = st0; st < st1; ++st) {
+            if (st > st0 && !mbar_wait(&full[s], ph, &g_decode_fault, 13)) {
                 ok = false;
                 break;
             }
@@ -336,7 +344,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         }
         if (!ok) break;
         if (!finish_group_mbar<EPI>(p, red, rfull, rfree, rgl, rg, warp, lane, c, rms, acc_a,
-                                    acc_b, &g_decode_fault))
+                                    acc_b, &g_decode_fault, ks ? (u & 1) : -1))
             break;
         ++rgl;
     }
@@ -492,8 +500,9 @@ static int launch_inst(const FusedGemv& p, cudaStream_t st, bool pdl) {
         int cap = 0;
         if ((r = max_ctas((const void*)kern, (kNWC + 1) * 32, smem, &cap))) return r;
         // dynamic schedule: every resident slot claims row groups; static: an even split
-        const int per = (n_rg + cap - 1) / cap;
-        const int grid = p.work ? (n_rg < cap ? n_rg : cap) : (n_rg + per - 1) / per;
+        const int per = ((k_split<EPI>(p, spg) ? 2 * n_rg : n_rg) + cap - 1) / cap;
+        const int n_units = k_split<EPI>(p, spg) ? 2 * n_rg : n_rg;
+        const int grid = p.work ? (n_units < cap ? n_units : cap) : (n_units + per - 1) / per;
         IB_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3((kNWC + 1) * 32), smem, st, pdl, p, S,
                                  slot_a, slot_b, wbytes));
     }

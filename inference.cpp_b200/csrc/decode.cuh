@@ -107,6 +107,12 @@ struct FusedGemv {
     // optional work counters {next row group, CTAs done}, zero between launches: row
     // groups are then claimed dynamically (balanced over SMs); null = static schedule
     int* work;
+    // optional K split of long rows (EPI_RESID with more than 8 stages per row): every
+    // row group is two work units, its first and second half of stages.  A unit's rows go
+    // to kpart[rg][half][16]; the unit that finishes second (kcnt[rg], zero between
+    // launches) adds the two halves and runs the epilogue.  Null: one unit per row group.
+    float* kpart;
+    int* kcnt;
 };
 
 // Launches the fused GEMV; IB_ERR_UNSUPPORTED when the type mix or shapes have no

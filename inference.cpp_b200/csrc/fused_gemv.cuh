@@ -94,6 +94,16 @@ __device__ __forceinline__ bool tp_exchanges(const FusedGemv& p) {
     return EPI == EPI_ALLRED || (EPI == EPI_ARGMAX && p.tp.world > 1);
 }
 
+// True when a launch splits its row groups over K (FusedGemv::kpart): residual-add
+// GEMVs whose rows span more than 8 stages (K > 16384).  Measured on the decode step:
+// the Llama-3-70B down projection (14 stages) 11.04 against 11.17 ms per step; the
+// Llama-3-8B one (7 stages) 2.34 against 2.19 ms, where the per-unit fence and counter
+// on warp 0 cost more than the shorter chains gain.
+template <int EPI>
+__host__ __device__ __forceinline__ bool k_split(const FusedGemv& p, int spg) {
+    return EPI == EPI_RESID && p.kpart && p.kcnt && !p.paired && spg > 8;
+}
+
 // Run once by the last CTA out, after every CTA's rows are pushed: sends this rank's
 // key (ARGMAX; the CTAs' atomicMax are fenced before their arrival) and advances the
 // exchange counter the pushes and the receivers derive their tag from.
@@ -245,12 +255,13 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
 // every warp posts its partials to red[b] and arrives on rfull[b]; warp 0 waits, reduces,
 // runs the epilogue and frees the buffer on rfree[b]; a warp reusing red[b] (two row
 // groups later) first waits for that free.  Use u = rgl >> 1 of buffer b = rgl & 1.
+// half >= 0: the unit is that half of a K-split row group (FusedGemv::kpart).
 template <int EPI>
 __device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*red)[kNWC][16],
                                                   uint64_t* rfull, uint64_t* rfree, int rgl,
                                                   int rg, int warp, int lane, const LaneCtx& c,
                                                   float rms, float& acc_a, float& acc_b,
-                                                  int* fault) {
+                                                  int* fault, int half = -1) {
     const int b = rgl & 1, u = rgl >> 1;
     acc_a = quad_sum(acc_a);
     acc_b = quad_sum(acc_b);
@@ -273,6 +284,18 @@ __device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*re
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&rfree[b]);
+    if (half >= 0) {  // K split: the second half of the row group to finish adds both
+        if (lane < 16) p.kpart[((size_t)rg * 2 + half) * 16 + lane] = v;
+        __threadfence();
+        __syncwarp();
+        int second = 0;
+        if (lane == 0) second = atomicAdd(p.kcnt + rg, 1);
+        if (!__shfl_sync(0xffffffffu, second, 0)) return true;
+        __threadfence();
+        const float o = lane < 16 ? __ldcg(p.kpart + ((size_t)rg * 2 + (half ^ 1)) * 16 + lane) : 0.f;
+        v = half == 0 ? v + o : o + v;
+        if (lane == 0) p.kcnt[rg] = 0;
+    }
     epilogue<EPI>(p, rg, lane, v / rms);
     return true;
 }

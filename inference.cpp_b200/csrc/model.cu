@@ -458,6 +458,13 @@ static int finalize_buffers(Model* m) {
             m->allocations.push_back(*slabs[i]);
         }
         if ((st = alloc_f(m, &m->ssq, (size_t)D / 32 + 1))) return st;
+        if (m->tp_size == 1) {  // the down projection's K split (row groups of 16 rows)
+            const size_t n_rg = ((size_t)D + 15) / 16;
+            if ((st = alloc_f(m, &m->kpart, n_rg * 32))) return st;
+            IB_CUDA_CHECK(cudaMalloc(&m->kcnt, n_rg * 4));
+            m->allocations.push_back(m->kcnt);
+            IB_CUDA_CHECK(cudaMemsetAsync(m->kcnt, 0, n_rg * 4, m->stream));
+        }
         const size_t nwork = (size_t)(4 * c.n_layers + 1) * 2;
         IB_CUDA_CHECK(cudaMalloc(&m->gemv_work, nwork * 4));
         m->allocations.push_back(m->gemv_work);
@@ -606,6 +613,8 @@ static FusedGemv fg_ffn_out(const Model* m, const Layer& L) {
     p.slab = m->slab_h;
     p.y = m->x;
     p.tp = m->tpx;
+    p.kpart = m->kpart;  // long rows split over K (null under TP)
+    p.kcnt = m->kcnt;
     return p;
 }
 

@@ -60,6 +60,9 @@ struct Model {
     bool use_fused = true;  // fused decode kernels when every weight supports them
     bool kv_f16 = false;    // the KV cache in FP16 (ib_model_set_kv_type)
     bool fused_ok = false;
+    // K split of the down projection (one GPU): partial rows and arrival counters
+    float* kpart = nullptr;
+    int* kcnt = nullptr;
     // persistent decode step (step.cu): one kernel per token, single GPU
     bool use_persistent = false;
     bool persistent_ok = false;
