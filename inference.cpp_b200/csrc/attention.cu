@@ -350,6 +350,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
     constexpr int PW = ATT_TILE / ATT_WARPS;  // positions per warp per tile
     constexpr int PASSES = PW / PPP;
     constexpr int NVL = 2;                    // float4 per lane (head_dim <= 128)
+    static_assert(GMAX * 32 <= ATT_WARPS * 32, "one query float4 per thread");
     __shared__ float4 qs[GMAX][32];
     __shared__ float sc[GMAX][ATT_TILE];
     __shared__ float alpha[GMAX], mrun[GMAX], lrun[GMAX];
@@ -430,6 +431,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         if (sp < live) load_tile(p0, min(ATT_TILE, p1 - p0), 0, pos_pre);
     }
     pdl_wait();
+    // the query (G * nv <= 256 float4, one per thread) and the position word in one
+    // round trip: neither depends on the other
+    const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
+    const float4 qv = tid < G * nv ? q4[tid] : z4;
     const int pos = ld_relaxed_gpu(pos_dev);
     if (pos < 0 || pos >= max_seq) return;
     span(pos);
@@ -438,8 +443,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) attn_fused_kernel(
         load_tile(p0, min(ATT_TILE, p1 - p0), pos, pos + 1);
     else if (kPrefetch)
         load_full(p0, min(ATT_TILE, p1 - p0));
-    const float4* q4 = reinterpret_cast<const float4*>(q) + (size_t)(hk * G) * nv;
-    for (int i = tid; i < G * nv; i += ATT_WARPS * 32) qs[i / nv][i % nv] = q4[i];
+    if (tid < G * nv) qs[tid / nv][tid % nv] = qv;
     if (tid < G) {
         mrun[tid] = -INFINITY;
         lrun[tid] = 0.f;
