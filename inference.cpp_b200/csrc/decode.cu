@@ -288,6 +288,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         return;
     }
     pdl_wait();
+    const int ps = (EPI == EPI_QKV && warp == 0) ? *p.pos : 0;  // fixed during a step
     const float rms = PRO == PRO_NORM ? rms_of<P::GS>(p, lane) : 1.0f;
     const LaneCtx c = lane_ctx();
     const LeanLane ll = lean_lane(c);
@@ -303,6 +304,8 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         const bool isb = group_is_b<TA, TB>(p, rg);
         const int n = group_rows(p, rg);
         const int ra = c.g < n ? c.g : n - 1, rb = c.g + 8 < n ? c.g + 8 : n - 1;
+        EpiPre pre{};
+        if (warp == 0) pre = epi_fetch<EPI>(p, rg, lane, ps);
         const size_t rbytes = (size_t)nb * (isb ? Fmt<TB>::BB : Fmt<TA>::BB);
         int oa = 0, ob = 0;
         if (GEN) {
@@ -344,7 +347,7 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
         }
         if (!ok) break;
         if (!finish_group_mbar<EPI>(p, red, rfull, rfree, rgl, rg, warp, lane, c, rms, acc_a,
-                                    acc_b, &g_decode_fault, ks ? (u & 1) : -1))
+                                    acc_b, &g_decode_fault, pre, ks ? (u & 1) : -1))
             break;
         ++rgl;
     }

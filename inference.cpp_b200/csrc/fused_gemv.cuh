@@ -180,9 +180,38 @@ __device__ __forceinline__ float rms_of(const FusedGemv& p, int lane) {
 }
 
 // ---- epilogue ------------------------------------------------------------------------
-// Row-group epilogue on warp 0: lanes 0..15 hold the finished rows (v).
+// What a row group's epilogue reads from global memory, loaded by warp 0 when the row
+// group's first stage arrives so that the loads overlap the group's math: the residual
+// rows (RESID) and the RoPE factors of the position (QKV).  Nothing in the launch writes
+// them before the epilogue: the row group's own rows are written only there, and the
+// rotary table and the position are fixed during a step.
+struct EpiPre {
+    float y, c, s;
+    int ps;
+};
+
 template <int EPI>
-__device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, float v) {
+__device__ __forceinline__ EpiPre epi_fetch(const FusedGemv& p, int rg, int lane, int ps) {
+    EpiPre e{0.f, 1.f, 0.f, ps};
+    if (EPI == EPI_RESID) {
+        if (lane < group_rows(p, rg)) e.y = p.y[rg * 16 + lane];
+    } else if (EPI == EPI_QKV) {
+        int seg = 0, lr = 0;
+        tile_row(p, rg, lane & 15, seg, lr);
+        if (seg < 2) {
+            const int HD = p.head_dim, j = (lr % HD) >> 1;
+            e.c = p.rope[((size_t)ps * (HD / 2) + j) * 2];
+            e.s = p.rope[((size_t)ps * (HD / 2) + j) * 2 + 1];
+        }
+    }
+    return e;
+}
+
+// Row-group epilogue on warp 0: lanes 0..15 hold the finished rows (v); e holds what
+// epi_fetch loaded for them.
+template <int EPI>
+__device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, float v,
+                                         const EpiPre& e) {
     const unsigned FULL = 0xffffffffu;
     int seg = 0, lr = 0;
     tile_row(p, rg, lane & 15, seg, lr);
@@ -191,18 +220,16 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
         const int R = rg * 16 + lane;
         if (live) {
             if (EPI == EPI_STORE) p.y[R] = v;
-            else p.y[R] += v;
+            else p.y[R] = e.y + v;
         }
     } else if (EPI == EPI_QKV) {
         const int HD = p.head_dim;
         const int d = lr % HD;
-        const int ps = *p.pos;
+        const int ps = e.ps;
         const float other = __shfl_xor_sync(FULL, v, 1);
         float out = v;
         if (seg < 2) {  // RoPE, rope_kernel's formula on the pair (2j, 2j+1)
-            const int j = d >> 1;
-            const float c = p.rope[((size_t)ps * (HD / 2) + j) * 2];
-            const float s = p.rope[((size_t)ps * (HD / 2) + j) * 2 + 1];
+            const float c = e.c, s = e.s;
             out = (d & 1) == 0 ? v * c - other * s : other * s + v * c;
         }
         if (live) {
@@ -249,6 +276,12 @@ __device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, f
     }
 }
 
+// The epilogue with its reads made on the spot (the persistent step's epilogue warp).
+template <int EPI>
+__device__ __forceinline__ void epilogue(const FusedGemv& p, int rg, int lane, float v) {
+    epilogue<EPI>(p, rg, lane, v, epi_fetch<EPI>(p, rg, lane, EPI == EPI_QKV ? *p.pos : 0));
+}
+
 // Sums the consumer warps' partials of the row group, applies the RMSNorm divisor and
 // runs the epilogue, with bounded mbarrier handshakes (the TMA kernel's consumer warps
 // leave their loop independently after a failed wait):
@@ -261,7 +294,7 @@ __device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*re
                                                   uint64_t* rfull, uint64_t* rfree, int rgl,
                                                   int rg, int warp, int lane, const LaneCtx& c,
                                                   float rms, float& acc_a, float& acc_b,
-                                                  int* fault, int half = -1) {
+                                                  int* fault, const EpiPre& pre, int half = -1) {
     const int b = rgl & 1, u = rgl >> 1;
     acc_a = quad_sum(acc_a);
     acc_b = quad_sum(acc_b);
@@ -296,7 +329,7 @@ __device__ __forceinline__ bool finish_group_mbar(const FusedGemv& p, float (*re
         v = half == 0 ? v + o : o + v;
         if (lane == 0) p.kcnt[rg] = 0;
     }
-    epilogue<EPI>(p, rg, lane, v / rms);
+    epilogue<EPI>(p, rg, lane, v / rms, pre);
     return true;
 }
 
