@@ -289,7 +289,8 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     }
     pdl_wait();
     const int ps = (EPI == EPI_QKV && warp == 0) ? *p.pos : 0;  // fixed during a step
-    const float rms = PRO == PRO_NORM ? rms_of<P::GS>(p, lane) : 1.0f;
+    // the RMSNorm divisor is applied by warp 0's epilogue only
+    const float rms = (PRO == PRO_NORM && warp == 0) ? rms_of<P::GS>(p, lane) : 1.0f;
     const LaneCtx c = lane_ctx();
     const LeanLane ll = lean_lane(c);
     float acc_a = 0.f, acc_b = 0.f;
