@@ -355,8 +355,8 @@ __global__ void __launch_bounds__((kNWC + 1) * 32)
     // the last consumer warp of the last CTA out resets the work counters (and ends the
     // exchange: its key and the exchange counter)
     if (EPI == EPI_ARGMAX && tp_exchanges<EPI>(p) && warp == 0) __threadfence();
-    if (p.work && lane == 0 && atomicAdd(&warps_done, 1) == kNWC - 1 &&
-        atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+    if (p.work && (!p.work_ext || tp_exchanges<EPI>(p)) && lane == 0 &&
+        atomicAdd(&warps_done, 1) == kNWC - 1 && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
         if (tp_exchanges<EPI>(p)) tp_finish<EPI>(p);
         p.work[0] = 0;
         p.work[1] = 0;

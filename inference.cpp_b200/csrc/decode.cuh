@@ -105,8 +105,11 @@ struct FusedGemv {
     // both need `work` (its second counter finds the last CTA, which exchanges)
     TpExchange tp;
     // optional work counters {next row group, CTAs done}, zero between launches: row
-    // groups are then claimed dynamically (balanced over SMs); null = static schedule
+    // groups are then claimed dynamically (balanced over SMs); null = static schedule.
+    // work_ext = 1: the caller zeroes them between launches, so the CTAs skip counting
+    // themselves out on exit (an exchange's last CTA still does)
     int* work;
+    int work_ext;
     // optional K split of long rows (EPI_RESID with more than 8 stages per row): every
     // row group is two work units, its first and second half of stages.  A unit's rows go
     // to kpart[rg][half][16]; the unit that finishes second (kcnt[rg], zero between

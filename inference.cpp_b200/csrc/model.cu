@@ -51,7 +51,10 @@ __global__ void feedback_kernel(int32_t* dev_i32, int32_t* out_tokens, int max_s
 // Fused-path feedback: the head's argmax key gives the next token; the key is reset
 // for the next step.
 __global__ void feedback_best_kernel(unsigned long long* best, int32_t* dev_i32,
-                                     int32_t* out_tokens, int max_seq) {
+                                     int32_t* out_tokens, int max_seq, int* work, int n_work) {
+    // the step's GEMV work counters for the next step (the GEMVs do not count out)
+    for (int i = threadIdx.x; i < n_work; i += blockDim.x) work[i] = 0;
+    if (threadIdx.x) return;
     const int next = argmax_key_row(*best);
     *best = 0ull;
     const int pos = dev_i32[1];
@@ -555,6 +558,7 @@ namespace ib {
 static FusedGemv fg_common(const Model* m) {
     FusedGemv p = {};
     p.eps = m->cfg.rms_eps;
+    p.work_ext = 1;  // the step's feedback kernel zeroes the work counters
     return p;
 }
 
@@ -890,7 +894,8 @@ static int decode_launches_fused(Model* m) {
     head.work = work;
     if ((r = fused_gemv_launch(head, PRO_NORM, EPI_ARGMAX, st, true))) return r;
     if (tx && (r = tp_key_max_launch(*tx, m->best, st))) return r;
-    feedback_best_kernel<<<1, 1, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq);
+    feedback_best_kernel<<<1, 256, 0, st>>>(m->best, m->dev_i32, m->dev_tokens, c.max_seq,
+                                            m->gemv_work, (int)(work + 2 - m->gemv_work));
     IB_LAUNCH_CHECK("decode step");
     return IB_OK;
 }
