@@ -71,8 +71,14 @@ __global__ void __launch_bounds__(256) xq_slab_kernel(float* __restrict__ x,
                                                       float* __restrict__ ssq,
                                                       const TpExchange tp) {
     pdl_launch_dependents();
-    pdl_wait();
     constexpr int GS = SlabG<KQ>::GS, PER = GS / 32;
+    // the norm weights are constant: loaded while the previous kernel finishes
+    float w[PER];
+    {
+        const int g0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (norm && g0 * GS < K) slab_load<KQ>(norm, g0, threadIdx.x & 31, w);
+    }
+    pdl_wait();
     const uint64_t* parts = nullptr;
     uint32_t tag = 0;
     if constexpr (TP) {
@@ -108,10 +114,9 @@ __global__ void __launch_bounds__(256) xq_slab_kernel(float* __restrict__ x,
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-        const int i = slab_elem<KQ>(gi, j, lane);
         float t = v[j];
         ss = fmaf(t, t, ss);
-        if (norm) t *= norm[i];
+        if (norm) t *= w[j];
         v[j] = t;
     }
     if (ssq) {
